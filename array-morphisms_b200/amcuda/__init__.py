@@ -1,0 +1,26 @@
+"""amcuda — B200 (sm_100a) realization backend for array-morphisms.
+
+The lazy-morphism API of the reference (constructors in amcuda.morph,
+realize / realize_ctx) over libamcuda.so, the C-ABI library of hand-written
+sm_100a kernels.  Importing this package loads the library and fails loudly
+when it is missing; there is no CPU fallback.
+"""
+from . import _abi
+from ._abi import AmcError
+
+_abi.load()
+
+from .morph import (Concrete, Expr, Morphism, attention_morphism, broadcast_shapes, col2im_morph,  # noqa: E402
+                    compute_strides, im2col_morph, infer_reduction_dtype, morph_abs, morph_add, morph_ceiling,
+                    morph_concat, morph_cos, morph_div, morph_dot, morph_eq, morph_exp, morph_floor, morph_from_list,
+                    morph_from_numpy, morph_ge, morph_gt, morph_le, morph_log, morph_lt, morph_map, morph_matmul,
+                    morph_matvec, morph_mul, morph_negate, morph_pad, morph_pow, morph_reduce, morph_relu,
+                    morph_reshape, morph_sigmoid, morph_sin, morph_slice, morph_split, morph_sqrt, morph_squeeze,
+                    morph_stack, morph_sub, morph_tan, morph_tanh, morph_transpose, morph_unsqueeze, morph_unstack,
+                    promote_types)
+from .realize import DeviceBuffer, Plan, force_morphism, init, morph_to_list, realize, to_numpy  # noqa: E402
+from .context import (MorphismContext, context_stats, finalize_context, make_morphism_context, plan_ctx,  # noqa: E402
+                      realize_ctx, reset_context)
+from . import fn  # noqa: E402
+
+__all__ = [n for n in dir() if not n.startswith("_")]

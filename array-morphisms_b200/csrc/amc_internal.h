@@ -1,0 +1,179 @@
+// Internal declarations shared by the libamcuda translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <atomic>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/amc.h"
+
+namespace amc {
+
+// ------------------------------------------------------------------ errors
+void set_error(const std::string& msg);
+int fail(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+#define AMC_CUDA(call)                                         \
+  do {                                                         \
+    cudaError_t _e = (call);                                   \
+    if (_e != cudaSuccess) return ::amc::cuda_fail(_e, #call); \
+  } while (0)
+
+// Host-side fault injection: AMC_FAULT=alloc|launch|timeout makes the named
+// class of operation fail with AMC_ERR_INJECTED before touching the device.
+bool fault_injected(const char* what);
+
+size_t dtype_size(int32_t dtype);
+bool dtype_valid(int32_t dtype);
+bool dtype_float(int32_t dtype);
+
+// ------------------------------------------------------------------ buffers
+struct Buffer {
+  void* ptr = nullptr;
+  int32_t dtype = AMC_F64;
+  int64_t nelem = 0;
+  bool owned = true;
+  int device = 0;
+  std::atomic<int> refs{1};
+  std::shared_ptr<void> keepalive;  // arena backing for context sub-buffers
+};
+
+uint64_t buf_register(Buffer* b);
+Buffer* buf_get(uint64_t h);
+void buf_retain(uint64_t h);
+void buf_release(uint64_t h);
+int buf_alloc(int32_t dtype, int64_t nelem, uint64_t* out);
+
+cudaStream_t default_stream();
+inline cudaStream_t pick_stream(void* s) { return s ? (cudaStream_t)s : default_stream(); }
+int num_sms();
+
+// ------------------------------------------------------------------ device descriptors
+struct DLeaf {
+  const void* ptr;       // base pointer with the view offset folded in
+  int32_t dtype;
+  int32_t _pad;
+  int64_t strides[AMC_MAX_RANK];  // over the kernel's index space (0 = broadcast)
+};
+
+constexpr int kMaxLeaves = 8;
+
+struct DProg {
+  int32_t n;
+  int32_t all_float;     // every load is f32/f64 and no ICONST: inexact-only evaluation
+  amc_insn code[AMC_PROG_MAX];
+};
+
+// Element-wise launch: out[i] = store(out_dtype, prog(leaves at i)), i over shape.
+struct MapArgs {
+  int32_t rank;
+  int32_t nleaf;
+  int64_t shape[AMC_MAX_RANK];
+  int64_t total;
+  DLeaf leaf[kMaxLeaves];
+  DProg prog;
+  void* out;
+  int32_t out_dtype;
+  int32_t _pad;
+};
+
+// Reduction launch: source index space = (kept dims..., reduced dims...) after
+// the planner has permuted the reduced axes last and collapsed dims.
+struct ReduceArgs {
+  int32_t orank, rrank;
+  int64_t oshape[AMC_MAX_RANK];   // kept dims (row-major output order)
+  int64_t rshape[AMC_MAX_RANK];   // reduced dims (row-major source order)
+  int64_t O, R;
+  int32_t nleaf;
+  int32_t src_dtype;              // dtype of the reduced values (source node)
+  DLeaf leaf_o[kMaxLeaves];       // leaf strides over kept dims
+  int64_t leaf_r[kMaxLeaves][AMC_MAX_RANK];  // leaf strides over reduced dims
+  DProg prog;
+  void* out;
+  int32_t out_dtype;
+  int32_t op;                     // AMC_RED_*
+};
+
+int launch_map(const MapArgs& a, cudaStream_t s);
+int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scratch_bytes, size_t* scratch_need);
+
+struct PadArgs {
+  int32_t rank, mode;
+  int64_t oshape[AMC_MAX_RANK];
+  int64_t sshape[AMC_MAX_RANK];
+  int64_t sstrides[AMC_MAX_RANK];
+  int64_t before[AMC_MAX_RANK];
+  const void* src; int32_t src_dtype;
+  void* out; int32_t out_dtype;
+  double value;
+  int64_t total;
+};
+int launch_pad(const PadArgs& a, cudaStream_t s);
+
+struct Im2colArgs {
+  int64_t N, C, H, W, OH, OW;
+  int32_t KH, KW, SH, SW, PH, PW;
+  int64_t sN, sC, sH, sW;
+  const void* src; int32_t src_dtype;
+  void* out; int32_t out_dtype;
+};
+int launch_im2col(const Im2colArgs& a, cudaStream_t s);
+
+struct Col2imArgs {
+  int64_t N, C, H, W, OH, OW;
+  int32_t KH, KW, SH, SW, PH, PW;
+  const void* col; int32_t col_dtype;   // contiguous (N, C*KH*KW, OH*OW)
+  void* out; int32_t out_dtype;
+};
+int launch_col2im(const Col2imArgs& a, cudaStream_t s);
+
+struct RouteArgs {
+  int32_t rank, axis, is_stack, nsrc;
+  int64_t oshape[AMC_MAX_RANK];
+  const DLeaf* srcs;         // device array of nsrc source views (strides in source dims)
+  const int64_t* extents;    // device array: each source's size along axis (concat)
+  void* out; int32_t out_dtype;
+  int64_t total;
+};
+int launch_route(const RouteArgs& a, cudaStream_t s);
+
+// C[M,N] = A[M,K] B[K,N] with arbitrary element strides, double accumulation,
+// stored as out_dtype (row-major contiguous output with leading dim N).
+struct GemmArgs {
+  int64_t M, N, K;
+  const void* A; int32_t a_dtype; int64_t sa0, sa1;
+  const void* B; int32_t b_dtype; int64_t sb0, sb1;
+  void* C; int32_t c_dtype;
+  double alpha, beta;            // C = alpha*AB + beta*C (beta=0 ignores C)
+};
+int launch_gemm(const GemmArgs& a, cudaStream_t s);
+
+struct AttnArgs {
+  int64_t blocks;
+  int32_t n, dk, dv, dtype;
+  const void* Q; int64_t qb, q0, q1;
+  const void* K; int64_t kb, k0, k1;
+  const void* V; int64_t vb, v0, v1;
+  void* O;                        // contiguous (blocks, n, dv)
+  double scale;
+};
+int launch_attention_generic(const AttnArgs& a, cudaStream_t s);
+
+// Windowed FIR (the polyphase filter-bank reduction).
+struct FirArgs {
+  const float* x; int64_t batch, x_bstride, frames, hop;
+  int32_t taps, branches;
+  int64_t x_tstride;              // stride between taps (== branches for the filter bank)
+  const float* h; int64_t h_tstride;   // h[t*h_tstride + m]
+  float* out; int64_t o_bstride, o_fstride;  // out[b*o_bstride + f*o_fstride + m]
+};
+bool fir_supported(const FirArgs& a);
+int launch_fir(const FirArgs& a, cudaStream_t s);
+
+}  // namespace amc

@@ -1,0 +1,741 @@
+// Generic device kernels of the realization engine:
+//   - fused element-wise programs over strided views   (realization.scm:876-997)
+//   - ordered reductions                                (realization.scm:1309-1388)
+//   - pad / im2col / col2im / stack-concat gathers      (realization.scm:1003-1268, 1425-1459)
+//   - double-accumulating GEMM                          (blas-exec.scm:405-458)
+//   - reference-order streaming attention               (realization.scm:279-396)
+// Numeric semantics follow the reference's Scheme numbers: inexact values are
+// IEEE doubles, exact values are 64-bit integers, and a node's result is
+// converted only when stored (typed-vector-set!, core.scm:649-658).
+#include <cfloat>
+#include <cmath>
+
+#include "amc_internal.h"
+
+namespace amc {
+
+// ------------------------------------------------------------------ numbers
+struct Num {
+  double f;
+  long long i;
+  int exact;
+};
+
+__device__ __forceinline__ Num nfl(double f) { Num r; r.f = f; r.i = 0; r.exact = 0; return r; }
+__device__ __forceinline__ Num nex(long long i) { Num r; r.f = (double)i; r.i = i; r.exact = 1; return r; }
+__device__ __forceinline__ double as_f(const Num& a) { return a.exact ? (double)a.i : a.f; }
+__device__ __forceinline__ bool dtype_is_float_d(int d) { return d == AMC_F32 || d == AMC_F64; }
+
+__device__ __forceinline__ Num load_num(const void* p, int dtype, long long k) {
+  switch (dtype) {
+    case AMC_F32: return nfl((double)__ldg((const float*)p + k));
+    case AMC_F64: return nfl(__ldg((const double*)p + k));
+    case AMC_S32: return nex(__ldg((const int*)p + k));
+    case AMC_S64: return nex(__ldg((const long long*)p + k));
+    case AMC_U32: return nex((long long)__ldg((const unsigned*)p + k));
+    default: return nex((long long)__ldg((const unsigned long long*)p + k));
+  }
+}
+
+__device__ __forceinline__ double load_f(const void* p, int dtype, long long k) {
+  return dtype == AMC_F32 ? (double)__ldg((const float*)p + k) : __ldg((const double*)p + k);
+}
+
+__device__ __forceinline__ long long trunc_i(const Num& x) { return x.exact ? x.i : (long long)trunc(x.f); }
+
+__device__ __forceinline__ Num round_store(int dtype, const Num& x) {
+  switch (dtype) {
+    case AMC_F32: return nfl((double)__double2float_rn(as_f(x)));
+    case AMC_F64: return nfl(as_f(x));
+    case AMC_S32: return nex((int)trunc_i(x));
+    case AMC_S64: return nex(trunc_i(x));
+    case AMC_U32: { long long t = trunc_i(x); return nex((unsigned)(t < 0 ? -t : t)); }
+    default: { long long t = trunc_i(x); return nex(t < 0 ? -t : t); }
+  }
+}
+
+__device__ __forceinline__ void store_num(void* p, int dtype, long long k, const Num& x) {
+  switch (dtype) {
+    case AMC_F32: ((float*)p)[k] = __double2float_rn(as_f(x)); break;
+    case AMC_F64: ((double*)p)[k] = as_f(x); break;
+    case AMC_S32: ((int*)p)[k] = (int)trunc_i(x); break;
+    case AMC_S64: ((long long*)p)[k] = trunc_i(x); break;
+    case AMC_U32: { long long t = trunc_i(x); ((unsigned*)p)[k] = (unsigned)(t < 0 ? -t : t); } break;
+    default: { long long t = trunc_i(x); ((unsigned long long*)p)[k] = (unsigned long long)(t < 0 ? -t : t); } break;
+  }
+}
+
+__device__ __forceinline__ long long ipow_d(long long a, long long b) {
+  long long r = 1;
+  while (b > 0) { if (b & 1) r *= a; a *= a; b >>= 1; }
+  return r;
+}
+
+__device__ __forceinline__ Num un_op(int op, const Num& a) {
+  double x = as_f(a);
+  switch (op) {
+    case AMC_OP_NEG: return a.exact ? nex(-a.i) : nfl(-a.f);
+    case AMC_OP_ABS: return a.exact ? nex(a.i < 0 ? -a.i : a.i) : nfl(fabs(a.f));
+    case AMC_OP_FLOOR: return a.exact ? a : nfl(floor(a.f));
+    case AMC_OP_CEIL: return a.exact ? a : nfl(ceil(a.f));
+    case AMC_OP_SQRT:
+      if (a.exact && a.i >= 0) {
+        long long r = llround(sqrt((double)a.i));
+        if (r * r == a.i) return nex(r);
+      }
+      return nfl(sqrt(x));
+    case AMC_OP_EXP: return nfl(exp(x));
+    case AMC_OP_LOG: return nfl(log(x));
+    case AMC_OP_SIN: return nfl(sin(x));
+    case AMC_OP_COS: return nfl(cos(x));
+    case AMC_OP_TAN: return nfl(tan(x));
+    case AMC_OP_RELU: return nfl(x > 0.0 ? x : 0.0);
+    case AMC_OP_SIGMOID: return nfl(__ddiv_rn(1.0, __dadd_rn(1.0, exp(-x))));
+    case AMC_OP_TANH: { double e2 = exp(__dmul_rn(2.0, x)); return nfl(__ddiv_rn(__dsub_rn(e2, 1.0), __dadd_rn(e2, 1.0))); }
+  }
+  return nfl(NAN);
+}
+
+__device__ __forceinline__ Num bin_op(int op, const Num& a, const Num& b) {
+  bool ex = a.exact && b.exact;
+  double x = as_f(a), y = as_f(b);
+  switch (op) {
+    case AMC_OP_ADD: return ex ? nex(a.i + b.i) : nfl(__dadd_rn(x, y));
+    case AMC_OP_SUB: return ex ? nex(a.i - b.i) : nfl(__dsub_rn(x, y));
+    case AMC_OP_MUL: return ex ? nex(a.i * b.i) : nfl(__dmul_rn(x, y));
+    case AMC_OP_DIV:
+      if (ex) {
+        if (b.i != 0 && a.i % b.i == 0) return nex(a.i / b.i);
+        return nfl(__ddiv_rn((double)a.i, (double)b.i));
+      }
+      return nfl(__ddiv_rn(x, y));
+    case AMC_OP_POW: return (ex && b.i >= 0) ? nex(ipow_d(a.i, b.i)) : nfl(pow(x, y));
+    case AMC_OP_MAX: return ex ? nex(a.i > b.i ? a.i : b.i) : nfl(x > y ? x : y);
+    case AMC_OP_MIN: return ex ? nex(a.i < b.i ? a.i : b.i) : nfl(x < y ? x : y);
+    case AMC_OP_GT: return nfl(ex ? (double)(a.i > b.i) : (double)(x > y));
+    case AMC_OP_LT: return nfl(ex ? (double)(a.i < b.i) : (double)(x < y));
+    case AMC_OP_EQ: return nfl(ex ? (double)(a.i == b.i) : (double)(x == y));
+    case AMC_OP_GE: return nfl(ex ? (double)(a.i >= b.i) : (double)(x >= y));
+    case AMC_OP_LE: return nfl(ex ? (double)(a.i <= b.i) : (double)(x <= y));
+  }
+  return nfl(NAN);
+}
+
+// Tagged evaluation (exact integers and doubles).
+__device__ Num eval_prog(const DProg& P, const DLeaf* L, const long long* off) {
+  Num st[AMC_STACK_MAX];
+  int sp = 0;
+  for (int pc = 0; pc < P.n; ++pc) {
+    const amc_insn I = P.code[pc];
+    switch (I.op) {
+      case AMC_OP_LOAD: st[sp++] = load_num(L[I.a].ptr, L[I.a].dtype, off[I.a]); break;
+      case AMC_OP_CONST: st[sp++] = nfl(I.imm); break;
+      case AMC_OP_ICONST: st[sp++] = nex((long long)I.imm); break;
+      case AMC_OP_CVT: st[sp - 1] = round_store(I.a, st[sp - 1]); break;
+      default:
+        if (I.op < AMC_OP_ADD) st[sp - 1] = un_op(I.op, st[sp - 1]);
+        else { st[sp - 2] = bin_op(I.op, st[sp - 2], st[sp - 1]); --sp; }
+    }
+  }
+  return st[0];
+}
+
+// Inexact-only evaluation: every value is a double.
+__device__ __forceinline__ double un_f(int op, double x) {
+  switch (op) {
+    case AMC_OP_NEG: return -x;
+    case AMC_OP_ABS: return fabs(x);
+    case AMC_OP_FLOOR: return floor(x);
+    case AMC_OP_CEIL: return ceil(x);
+    case AMC_OP_SQRT: return sqrt(x);
+    case AMC_OP_EXP: return exp(x);
+    case AMC_OP_LOG: return log(x);
+    case AMC_OP_SIN: return sin(x);
+    case AMC_OP_COS: return cos(x);
+    case AMC_OP_TAN: return tan(x);
+    case AMC_OP_RELU: return x > 0.0 ? x : 0.0;
+    case AMC_OP_SIGMOID: return __ddiv_rn(1.0, __dadd_rn(1.0, exp(-x)));
+    case AMC_OP_TANH: { double e2 = exp(__dmul_rn(2.0, x)); return __ddiv_rn(__dsub_rn(e2, 1.0), __dadd_rn(e2, 1.0)); }
+  }
+  return NAN;
+}
+
+__device__ __forceinline__ double bin_f(int op, double x, double y) {
+  switch (op) {
+    case AMC_OP_ADD: return __dadd_rn(x, y);
+    case AMC_OP_SUB: return __dsub_rn(x, y);
+    case AMC_OP_MUL: return __dmul_rn(x, y);
+    case AMC_OP_DIV: return __ddiv_rn(x, y);
+    case AMC_OP_POW: return pow(x, y);
+    case AMC_OP_MAX: return x > y ? x : y;
+    case AMC_OP_MIN: return x < y ? x : y;
+    case AMC_OP_GT: return (double)(x > y);
+    case AMC_OP_LT: return (double)(x < y);
+    case AMC_OP_EQ: return (double)(x == y);
+    case AMC_OP_GE: return (double)(x >= y);
+    case AMC_OP_LE: return (double)(x <= y);
+  }
+  return NAN;
+}
+
+__device__ __forceinline__ double round_f(int dtype, double x) {
+  switch (dtype) {
+    case AMC_F32: return (double)__double2float_rn(x);
+    case AMC_F64: return x;
+    case AMC_S32: return (double)(int)(long long)trunc(x);
+    case AMC_S64: return (double)(long long)trunc(x);
+    case AMC_U32: { long long t = (long long)trunc(x); return (double)(unsigned)(t < 0 ? -t : t); }
+    default: { long long t = (long long)trunc(x); return (double)(t < 0 ? -t : t); }
+  }
+}
+
+__device__ double eval_prog_f(const DProg& P, const DLeaf* L, const long long* off) {
+  double st[AMC_STACK_MAX];
+  int sp = 0;
+  for (int pc = 0; pc < P.n; ++pc) {
+    const amc_insn I = P.code[pc];
+    switch (I.op) {
+      case AMC_OP_LOAD: st[sp++] = load_f(L[I.a].ptr, L[I.a].dtype, off[I.a]); break;
+      case AMC_OP_CONST: st[sp++] = I.imm; break;
+      case AMC_OP_CVT: st[sp - 1] = round_f(I.a, st[sp - 1]); break;
+      default:
+        if (I.op < AMC_OP_ADD) st[sp - 1] = un_f(I.op, st[sp - 1]);
+        else { st[sp - 2] = bin_f(I.op, st[sp - 2], st[sp - 1]); --sp; }
+    }
+  }
+  return st[0];
+}
+
+// ------------------------------------------------------------------ map
+template <bool ALLF>
+__global__ void __launch_bounds__(256) k_map(const __grid_constant__ MapArgs a) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < a.total; i += stride) {
+    long long off[kMaxLeaves];
+    for (int l = 0; l < a.nleaf; ++l) off[l] = 0;
+    long long rem = i;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      long long s = a.shape[d];
+      long long c = rem % s;
+      rem /= s;
+      for (int l = 0; l < a.nleaf; ++l) off[l] += c * a.leaf[l].strides[d];
+    }
+    if (ALLF) {
+      double v = eval_prog_f(a.prog, a.leaf, off);
+      store_num(a.out, a.out_dtype, i, nfl(v));
+    } else {
+      Num v = eval_prog(a.prog, a.leaf, off);
+      store_num(a.out, a.out_dtype, i, v);
+    }
+  }
+}
+
+static unsigned grid_for(long long total, int block) {
+  long long g = (total + block - 1) / block;
+  long long cap = (long long)num_sms() * 16;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (unsigned)g;
+}
+
+int launch_map(const MapArgs& a, cudaStream_t s) {
+  if (a.total == 0) return AMC_OK;
+  if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "map: injected launch failure (AMC_FAULT=launch)");
+  unsigned g = grid_for(a.total, 256);
+  if (a.prog.all_float) k_map<true><<<g, 256, 0, s>>>(a);
+  else k_map<false><<<g, 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ reductions
+// Accumulator with the reference's reducer semantics: the running value is
+// re-read from the typed output vector at every step, so it is rounded to
+// the output dtype after each combination.
+struct Acc {
+  double f;
+  long long i;
+};
+
+__device__ __forceinline__ void acc_init(Acc& A, int op, int out_dtype) {
+  double v = op == AMC_RED_PROD ? 1.0 : op == AMC_RED_MAX ? -INFINITY : op == AMC_RED_MIN ? INFINITY : 0.0;
+  A.f = v;
+  A.i = op == AMC_RED_PROD ? 1 : 0;
+}
+
+// src values are either all exact (integer source dtype) or all inexact.
+__device__ __forceinline__ void acc_step(Acc& A, int op, int out_dtype, bool src_exact, double vf, long long vi) {
+  if (dtype_is_float_d(out_dtype)) {
+    double x = src_exact ? (double)vi : vf;
+    double r;
+    switch (op) {
+      case AMC_RED_PROD: r = __dmul_rn(A.f, x); break;
+      case AMC_RED_MAX: r = A.f > x ? A.f : x; break;  // (max acc x): acc kept only when strictly larger
+      case AMC_RED_MIN: r = A.f < x ? A.f : x; break;
+      default: r = __dadd_rn(A.f, x); break;
+    }
+    A.f = out_dtype == AMC_F32 ? (double)__double2float_rn(r) : r;
+  } else {
+    long long r = op == AMC_RED_PROD ? A.i * vi : A.i + vi;
+    switch (out_dtype) {
+      case AMC_S32: r = (int)r; break;
+      case AMC_U32: r = (unsigned)(r < 0 ? -r : r); break;
+      case AMC_U64: r = r < 0 ? -r : r; break;
+      default: break;
+    }
+    A.i = r;
+  }
+}
+
+__device__ __forceinline__ void acc_store(const Acc& A, void* out, int out_dtype, int op, long long R, long long o) {
+  if (dtype_is_float_d(out_dtype)) {
+    double v = A.f;
+    if (op == AMC_RED_MEAN) v = __ddiv_rn(v, (double)R);
+    store_num(out, out_dtype, o, nfl(v));
+  } else {
+    store_num(out, out_dtype, o, nex(A.i));
+  }
+}
+
+__device__ __forceinline__ void leaf_offsets(const ReduceArgs& a, long long o, long long r, long long* off) {
+  for (int l = 0; l < a.nleaf; ++l) off[l] = 0;
+  long long rem = o;
+  for (int d = a.orank - 1; d >= 0; --d) {
+    long long s = a.oshape[d], c = rem % s;
+    rem /= s;
+    for (int l = 0; l < a.nleaf; ++l) off[l] += c * a.leaf_o[l].strides[d];
+  }
+  rem = r;
+  for (int d = a.rrank - 1; d >= 0; --d) {
+    long long s = a.rshape[d], c = rem % s;
+    rem /= s;
+    for (int l = 0; l < a.nleaf; ++l) off[l] += c * a.leaf_r[l][d];
+  }
+}
+
+// Evaluate the source element (o, r): the value after the source node's store
+// conversion, returned as (double, int64) by the source dtype's exactness.
+__device__ __forceinline__ void eval_src(const ReduceArgs& a, long long o, long long r, double& vf, long long& vi) {
+  long long off[kMaxLeaves];
+  leaf_offsets(a, o, r, off);
+  if (a.prog.all_float) {
+    vf = eval_prog_f(a.prog, a.leaf_o, off);
+    vi = 0;
+  } else {
+    Num v = eval_prog(a.prog, a.leaf_o, off);
+    vf = as_f(v);
+    vi = trunc_i(v);
+  }
+}
+
+// Ordered ("sequential") reduction: CTA owns OT consecutive outputs.  All
+// threads evaluate a (OT x RC) tile of source values into shared memory in
+// parallel; then one thread per output folds its RC values in ascending r.
+// This reproduces the reference's accumulation order exactly.
+__global__ void __launch_bounds__(256) k_reduce_seq(const __grid_constant__ ReduceArgs a, int OT, int RC, int ofast) {
+  extern __shared__ unsigned long long smem_u64[];
+  const bool src_exact = !dtype_is_float_d(a.src_dtype);
+  const long long o0 = (long long)blockIdx.x * OT;
+  Acc A;
+  acc_init(A, a.op, a.out_dtype);
+  for (long long r0 = 0; r0 < a.R; r0 += RC) {
+    int rc = (int)((a.R - r0) < RC ? (a.R - r0) : RC);
+    int tile = OT * rc;
+    for (int e = threadIdx.x; e < tile; e += blockDim.x) {
+      int ol, rl;
+      if (ofast) { ol = e % OT; rl = e / OT; } else { ol = e / rc; rl = e % rc; }
+      long long o = o0 + ol;
+      if (o >= a.O) continue;
+      double vf; long long vi;
+      eval_src(a, o, r0 + rl, vf, vi);
+      smem_u64[ol * (RC + 1) + rl] = src_exact ? (unsigned long long)vi : __double_as_longlong(vf);
+    }
+    __syncthreads();
+    if (threadIdx.x < OT && o0 + threadIdx.x < a.O) {
+      const unsigned long long* row = smem_u64 + threadIdx.x * (RC + 1);
+      for (int rl = 0; rl < rc; ++rl) {
+        unsigned long long bits = row[rl];
+        acc_step(A, a.op, a.out_dtype, src_exact, __longlong_as_double(bits), (long long)bits);
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x < OT && o0 + threadIdx.x < a.O) acc_store(A, a.out, a.out_dtype, a.op, a.R, o0 + threadIdx.x);
+}
+
+// Tree reduction for few outputs over long axes: pass 1 gives each CTA of
+// grid (G, O) a contiguous r-range, folded per thread in ascending order and
+// combined across the block in a fixed tree; pass 2 folds the G partials of
+// each output in ascending order.  Deterministic; float sums accumulate in
+// double (tighter than the reference's running f32 sum).
+__device__ __forceinline__ void tree_combine(int op, bool exact, double& f, long long& i, double f2, long long i2) {
+  if (exact) {
+    i = op == AMC_RED_PROD ? i * i2 : i + i2;
+  } else {
+    switch (op) {
+      case AMC_RED_PROD: f = f * f2; break;
+      case AMC_RED_MAX: f = f2 > f ? f2 : f; break;
+      case AMC_RED_MIN: f = f2 < f ? f2 : f; break;
+      default: f = f + f2; break;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) k_reduce_tree1(const __grid_constant__ ReduceArgs a, double* pf, long long* pi, int G) {
+  const bool exact = !dtype_is_float_d(a.src_dtype);
+  const int g = blockIdx.x;
+  const long long o = blockIdx.y;
+  long long chunk = (a.R + G - 1) / G, r_begin = g * chunk, r_end = r_begin + chunk < a.R ? r_begin + chunk : a.R;
+  double f = a.op == AMC_RED_PROD ? 1.0 : a.op == AMC_RED_MAX ? -INFINITY : a.op == AMC_RED_MIN ? INFINITY : 0.0;
+  long long i = a.op == AMC_RED_PROD ? 1 : 0;
+  for (long long r = r_begin + threadIdx.x; r < r_end; r += blockDim.x) {
+    double vf; long long vi;
+    eval_src(a, o, r, vf, vi);
+    tree_combine(a.op, exact, f, i, vf, vi);
+  }
+  __shared__ double sf[256];
+  __shared__ long long si[256];
+  sf[threadIdx.x] = f;
+  si[threadIdx.x] = i;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      double f2 = sf[threadIdx.x + w]; long long i2 = si[threadIdx.x + w];
+      double f1 = sf[threadIdx.x]; long long i1 = si[threadIdx.x];
+      tree_combine(a.op, exact, f1, i1, f2, i2);
+      sf[threadIdx.x] = f1; si[threadIdx.x] = i1;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) { pf[o * G + g] = sf[0]; pi[o * G + g] = si[0]; }
+}
+
+__global__ void k_reduce_tree2(const __grid_constant__ ReduceArgs a, const double* pf, const long long* pi, int G) {
+  long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= a.O) return;
+  const bool exact = !dtype_is_float_d(a.src_dtype);
+  double f = a.op == AMC_RED_PROD ? 1.0 : a.op == AMC_RED_MAX ? -INFINITY : a.op == AMC_RED_MIN ? INFINITY : 0.0;
+  long long i = a.op == AMC_RED_PROD ? 1 : 0;
+  for (int g = 0; g < G; ++g) tree_combine(a.op, exact, f, i, pf[o * G + g], pi[o * G + g]);
+  if (dtype_is_float_d(a.out_dtype)) {
+    double v = exact ? (double)i : f;
+    if (a.op == AMC_RED_MEAN) v = v / (double)a.R;
+    store_num(a.out, a.out_dtype, o, nfl(v));
+  } else {
+    store_num(a.out, a.out_dtype, o, nex(i));
+  }
+}
+
+int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scratch_bytes, size_t* scratch_need) {
+  const int sms = num_sms();
+  // decide: ordered (bit-exact) unless few outputs over a long axis
+  bool tree = (a.R > 16384) && (a.O < (long long)sms * 64);
+  int G = 0;
+  if (tree) {
+    long long want = ((long long)sms * 8 + a.O - 1) / (a.O > 0 ? a.O : 1);
+    G = (int)(want < 1 ? 1 : want > 1024 ? 1024 : want);
+    long long per = (a.R + G - 1) / G;
+    if (per < 1024) G = (int)((a.R + 1023) / 1024);
+    if (G < 1) G = 1;
+  }
+  size_t need = tree ? (size_t)a.O * G * (sizeof(double) + sizeof(long long)) : 0;
+  if (scratch_need) *scratch_need = need;
+  if (!s && !scratch) return AMC_OK;  // sizing query only
+  if (a.O == 0) return AMC_OK;
+  if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "reduce: injected launch failure (AMC_FAULT=launch)");
+  if (tree) {
+    if (scratch_bytes < need || !scratch) return fail(AMC_ERR_INVALID, "reduce: scratch too small");
+    double* pf = (double*)scratch;
+    long long* pi = (long long*)((char*)scratch + (size_t)a.O * G * sizeof(double));
+    dim3 g1((unsigned)G, (unsigned)a.O);
+    k_reduce_tree1<<<g1, 256, 0, s>>>(a, pf, pi, G);
+    AMC_CUDA(cudaGetLastError());
+    k_reduce_tree2<<<(unsigned)((a.O + 127) / 128), 128, 0, s>>>(a, pf, pi, G);
+    AMC_CUDA(cudaGetLastError());
+    return AMC_OK;
+  }
+  if (a.R == 0) {
+    // empty reduction: neutral element (and mean of nothing = 0/0 as the reference)
+  }
+  // tile shape: outputs per CTA so that the grid covers the SMs, RC to fit smem
+  long long O = a.O;
+  int OT = 256;
+  while (OT > 1 && (O + OT - 1) / OT < (long long)sms * 2) OT >>= 1;
+  int RC = (int)(a.R < 1 ? 1 : a.R);
+  int maxRC = (int)((48 * 1024) / (8 * OT)) - 1;
+  if (maxRC < 1) maxRC = 1;
+  if (RC > maxRC) RC = maxRC;
+  // thread->element mapping: outputs fastest when the first leaf moves less
+  // along the innermost kept axis than along the innermost reduced axis.
+  int ofast = 1;
+  if (a.orank > 0 && a.rrank > 0) {
+    long long so = a.leaf_o[0].strides[a.orank - 1], sr = a.leaf_r[0][a.rrank - 1];
+    so = so < 0 ? -so : so;
+    sr = sr < 0 ? -sr : sr;
+    ofast = (sr == 1 && so != 1) ? 0 : 1;
+    if (so == 0 && sr != 0) ofast = 0;
+  } else if (a.orank == 0) {
+    ofast = 0;
+  }
+  size_t sm = (size_t)OT * (RC + 1) * 8;
+  unsigned grid = (unsigned)((O + OT - 1) / OT);
+  k_reduce_seq<<<grid, 256, sm, s>>>(a, OT, RC, ofast);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ pad (structural-ops.scm:449-507)
+__global__ void k_pad(const __grid_constant__ PadArgs a) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < a.total; i += stride) {
+    long long rem = i, off = 0;
+    bool inb = true;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      long long c = rem % a.oshape[d];
+      rem /= a.oshape[d];
+      long long dim = a.sshape[d], s = c - a.before[d];
+      if (a.mode == AMC_PAD_CONSTANT) {
+        if (s < 0 || s >= dim) inb = false;
+      } else if (a.mode == AMC_PAD_EDGE) {
+        s = s < 0 ? 0 : (s >= dim ? dim - 1 : s);
+      } else {
+        for (int guard = 0; guard < 64 && (s < 0 || s >= dim); ++guard) s = s < 0 ? (-1 - s) : (2 * dim - s - 1);
+        if (s < 0 || s >= dim) s = 0;
+      }
+      off += s * a.sstrides[d];
+    }
+    if (inb) store_num(a.out, a.out_dtype, i, load_num(a.src, a.src_dtype, off));
+    else store_num(a.out, a.out_dtype, i, nfl(a.value));
+  }
+}
+
+int launch_pad(const PadArgs& a, cudaStream_t s) {
+  if (!a.total) return AMC_OK;
+  k_pad<<<grid_for(a.total, 256), 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ im2col (structural-ops.scm:581-627)
+__global__ void k_im2col(const __grid_constant__ Im2colArgs a) {
+  long long rows = a.C * a.KH * a.KW, cols = a.OH * a.OW, total = a.N * rows * cols;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < total; i += stride) {
+    long long c = i % cols, r = (i / cols) % rows, n = i / (rows * cols);
+    long long ch = r / (a.KH * a.KW), kh = (r / a.KW) % a.KH, kw = r % a.KW, oh = c / a.OW, ow = c % a.OW;
+    long long ih = oh * a.SH + kh - a.PH, iw = ow * a.SW + kw - a.PW;
+    if (ih >= 0 && ih < a.H && iw >= 0 && iw < a.W)
+      store_num(a.out, a.out_dtype, i, load_num(a.src, a.src_dtype, n * a.sN + ch * a.sC + ih * a.sH + iw * a.sW));
+    else
+      store_num(a.out, a.out_dtype, i, nfl(0.0));
+  }
+}
+
+int launch_im2col(const Im2colArgs& a, cudaStream_t s) {
+  long long total = a.N * a.C * a.KH * a.KW * a.OH * a.OW;
+  if (!total) return AMC_OK;
+  k_im2col<<<grid_for(total, 256), 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ col2im
+// Gather form of the reference's scatter-add (realization.scm:1196-1268):
+// output (n,c,h,w) receives col[(n), (c,kh,kw), (oh,ow)] for every window
+// position covering it, added in ascending col-row order (kh, then kw), the
+// order the reference's outer col-row loop visits them.
+__global__ void k_col2im(const __grid_constant__ Col2imArgs a) {
+  long long total = a.N * a.C * a.H * a.W;
+  long long rows = a.C * a.KH * a.KW, cols = a.OH * a.OW;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  const bool fp = a.out_dtype == AMC_F32 || a.out_dtype == AMC_F64;
+  for (; i < total; i += stride) {
+    long long w = i % a.W, h = (i / a.W) % a.H, c = (i / (a.W * a.H)) % a.C, n = i / (a.W * a.H * a.C);
+    Num acc = nfl(0.0);
+    if (!fp) acc = nex(0);
+    for (int kh = 0; kh < a.KH; ++kh) {
+      long long th = h + a.PH - kh;
+      if (th < 0 || th % a.SH) continue;
+      long long oh = th / a.SH;
+      if (oh >= a.OH) continue;
+      for (int kw = 0; kw < a.KW; ++kw) {
+        long long tw = w + a.PW - kw;
+        if (tw < 0 || tw % a.SW) continue;
+        long long ow = tw / a.SW;
+        if (ow >= a.OW) continue;
+        long long r = c * a.KH * a.KW + kh * a.KW + kw;
+        Num v = load_num(a.col, a.col_dtype, n * rows * cols + r * cols + oh * a.OW + ow);
+        acc = round_store(a.out_dtype, bin_op(AMC_OP_ADD, acc, v));
+      }
+    }
+    store_num(a.out, a.out_dtype, i, acc);
+  }
+}
+
+int launch_col2im(const Col2imArgs& a, cudaStream_t s) {
+  long long total = a.N * a.C * a.H * a.W;
+  if (!total) return AMC_OK;
+  k_col2im<<<grid_for(total, 256), 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ stack / concat routing
+__global__ void k_route(const __grid_constant__ RouteArgs a) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < a.total; i += stride) {
+    long long idx[AMC_MAX_RANK];
+    long long rem = i;
+    for (int d = a.rank - 1; d >= 0; --d) { idx[d] = rem % a.oshape[d]; rem /= a.oshape[d]; }
+    int src = 0;
+    long long off = 0;
+    if (a.is_stack) {
+      src = (int)idx[a.axis];
+      const DLeaf& L = a.srcs[src];
+      int k = 0;
+      for (int d = 0; d < a.rank; ++d) if (d != a.axis) off += idx[d] * L.strides[k++];
+    } else {
+      long long pos = idx[a.axis];
+      while (src < a.nsrc - 1 && pos >= a.extents[src]) pos -= a.extents[src++];
+      idx[a.axis] = pos;
+      const DLeaf& L = a.srcs[src];
+      for (int d = 0; d < a.rank; ++d) off += idx[d] * L.strides[d];
+    }
+    store_num(a.out, a.out_dtype, i, load_num(a.srcs[src].ptr, a.srcs[src].dtype, off));
+  }
+}
+
+int launch_route(const RouteArgs& a, cudaStream_t s) {
+  if (!a.total) return AMC_OK;
+  k_route<<<grid_for(a.total, 256), 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ GEMM (double accumulation)
+// Tiles of 64x64 outputs, 4x4 per thread, K staged through shared memory as
+// doubles.  Each output accumulates a*b in ascending k from 0.0 with separate
+// multiply and add roundings, the reference's loop exactly.
+__global__ void __launch_bounds__(256) k_gemm(const __grid_constant__ GemmArgs a) {
+  __shared__ double As[16][64 + 1];
+  __shared__ double Bs[16][64 + 1];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const long long m0 = (long long)blockIdx.y * 64, n0 = (long long)blockIdx.x * 64;
+  double acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+  for (long long k0 = 0; k0 < a.K; k0 += 16) {
+    for (int e = threadIdx.x; e < 16 * 64; e += 256) {
+      int kk = e / 64, mm = e % 64;
+      long long m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < a.M && k < a.K) ? load_f(a.A, a.a_dtype, m * a.sa0 + k * a.sa1) : 0.0;
+      long long n = n0 + mm;
+      Bs[kk][mm] = (n < a.N && k < a.K) ? load_f(a.B, a.b_dtype, k * a.sb0 + n * a.sb1) : 0.0;
+    }
+    __syncthreads();
+    int kmax = (int)((a.K - k0) < 16 ? (a.K - k0) : 16);
+    for (int kk = 0; kk < kmax; ++kk) {
+      double av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[kk][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[kk][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __dadd_rn(acc[i][j], __dmul_rn(av[i], bv[j]));
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      long long m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+      if (m < a.M && n < a.N) {
+        double v = acc[i][j];
+        if (a.alpha != 1.0) v = __dmul_rn(a.alpha, v);
+        if (a.beta != 0.0) v = __dadd_rn(v, __dmul_rn(a.beta, load_f(a.C, a.c_dtype, m * a.N + n)));
+        store_num(a.C, a.c_dtype, m * a.N + n, nfl(v));
+      }
+    }
+}
+
+int launch_gemm(const GemmArgs& a, cudaStream_t s) {
+  if (a.M == 0 || a.N == 0) return AMC_OK;
+  if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "gemm: injected launch failure (AMC_FAULT=launch)");
+  dim3 g((unsigned)((a.N + 63) / 64), (unsigned)((a.M + 63) / 64));
+  k_gemm<<<g, 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+// ------------------------------------------------------------------ attention (reference order)
+// One warp per query row.  Pass 1: each lane computes whole scores for its
+// keys with the j-sum in ascending order, stores them rounded to the dtype in
+// shared memory and tracks the unrounded row max.  Pass 2: e_k = exp(s_k - max)
+// rounded to the dtype; Z summed in double.  Pass 3: each lane owns output
+// columns and accumulates (e_k/Z)*V[k,p] in ascending k.
+__global__ void __launch_bounds__(128) k_attention_generic(const __grid_constant__ AttnArgs a) {
+  extern __shared__ double att_sm[];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, wpb = blockDim.x / 32;
+  double* s = att_sm + (size_t)warp * a.n;
+  long long row = (long long)blockIdx.x * wpb + warp;
+  long long rows = a.blocks * a.n;
+  if (row >= rows) return;
+  long long b = row / a.n, i = row % a.n;
+  const long long qb = b * a.qb + i * a.q0, kb = b * a.kb, vb = b * a.vb;
+  double rmax = -INFINITY;
+  for (int k = lane; k < a.n; k += 32) {
+    double acc = 0.0;
+    for (int j = 0; j < a.dk; ++j)
+      acc = __dadd_rn(acc, __dmul_rn(load_f(a.Q, a.dtype, qb + j * a.q1), load_f(a.K, a.dtype, kb + k * a.k0 + j * a.k1)));
+    double score = __dmul_rn(a.scale, acc);
+    s[k] = a.dtype == AMC_F32 ? (double)__double2float_rn(score) : score;
+    rmax = score > rmax ? score : rmax;
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    double t = __shfl_xor_sync(0xffffffffu, rmax, o);
+    rmax = t > rmax ? t : rmax;
+  }
+  double Z = 0.0;
+  for (int k = lane; k < a.n; k += 32) {
+    double e = exp(s[k] - rmax);
+    e = a.dtype == AMC_F32 ? (double)__double2float_rn(e) : e;
+    s[k] = e;
+    Z += e;
+  }
+  for (int o = 16; o > 0; o >>= 1) Z += __shfl_xor_sync(0xffffffffu, Z, o);
+  __syncwarp();
+  for (int p = lane; p < a.dv; p += 32) {
+    double acc = 0.0;
+    for (int k = 0; k < a.n; ++k)
+      acc = __dadd_rn(acc, __dmul_rn(__ddiv_rn(s[k], Z), load_f(a.V, a.dtype, vb + k * a.v0 + p * a.v1)));
+    store_num(a.O, a.dtype, row * a.dv + p, nfl(acc));
+  }
+}
+
+int launch_attention_generic(const AttnArgs& a, cudaStream_t s) {
+  long long rows = a.blocks * a.n;
+  if (!rows) return AMC_OK;
+  int wpb = 4;
+  size_t sm = (size_t)wpb * a.n * sizeof(double);
+  if (sm > 200 * 1024) {
+    wpb = 1;
+    sm = (size_t)a.n * sizeof(double);
+  }
+  if (sm > 200 * 1024) return fail(AMC_ERR_UNSUPPORTED, "attention: sequence too long for the reference-order kernel");
+  if (sm > 48 * 1024) AMC_CUDA(cudaFuncSetAttribute(k_attention_generic, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+  k_attention_generic<<<(unsigned)((rows + wpb - 1) / wpb), wpb * 32, sm, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+}  // namespace amc

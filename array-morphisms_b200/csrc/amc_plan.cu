@@ -1,0 +1,1086 @@
+// The realize planner.  Input: the morphism tree the reference's realize
+// would walk (realization.scm:92-115), serialized as amc_node records.
+// Output: a list of device launches over buffers fixed at plan creation.
+//
+// Lowering rules (each keeps the reference's values):
+//   - reshape / transpose / slice of a concrete view are zero-copy views
+//     (create-view, realization.scm:649-717).  A reshape the strides cannot
+//     express (the reference's execute-affine-morphism copy, :849-862) is a
+//     copy in logical row-major order.
+//   - element-wise nodes stay lazy: a node is a postfix program over strided
+//     leaf views broadcast to its shape.  Operands that are themselves lazy
+//     are inlined, followed by a store conversion to the operand's dtype, so
+//     the fused kernel rounds exactly where the reference materialises.
+//     Transposes and slices of lazy nodes move onto their leaves.
+//   - a reduction evaluates its (lazy) operand at source coordinates and folds
+//     in the reference's order (realization.scm:1309-1388).
+//   - im2col without padding is a strided view when the strides allow it;
+//     otherwise it, pad, col2im, stack and concat are gather kernels.
+//   - matmul / matvec / dot run the double-accumulating GEMM; attention runs
+//     the streaming-softmax kernels.
+//   - the polyphase filter bank (a tap reduction of a product of a windowed
+//     view and a broadcast filter) runs the streaming FIR kernel.
+#include <algorithm>
+#include <cstring>
+#include <functional>
+#include <optional>
+
+#include "amc_internal.h"
+#include "amc_plan.h"
+
+namespace amc {
+
+// ------------------------------------------------------------------ views
+struct View {
+  uint64_t buf = 0;
+  int32_t dtype = AMC_F64;
+  int32_t rank = 0;
+  int64_t shape[AMC_MAX_RANK] = {0};
+  int64_t strides[AMC_MAX_RANK] = {0};
+  int64_t offset = 0;
+};
+
+static int64_t numel(int32_t rank, const int64_t* shape) {
+  int64_t n = 1;
+  for (int i = 0; i < rank; ++i) n *= shape[i];
+  return n;
+}
+
+static void row_major(int32_t rank, const int64_t* shape, int64_t* strides) {
+  int64_t s = 1;
+  for (int i = rank - 1; i >= 0; --i) {
+    strides[i] = s;
+    s *= shape[i];
+  }
+}
+
+static bool same_view(const View& a, const View& b) {
+  if (a.buf != b.buf || a.dtype != b.dtype || a.rank != b.rank || a.offset != b.offset) return false;
+  for (int i = 0; i < a.rank; ++i)
+    if (a.shape[i] != b.shape[i] || a.strides[i] != b.strides[i]) return false;
+  return true;
+}
+
+// Stride-only reshape (merge/split of dims that are laid out compatibly).
+static bool try_reshape(const View& v, int32_t nrank, const int64_t* nshape, View& out) {
+  out = v;
+  out.rank = nrank;
+  for (int i = 0; i < nrank; ++i) out.shape[i] = nshape[i];
+  int64_t total = numel(v.rank, v.shape);
+  if (total != numel(nrank, nshape)) return false;
+  if (total == 0) {
+    row_major(nrank, nshape, out.strides);
+    return true;
+  }
+  int64_t od[AMC_MAX_RANK], os[AMC_MAX_RANK];
+  int on = 0;
+  for (int i = 0; i < v.rank; ++i)
+    if (v.shape[i] != 1) { od[on] = v.shape[i]; os[on] = v.strides[i]; ++on; }
+  int64_t ns[AMC_MAX_RANK];
+  int oi = 0, oj = 1, ni = 0, nj = 1;
+  while (ni < nrank && oi < on) {
+    if (nshape[ni] == 1) { ns[ni] = 0; ++ni; nj = ni + 1; continue; }
+    int64_t np = nshape[ni], op = od[oi];
+    while (np != op) {
+      if (np < op) { if (nj >= nrank) return false; np *= nshape[nj++]; }
+      else { if (oj >= on) return false; op *= od[oj++]; }
+    }
+    for (int ok = oi; ok < oj - 1; ++ok)
+      if (os[ok] != od[ok + 1] * os[ok + 1]) return false;
+    ns[nj - 1] = os[oj - 1];
+    for (int nk = nj - 1; nk > ni; --nk) ns[nk - 1] = ns[nk] * nshape[nk];
+    ni = nj++;
+    oi = oj++;
+  }
+  for (; ni < nrank; ++ni) ns[ni] = 0;  // trailing size-1 dims
+  for (int i = 0; i < nrank; ++i) out.strides[i] = ns[i];
+  return true;
+}
+
+// Broadcast a view to a target shape (numpy rules: trailing alignment, size-1
+// dims and missing leading dims get stride 0; basic-ops.scm:84-115).
+static bool broadcast_to(const View& v, int32_t rank, const int64_t* shape, View& out) {
+  if (v.rank > rank) return false;
+  out = v;
+  out.rank = rank;
+  int lead = rank - v.rank;
+  for (int d = 0; d < rank; ++d) {
+    out.shape[d] = shape[d];
+    if (d < lead) { out.strides[d] = 0; continue; }
+    int64_t s = v.shape[d - lead];
+    if (s == shape[d]) out.strides[d] = v.strides[d - lead];
+    else if (s == 1) out.strides[d] = 0;
+    else return false;
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ values
+struct Val {
+  bool expr = false;
+  View view;                   // concrete value
+  int32_t dtype = AMC_F64;     // lazy value
+  int32_t rank = 0;
+  int64_t shape[AMC_MAX_RANK] = {0};
+  std::vector<View> leaves;
+  std::vector<amc_insn> prog;
+};
+
+static amc_insn ins(int op, int a = 0, double imm = 0.0) {
+  amc_insn I;
+  I.op = op;
+  I.a = a;
+  I.imm = imm;
+  return I;
+}
+
+// ------------------------------------------------------------------ plan
+int Plan::add_slot(int32_t dtype, int64_t n, const std::vector<uint64_t>& reads, uint64_t* h) {
+  int rc;
+  if (ctx) rc = ctx_alloc(ctx, dtype, n, reads, h);
+  else rc = buf_alloc(dtype, n, h);
+  if (rc) return rc;
+  slots.push_back(*h);
+  bytes += (int64_t)n * (int64_t)dtype_size(dtype);
+  return AMC_OK;
+}
+
+Plan::~Plan() {
+  if (graph_exec) cudaGraphExecDestroy(graph_exec);
+  for (uint64_t h : slots) buf_release(h);
+  for (uint64_t h : held) buf_release(h);
+  for (void* p : dev_small) cudaFree(p);
+  if (result.buf && result_owned) buf_release(result.buf);
+}
+
+struct Builder {
+  const amc_node* nodes;
+  int32_t n;
+  Plan* plan;
+  std::vector<std::optional<Val>> memo;
+
+  int err(int code, const std::string& m) { return fail(code, "plan: " + m); }
+
+  void* ptr_of(uint64_t h) {
+    Buffer* b = buf_get(h);
+    return b ? b->ptr : nullptr;
+  }
+
+  DLeaf dleaf(const View& v, int rank_check = -1) {
+    DLeaf L;
+    memset(&L, 0, sizeof L);
+    L.ptr = (const char*)ptr_of(v.buf) + v.offset * (int64_t)dtype_size(v.dtype);
+    L.dtype = v.dtype;
+    for (int d = 0; d < v.rank; ++d) L.strides[d] = v.strides[d];
+    (void)rank_check;
+    return L;
+  }
+
+  int leaf_view(const amc_node& nd, View& v) {
+    const amc_view& lv = nd.leaf;
+    Buffer* b = buf_get(lv.buf);
+    if (!b) return err(AMC_ERR_INVALID, "leaf refers to an unknown buffer");
+    if (lv.dtype != b->dtype) return err(AMC_ERR_INVALID, "leaf dtype does not match its buffer");
+    if (lv.rank < 0 || lv.rank > AMC_MAX_RANK) return err(AMC_ERR_INVALID, "leaf rank out of range");
+    v.buf = lv.buf;
+    v.dtype = lv.dtype;
+    v.rank = lv.rank;
+    v.offset = lv.offset;
+    int64_t lo = lv.offset, hi = lv.offset;
+    bool empty = false;
+    for (int d = 0; d < lv.rank; ++d) {
+      v.shape[d] = lv.shape[d];
+      v.strides[d] = lv.strides[d];
+      if (lv.shape[d] < 0) return err(AMC_ERR_INVALID, "negative extent");
+      if (lv.shape[d] == 0) empty = true;
+      else if (lv.strides[d] >= 0) hi += (lv.shape[d] - 1) * lv.strides[d];
+      else lo += (lv.shape[d] - 1) * lv.strides[d];
+    }
+    if (!empty && (lo < 0 || hi >= b->nelem)) return err(AMC_ERR_INVALID, "leaf view reaches outside its buffer");
+    return AMC_OK;
+  }
+
+  // A contiguous output slot of the given dtype/shape.
+  int new_slot(int32_t dtype, int32_t rank, const int64_t* shape, const std::vector<uint64_t>& reads, View& v) {
+    uint64_t h = 0;
+    int rc = plan->add_slot(dtype, numel(rank, shape), reads, &h);
+    if (rc) return rc;
+    v = View();
+    v.buf = h;
+    v.dtype = dtype;
+    v.rank = rank;
+    for (int d = 0; d < rank; ++d) v.shape[d] = shape[d];
+    row_major(rank, shape, v.strides);
+    v.offset = 0;
+    return AMC_OK;
+  }
+
+  static std::vector<uint64_t> reads_of(const std::vector<View>& vs) {
+    std::vector<uint64_t> r;
+    for (auto& v : vs) r.push_back(v.buf);
+    return r;
+  }
+
+  Val as_expr(const Val& x) {
+    if (x.expr) return x;
+    Val e;
+    e.expr = true;
+    e.dtype = x.view.dtype;
+    e.rank = x.view.rank;
+    for (int d = 0; d < e.rank; ++d) e.shape[d] = x.view.shape[d];
+    e.leaves.push_back(x.view);
+    e.prog.push_back(ins(AMC_OP_LOAD, 0));
+    return e;
+  }
+
+  static void fill_prog(DProg& P, const std::vector<amc_insn>& prog, const std::vector<View>& leaves) {
+    P.n = (int32_t)prog.size();
+    bool allf = true;
+    for (auto& I : prog) {
+      if (I.op == AMC_OP_ICONST) allf = false;
+      if (I.op == AMC_OP_CVT && !dtype_float(I.a)) allf = false;
+    }
+    for (auto& L : leaves)
+      if (!dtype_float(L.dtype)) allf = false;
+    P.all_float = allf ? 1 : 0;
+    for (size_t i = 0; i < prog.size(); ++i) P.code[i] = prog[i];
+  }
+
+  // Materialise a value into a fresh contiguous slot.
+  int materialize(const Val& x, View& out) {
+    Val e = as_expr(x);
+    int rc = new_slot(e.dtype, e.rank, e.shape, reads_of(e.leaves), out);
+    if (rc) return rc;
+    MapArgs a;
+    memset(&a, 0, sizeof a);
+    a.rank = e.rank;
+    for (int d = 0; d < e.rank; ++d) a.shape[d] = e.shape[d];
+    a.total = numel(e.rank, e.shape);
+    a.nleaf = (int32_t)e.leaves.size();
+    for (size_t l = 0; l < e.leaves.size(); ++l) a.leaf[l] = dleaf(e.leaves[l]);
+    fill_prog(a.prog, e.prog, e.leaves);
+    a.out = ptr_of(out.buf);
+    a.out_dtype = e.dtype;
+    collapse_map(a);
+    plan->steps.push_back([a](cudaStream_t s) { return launch_map(a, s); });
+    plan->launches += 1;
+    return AMC_OK;
+  }
+
+  // Merge adjacent dims that every leaf (and the contiguous output) walks
+  // linearly; drops size-1 dims.
+  static void collapse_map(MapArgs& a) {
+    int r = 0;
+    int64_t sh[AMC_MAX_RANK];
+    int64_t st[kMaxLeaves][AMC_MAX_RANK];
+    for (int d = 0; d < a.rank; ++d) {
+      if (a.shape[d] == 1) continue;
+      if (r > 0) {
+        bool ok = true;
+        for (int l = 0; l < a.nleaf; ++l)
+          if (st[l][r - 1] != a.leaf[l].strides[d] * a.shape[d]) ok = false;
+        if (ok) {
+          sh[r - 1] *= a.shape[d];
+          for (int l = 0; l < a.nleaf; ++l) st[l][r - 1] = a.leaf[l].strides[d];
+          continue;
+        }
+      }
+      sh[r] = a.shape[d];
+      for (int l = 0; l < a.nleaf; ++l) st[l][r] = a.leaf[l].strides[d];
+      ++r;
+    }
+    if (r == 0) {
+      r = 1;
+      sh[0] = 1;
+      for (int l = 0; l < a.nleaf; ++l) st[l][0] = 0;
+    }
+    a.rank = r;
+    for (int d = 0; d < r; ++d) {
+      a.shape[d] = sh[d];
+      for (int l = 0; l < a.nleaf; ++l) a.leaf[l].strides[d] = st[l][d];
+    }
+    for (int d = r; d < AMC_MAX_RANK; ++d) {
+      a.shape[d] = 1;
+      for (int l = 0; l < a.nleaf; ++l) a.leaf[l].strides[d] = 0;
+    }
+  }
+
+  int concrete(int idx, View& out) {
+    Val v;
+    int rc = get(idx, v);
+    if (rc) return rc;
+    if (!v.expr) { out = v.view; return AMC_OK; }
+    rc = materialize(v, out);
+    if (rc) return rc;
+    memo[idx] = Val();
+    memo[idx]->view = out;
+    return AMC_OK;
+  }
+
+  // Append the program of operand value x (broadcast to shape) into e.
+  bool inline_operand(Val& e, const Val& x, int32_t rank, const int64_t* shape) {
+    Val xe = as_expr(x);
+    std::vector<int> remap;
+    for (auto& L : xe.leaves) {
+      View b;
+      if (!broadcast_to(L, rank, shape, b)) return false;
+      int found = -1;
+      for (size_t k = 0; k < e.leaves.size(); ++k)
+        if (same_view(e.leaves[k], b)) { found = (int)k; break; }
+      if (found < 0) {
+        if ((int)e.leaves.size() >= kMaxLeaves) return false;
+        e.leaves.push_back(b);
+        found = (int)e.leaves.size() - 1;
+      }
+      remap.push_back(found);
+    }
+    if (e.prog.size() + xe.prog.size() + 1 > AMC_PROG_MAX) return false;
+    for (auto I : xe.prog) {
+      if (I.op == AMC_OP_LOAD) I.a = remap[I.a];
+      e.prog.push_back(I);
+    }
+    if (x.expr) e.prog.push_back(ins(AMC_OP_CVT, x.dtype));
+    return true;
+  }
+
+  int node_map(const amc_node& nd, Val& out) {
+    if (nd.n_in < 1 || nd.n_in > AMC_NODE_MAX_IN) return err(AMC_ERR_INVALID, "map node needs 1..4 operands");
+    if (!nd.prog || nd.prog_len <= 0 || nd.prog_len > AMC_PROG_MAX) return err(AMC_ERR_INVALID, "map node without a program");
+    // validate program stack discipline
+    {
+      int sp = 0;
+      for (int i = 0; i < nd.prog_len; ++i) {
+        int op = nd.prog[i].op;
+        if (op == AMC_OP_LOAD) { if (nd.prog[i].a < 0 || nd.prog[i].a >= nd.n_in) return err(AMC_ERR_INVALID, "LOAD of a missing operand"); ++sp; }
+        else if (op == AMC_OP_CONST || op == AMC_OP_ICONST) ++sp;
+        else if (op == AMC_OP_CVT) { if (sp < 1 || !dtype_valid(nd.prog[i].a)) return err(AMC_ERR_INVALID, "bad CVT"); }
+        else if (op >= AMC_OP_NEG && op <= AMC_OP_TANH) { if (sp < 1) return err(AMC_ERR_INVALID, "stack underflow"); }
+        else if (op >= AMC_OP_ADD && op <= AMC_OP_LE) { if (sp < 2) return err(AMC_ERR_INVALID, "stack underflow"); --sp; }
+        else return err(AMC_ERR_INVALID, "unknown opcode");
+        if (sp > AMC_STACK_MAX) return err(AMC_ERR_INVALID, "program needs too deep a stack");
+      }
+      if (sp != 1) return err(AMC_ERR_INVALID, "program must leave one value");
+    }
+    Val e;
+    e.expr = true;
+    e.dtype = nd.dtype;
+    e.rank = nd.rank;
+    for (int d = 0; d < nd.rank; ++d) e.shape[d] = nd.shape[d];
+    // operand programs become sub-programs; record where each starts
+    std::vector<std::vector<amc_insn>> sub(nd.n_in);
+    for (int k = 0; k < nd.n_in; ++k) {
+      Val x;
+      int rc = get(nd.in[k], x);
+      if (rc) return rc;
+      Val trial = e;
+      trial.prog.clear();
+      if (!inline_operand(trial, x, e.rank, e.shape)) {
+        View m;
+        if (x.expr) {
+          rc = materialize(x, m);
+          if (rc) return rc;
+        } else {
+          m = x.view;
+        }
+        Val mv;
+        mv.view = m;
+        trial = e;
+        trial.prog.clear();
+        if (!inline_operand(trial, mv, e.rank, e.shape)) return err(AMC_ERR_INVALID, "operand shape does not broadcast");
+      }
+      e.leaves = trial.leaves;
+      sub[k] = trial.prog;
+    }
+    // splice: each LOAD k of the node program becomes operand k's sub-program
+    std::vector<amc_insn> prog;
+    for (int i = 0; i < nd.prog_len; ++i) {
+      const amc_insn& I = nd.prog[i];
+      if (I.op == AMC_OP_LOAD) prog.insert(prog.end(), sub[I.a].begin(), sub[I.a].end());
+      else prog.push_back(I);
+    }
+    if (prog.size() > AMC_PROG_MAX) {
+      // too long: materialise the operands and use plain loads
+      e.leaves.clear();
+      std::vector<View> ms;
+      for (int k = 0; k < nd.n_in; ++k) {
+        View m;
+        int rc = concrete(nd.in[k], m);
+        if (rc) return rc;
+        View b;
+        if (!broadcast_to(m, e.rank, e.shape, b)) return err(AMC_ERR_INVALID, "operand shape does not broadcast");
+        e.leaves.push_back(b);
+      }
+      prog.assign(nd.prog, nd.prog + nd.prog_len);
+    }
+    e.prog = prog;
+    out = e;
+    return AMC_OK;
+  }
+
+  int node_view(const amc_node& nd, Val& out) {
+    if (nd.n_in != 1) return err(AMC_ERR_INVALID, "view node needs one operand");
+    Val x;
+    int rc = get(nd.in[0], x);
+    if (rc) return rc;
+    int32_t r = x.expr ? x.rank : x.view.rank;
+    const int64_t* xs = x.expr ? x.shape : x.view.shape;
+    auto apply = [&](View& v) -> bool {
+      if (nd.kind == AMC_N_TRANSPOSE) {
+        View t = v;
+        for (int d = 0; d < r; ++d) {
+          int p = (int)nd.iparam[d];
+          t.shape[d] = v.shape[p];
+          t.strides[d] = v.strides[p];
+        }
+        v = t;
+        return true;
+      }
+      // slice: strides scale by step, offset moves by start
+      for (int d = 0; d < r; ++d) {
+        v.offset += nd.iparam[d] * v.strides[d];
+        v.strides[d] *= nd.iparam[8 + d];
+        v.shape[d] = nd.shape[d];
+      }
+      return true;
+    };
+    if (nd.kind == AMC_N_TRANSPOSE) {
+      if (nd.rank != r) return err(AMC_ERR_INVALID, "transpose rank mismatch");
+      std::vector<int> seen(r, 0);
+      for (int d = 0; d < r; ++d) {
+        int p = (int)nd.iparam[d];
+        if (p < 0 || p >= r || seen[p]) return err(AMC_ERR_INVALID, "invalid permutation");
+        seen[p] = 1;
+      }
+    } else {
+      if (nd.rank != r) return err(AMC_ERR_INVALID, "slice rank mismatch");
+      for (int d = 0; d < r; ++d) {
+        int64_t st = nd.iparam[d], step = nd.iparam[8 + d];
+        if (step <= 0 || st < 0 || (xs[d] > 0 && st >= xs[d]) || nd.shape[d] < 0 ||
+            (nd.shape[d] > 0 && st + (nd.shape[d] - 1) * step >= xs[d]))
+          return err(AMC_ERR_INVALID, "slice out of range");
+      }
+    }
+    if (!x.expr) {
+      out = x;
+      apply(out.view);
+      return AMC_OK;
+    }
+    out = x;
+    for (auto& L : out.leaves) apply(L);
+    for (int d = 0; d < nd.rank; ++d) out.shape[d] = nd.shape[d];
+    return AMC_OK;
+  }
+
+  int node_reshape(const amc_node& nd, Val& out) {
+    if (nd.n_in != 1) return err(AMC_ERR_INVALID, "reshape needs one operand");
+    Val x;
+    int rc = get(nd.in[0], x);
+    if (rc) return rc;
+    int64_t have = x.expr ? numel(x.rank, x.shape) : numel(x.view.rank, x.view.shape);
+    if (have != numel(nd.rank, nd.shape)) return err(AMC_ERR_INVALID, "reshape size mismatch");
+    View src;
+    if (x.expr) {
+      rc = materialize(x, src);
+      if (rc) return rc;
+    } else {
+      src = x.view;
+    }
+    View v;
+    if (!try_reshape(src, nd.rank, nd.shape, v)) {
+      // copy in the source's logical order, then view
+      Val sv;
+      sv.view = src;
+      View m;
+      rc = materialize(sv, m);
+      if (rc) return rc;
+      if (!try_reshape(m, nd.rank, nd.shape, v)) return err(AMC_ERR_INVALID, "reshape failed");
+    }
+    out = Val();
+    out.view = v;
+    return AMC_OK;
+  }
+
+  // ----------------------------------------------------------- reduce
+  int node_reduce(const amc_node& nd, Val& out) {
+    if (nd.n_in != 1) return err(AMC_ERR_INVALID, "reduce needs one operand");
+    Val x;
+    int rc = get(nd.in[0], x);
+    if (rc) return rc;
+    Val e = as_expr(x);
+    int op = (int)nd.iparam[0];
+    int64_t mask = nd.iparam[1];
+    if (op < AMC_RED_SUM || op > AMC_RED_MIN) return err(AMC_ERR_INVALID, "unknown reduction");
+    if (!dtype_float(nd.dtype) && (op == AMC_RED_MAX || op == AMC_RED_MIN))
+      return err(AMC_ERR_UNSUPPORTED, "integer max/min reduction: the reference stores +-inf into an integer vector and fails");
+    // the value the reduction reads is the operand node's stored value
+    if (x.expr) {
+      if (e.prog.size() + 1 > AMC_PROG_MAX) {
+        View m;
+        rc = materialize(x, m);
+        if (rc) return rc;
+        Val mv;
+        mv.view = m;
+        e = as_expr(mv);
+      } else {
+        e.prog.push_back(ins(AMC_OP_CVT, x.dtype));
+      }
+    }
+    ReduceArgs a;
+    memset(&a, 0, sizeof a);
+    a.op = op;
+    a.out_dtype = nd.dtype;
+    a.src_dtype = e.dtype;
+    a.nleaf = (int32_t)e.leaves.size();
+    int ko = 0, kr = 0;
+    for (int d = 0; d < e.rank; ++d) {
+      if (mask & (1LL << d)) {
+        a.rshape[kr] = e.shape[d];
+        for (int l = 0; l < a.nleaf; ++l) a.leaf_r[l][kr] = e.leaves[l].strides[d];
+        ++kr;
+      } else {
+        a.oshape[ko] = e.shape[d];
+        ++ko;
+      }
+    }
+    for (int l = 0; l < a.nleaf; ++l) {
+      a.leaf_o[l] = dleaf(e.leaves[l]);
+      int k = 0;
+      for (int d = 0; d < e.rank; ++d)
+        if (!(mask & (1LL << d))) a.leaf_o[l].strides[k++] = e.leaves[l].strides[d];
+      for (; k < AMC_MAX_RANK; ++k) a.leaf_o[l].strides[k] = 0;
+    }
+    a.orank = ko;
+    a.rrank = kr;
+    a.O = numel(ko, a.oshape);
+    a.R = numel(kr, a.rshape);
+    fill_prog(a.prog, e.prog, e.leaves);
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, reads_of(e.leaves), o);
+    if (rc) return rc;
+    a.out = ptr_of(o.buf);
+    if (try_fir(a, e)) {
+      out = Val();
+      out.view = o;
+      return AMC_OK;
+    }
+    size_t need = 0;
+    launch_reduce(a, nullptr, nullptr, 0, &need);
+    void* scratch = nullptr;
+    if (need) {
+      View sv;
+      int64_t sh[1] = {(int64_t)((need + 7) / 8)};
+      rc = new_slot(AMC_F64, 1, sh, {}, sv);
+      if (rc) return rc;
+      scratch = ptr_of(sv.buf);
+    }
+    plan->steps.push_back([a, scratch, need](cudaStream_t s) { return launch_reduce(a, s, scratch, need, nullptr); });
+    plan->launches += need ? 2 : 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  // Recognise the filter-bank reduction: sum over one axis of
+  // fl32(x * h) with x a view whose tap and frame strides coincide.
+  bool try_fir(const ReduceArgs& a, const Val& e) {
+    if (a.op != AMC_RED_SUM || a.out_dtype != AMC_F32 || a.src_dtype != AMC_F32) return false;
+    if (a.nleaf != 2 || a.rrank != 1 || a.orank < 2) return false;
+    // program: LOAD, LOAD, MUL, then store conversions to f32 only
+    const auto& P = e.prog;
+    if (P.size() < 4 || !(P[0].op == AMC_OP_LOAD && P[1].op == AMC_OP_LOAD && P[0].a != P[1].a && P[2].op == AMC_OP_MUL))
+      return false;
+    for (size_t i = 3; i < P.size(); ++i)
+      if (!(P[i].op == AMC_OP_CVT && P[i].a == AMC_F32)) return false;
+    if (e.leaves[0].dtype != AMC_F32 || e.leaves[1].dtype != AMC_F32) return false;
+    // which leaf is the filter: stride 0 over every kept axis but the last
+    int hi = -1;
+    for (int l = 0; l < 2; ++l) {
+      bool filt = true;
+      for (int d = 0; d < a.orank - 1; ++d)
+        if (a.leaf_o[l].strides[d] != 0) filt = false;
+      if (filt) hi = l;
+    }
+    if (hi < 0) return false;
+    int xi = 1 - hi;
+    const int ko = a.orank;
+    FirArgs f;
+    memset(&f, 0, sizeof f);
+    f.taps = (int32_t)a.rshape[0];
+    f.branches = (int32_t)a.oshape[ko - 1];
+    f.frames = a.oshape[ko - 2];
+    if (a.leaf_o[xi].strides[ko - 1] != 1 || a.leaf_o[hi].strides[ko - 1] != 1) return false;
+    f.hop = a.leaf_o[xi].strides[ko - 2];
+    f.x_tstride = a.leaf_r[xi][0];
+    f.h_tstride = a.leaf_r[hi][0];
+    // leading kept axes collapse into one batch axis for x (and the output)
+    int64_t B = 1, xbs = 0;
+    for (int d = ko - 3; d >= 0; --d) {
+      int64_t s = a.leaf_o[xi].strides[d];
+      if (a.oshape[d] == 1) continue;
+      if (B == 1) { xbs = s; B = a.oshape[d]; }
+      else if (s == xbs * B) { B *= a.oshape[d]; }
+      else return false;
+    }
+    f.batch = B;
+    f.x_bstride = xbs;
+    f.x = (const float*)a.leaf_o[xi].ptr;
+    f.h = (const float*)a.leaf_o[hi].ptr;
+    f.out = (float*)a.out;
+    f.o_fstride = f.branches;
+    f.o_bstride = f.frames * f.branches;
+    if (!fir_supported(f)) return false;
+    plan->steps.push_back([f](cudaStream_t s) { return launch_fir(f, s); });
+    plan->launches += 1;
+    plan->used_fir = true;
+    return true;
+  }
+
+  // ----------------------------------------------------------- structural gathers
+  int node_pad(const amc_node& nd, Val& out) {
+    View src;
+    int rc = concrete(nd.in[0], src);
+    if (rc) return rc;
+    if (nd.rank != src.rank) return err(AMC_ERR_INVALID, "pad rank mismatch");
+    PadArgs a;
+    memset(&a, 0, sizeof a);
+    a.rank = nd.rank;
+    a.mode = (int32_t)nd.iparam[0];
+    if (a.mode < AMC_PAD_CONSTANT || a.mode > AMC_PAD_REFLECT) return err(AMC_ERR_INVALID, "unknown pad mode");
+    for (int d = 0; d < nd.rank; ++d) {
+      a.oshape[d] = nd.shape[d];
+      a.sshape[d] = src.shape[d];
+      a.sstrides[d] = src.strides[d];
+      a.before[d] = nd.iparam[1 + 2 * d];
+      if (nd.shape[d] != src.shape[d] + nd.iparam[1 + 2 * d] + nd.iparam[2 + 2 * d]) return err(AMC_ERR_INVALID, "pad shape mismatch");
+      if (src.shape[d] == 0 && nd.shape[d] > 0 && a.mode != AMC_PAD_CONSTANT) return err(AMC_ERR_INVALID, "edge/reflect pad of an empty axis");
+    }
+    a.src = (const char*)ptr_of(src.buf) + src.offset * (int64_t)dtype_size(src.dtype);
+    a.src_dtype = src.dtype;
+    a.value = nd.fparam[0];
+    a.total = numel(nd.rank, nd.shape);
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, {src.buf}, o);
+    if (rc) return rc;
+    a.out = ptr_of(o.buf);
+    a.out_dtype = nd.dtype;
+    plan->steps.push_back([a](cudaStream_t s) { return launch_pad(a, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  int node_im2col(const amc_node& nd, Val& out) {
+    View src;
+    int rc = concrete(nd.in[0], src);
+    if (rc) return rc;
+    if (src.rank != 3 && src.rank != 4) return err(AMC_ERR_INVALID, "im2col needs (C,H,W) or (N,C,H,W)");
+    bool batched = src.rank == 4;
+    int b = batched ? 1 : 0;
+    Im2colArgs a;
+    memset(&a, 0, sizeof a);
+    a.N = batched ? src.shape[0] : 1;
+    a.C = src.shape[b];
+    a.H = src.shape[b + 1];
+    a.W = src.shape[b + 2];
+    a.KH = (int32_t)nd.iparam[0]; a.KW = (int32_t)nd.iparam[1];
+    a.SH = (int32_t)nd.iparam[2]; a.SW = (int32_t)nd.iparam[3];
+    a.PH = (int32_t)nd.iparam[4]; a.PW = (int32_t)nd.iparam[5];
+    if (a.KH <= 0 || a.KW <= 0 || a.SH <= 0 || a.SW <= 0 || a.PH < 0 || a.PW < 0) return err(AMC_ERR_INVALID, "bad im2col parameters");
+    a.OH = 1 + (a.H + 2 * a.PH - a.KH) / a.SH;
+    a.OW = 1 + (a.W + 2 * a.PW - a.KW) / a.SW;
+    if (a.OH <= 0 || a.OW <= 0) return err(AMC_ERR_INVALID, "im2col window larger than the padded image");
+    // zero-copy when no window touches padding and the strides allow it
+    if (a.PH == 0 && a.PW == 0) {
+      View v6 = src;
+      int k = 0;
+      int64_t sN = batched ? src.strides[0] : 0, sC = src.strides[b], sH = src.strides[b + 1], sW = src.strides[b + 2];
+      if (batched) { v6.shape[k] = a.N; v6.strides[k++] = sN; }
+      v6.shape[k] = a.C; v6.strides[k++] = sC;
+      v6.shape[k] = a.KH; v6.strides[k++] = sH;
+      v6.shape[k] = a.KW; v6.strides[k++] = sW;
+      v6.shape[k] = a.OH; v6.strides[k++] = sH * a.SH;
+      v6.shape[k] = a.OW; v6.strides[k++] = sW * a.SW;
+      v6.rank = k;
+      View v;
+      if (try_reshape(v6, nd.rank, nd.shape, v)) {
+        out = Val();
+        out.view = v;
+        return AMC_OK;
+      }
+    }
+    a.sN = batched ? src.strides[0] : 0;
+    a.sC = src.strides[b];
+    a.sH = src.strides[b + 1];
+    a.sW = src.strides[b + 2];
+    a.src = (const char*)ptr_of(src.buf) + src.offset * (int64_t)dtype_size(src.dtype);
+    a.src_dtype = src.dtype;
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, {src.buf}, o);
+    if (rc) return rc;
+    a.out = ptr_of(o.buf);
+    a.out_dtype = nd.dtype;
+    plan->steps.push_back([a](cudaStream_t s) { return launch_im2col(a, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  int node_col2im(const amc_node& nd, Val& out) {
+    View col;
+    int rc = concrete(nd.in[0], col);
+    if (rc) return rc;
+    bool batched = nd.rank == 4;
+    if (!((col.rank == 2 && nd.rank == 3) || (col.rank == 3 && nd.rank == 4))) return err(AMC_ERR_INVALID, "col2im rank mismatch");
+    // the reference reads col linearly from index 0; make it contiguous
+    int64_t rm[AMC_MAX_RANK];
+    row_major(col.rank, col.shape, rm);
+    bool contig = col.offset == 0;
+    for (int d = 0; d < col.rank; ++d)
+      if (col.shape[d] != 1 && col.strides[d] != rm[d]) contig = false;
+    if (!contig) {
+      Val cv;
+      cv.view = col;
+      rc = materialize(cv, col);
+      if (rc) return rc;
+    }
+    Col2imArgs a;
+    memset(&a, 0, sizeof a);
+    int b = batched ? 1 : 0;
+    a.N = batched ? nd.shape[0] : 1;
+    a.C = nd.shape[b];
+    a.H = nd.shape[b + 1];
+    a.W = nd.shape[b + 2];
+    a.KH = (int32_t)nd.iparam[0]; a.KW = (int32_t)nd.iparam[1];
+    a.SH = (int32_t)nd.iparam[2]; a.SW = (int32_t)nd.iparam[3];
+    a.PH = (int32_t)nd.iparam[4]; a.PW = (int32_t)nd.iparam[5];
+    if (a.KH <= 0 || a.KW <= 0 || a.SH <= 0 || a.SW <= 0 || a.PH < 0 || a.PW < 0) return err(AMC_ERR_INVALID, "bad col2im parameters");
+    a.OH = 1 + (a.H + 2 * a.PH - a.KH) / a.SH;
+    a.OW = 1 + (a.W + 2 * a.PW - a.KW) / a.SW;
+    if (col.shape[b] != a.C * a.KH * a.KW) return err(AMC_ERR_INVALID, "col2im: col-rows mismatch");
+    if (col.shape[b + 1] != a.OH * a.OW) return err(AMC_ERR_INVALID, "col2im: col-cols mismatch");
+    if (batched && col.shape[0] != a.N) return err(AMC_ERR_INVALID, "col2im: batch size mismatch");
+    a.col = ptr_of(col.buf);
+    a.col_dtype = col.dtype;
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, {col.buf}, o);
+    if (rc) return rc;
+    a.out = ptr_of(o.buf);
+    a.out_dtype = nd.dtype;
+    plan->steps.push_back([a](cudaStream_t s) { return launch_col2im(a, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  int node_route(const amc_node& nd, Val& out) {
+    const int32_t* ins_ = nd.n_in > AMC_NODE_MAX_IN ? nd.in_ext : nd.in;
+    if (nd.n_in < 1 || !ins_) return err(AMC_ERR_INVALID, "stack/concat needs operands");
+    bool stack = nd.kind == AMC_N_STACK;
+    int axis = (int)nd.iparam[0];
+    if (axis < 0 || axis >= nd.rank) return err(AMC_ERR_INVALID, "stack/concat axis out of range");
+    std::vector<DLeaf> ls(nd.n_in);
+    std::vector<int64_t> ext(nd.n_in);
+    std::vector<uint64_t> reads;
+    int64_t cat = 0;
+    for (int k = 0; k < nd.n_in; ++k) {
+      View v;
+      int rc = concrete(ins_[k], v);
+      if (rc) return rc;
+      int want = stack ? nd.rank - 1 : nd.rank;
+      if (v.rank != want) return err(AMC_ERR_INVALID, "stack/concat operand rank mismatch");
+      for (int d = 0, j = 0; d < nd.rank; ++d) {
+        if (stack && d == axis) continue;
+        if (!stack && d == axis) { ++j; continue; }
+        if (v.shape[j] != nd.shape[d]) return err(AMC_ERR_INVALID, "stack/concat operand shape mismatch");
+        ++j;
+      }
+      ls[k] = dleaf(v);
+      ext[k] = stack ? 1 : v.shape[axis];
+      cat += ext[k];
+      reads.push_back(v.buf);
+    }
+    if (stack ? nd.shape[axis] != nd.n_in : nd.shape[axis] != cat) return err(AMC_ERR_INVALID, "stack/concat extent mismatch");
+    // operand table in device memory (owned by the plan)
+    void* dl = nullptr;
+    void* de = nullptr;
+    AMC_CUDA(cudaMalloc(&dl, ls.size() * sizeof(DLeaf)));
+    plan->dev_small.push_back(dl);
+    AMC_CUDA(cudaMalloc(&de, ext.size() * sizeof(int64_t)));
+    plan->dev_small.push_back(de);
+    AMC_CUDA(cudaMemcpy(dl, ls.data(), ls.size() * sizeof(DLeaf), cudaMemcpyHostToDevice));
+    AMC_CUDA(cudaMemcpy(de, ext.data(), ext.size() * sizeof(int64_t), cudaMemcpyHostToDevice));
+    RouteArgs a;
+    memset(&a, 0, sizeof a);
+    a.rank = nd.rank;
+    a.axis = axis;
+    a.is_stack = stack ? 1 : 0;
+    a.nsrc = nd.n_in;
+    for (int d = 0; d < nd.rank; ++d) a.oshape[d] = nd.shape[d];
+    a.srcs = (const DLeaf*)dl;
+    a.extents = (const int64_t*)de;
+    a.total = numel(nd.rank, nd.shape);
+    View o;
+    int rc = new_slot(nd.dtype, nd.rank, nd.shape, reads, o);
+    if (rc) return rc;
+    a.out = ptr_of(o.buf);
+    a.out_dtype = nd.dtype;
+    plan->steps.push_back([a](cudaStream_t s) { return launch_route(a, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  // ----------------------------------------------------------- BLAS-shaped nodes
+  int node_gemm(const amc_node& nd, Val& out) {
+    if (nd.n_in != 2) return err(AMC_ERR_INVALID, "matmul/matvec/dot need two operands");
+    View A, B;
+    int rc = concrete(nd.in[0], A);
+    if (rc) return rc;
+    rc = concrete(nd.in[1], B);
+    if (rc) return rc;
+    if (!dtype_float(A.dtype) || !dtype_float(B.dtype) || !dtype_float(nd.dtype))
+      return err(AMC_ERR_UNSUPPORTED, "matmul/matvec/dot are defined for f32/f64 (blas-compat.scm:104-105)");
+    GemmArgs g;
+    memset(&g, 0, sizeof g);
+    g.alpha = 1.0;
+    g.beta = 0.0;
+    g.a_dtype = A.dtype;
+    g.b_dtype = B.dtype;
+    g.c_dtype = nd.dtype;
+    g.A = (const char*)ptr_of(A.buf) + A.offset * (int64_t)dtype_size(A.dtype);
+    g.B = (const char*)ptr_of(B.buf) + B.offset * (int64_t)dtype_size(B.dtype);
+    if (nd.kind == AMC_N_MATMUL) {
+      if (A.rank != 2 || B.rank != 2 || A.shape[1] != B.shape[0]) return err(AMC_ERR_INVALID, "matmul shape mismatch");
+      g.M = A.shape[0]; g.K = A.shape[1]; g.N = B.shape[1];
+      g.sa0 = A.strides[0]; g.sa1 = A.strides[1]; g.sb0 = B.strides[0]; g.sb1 = B.strides[1];
+    } else if (nd.kind == AMC_N_MATVEC) {
+      if (A.rank != 2 || B.rank != 1 || A.shape[1] != B.shape[0]) return err(AMC_ERR_INVALID, "matvec shape mismatch");
+      g.M = A.shape[0]; g.K = A.shape[1]; g.N = 1;
+      g.sa0 = A.strides[0]; g.sa1 = A.strides[1]; g.sb0 = B.strides[0]; g.sb1 = 0;
+    } else {
+      if (A.rank != 1 || B.rank != 1 || A.shape[0] != B.shape[0]) return err(AMC_ERR_INVALID, "dot shape mismatch");
+      g.M = 1; g.K = A.shape[0]; g.N = 1;
+      g.sa0 = 0; g.sa1 = A.strides[0]; g.sb0 = B.strides[0]; g.sb1 = 0;
+    }
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, {A.buf, B.buf}, o);
+    if (rc) return rc;
+    if (numel(nd.rank, nd.shape) != g.M * g.N) return err(AMC_ERR_INVALID, "matmul result shape mismatch");
+    g.C = ptr_of(o.buf);
+    plan->steps.push_back([g](cudaStream_t s) { return launch_gemm(g, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  int node_attention(const amc_node& nd, Val& out) {
+    if (nd.n_in != 3) return err(AMC_ERR_INVALID, "attention needs Q, K, V");
+    View Q, K, V;
+    int rc = concrete(nd.in[0], Q);
+    if (!rc) rc = concrete(nd.in[1], K);
+    if (!rc) rc = concrete(nd.in[2], V);
+    if (rc) return rc;
+    if (Q.rank < 2 || Q.rank > 4 || K.rank != Q.rank || V.rank != Q.rank) return err(AMC_ERR_INVALID, "attention operands must share rank 2..4");
+    if (!dtype_float(Q.dtype) || Q.dtype != K.dtype || Q.dtype != V.dtype) return err(AMC_ERR_UNSUPPORTED, "attention needs f32/f64 operands of one dtype");
+    int r = Q.rank;
+    AttnArgs a;
+    memset(&a, 0, sizeof a);
+    a.n = (int32_t)Q.shape[r - 2];
+    a.dk = (int32_t)Q.shape[r - 1];
+    a.dv = (int32_t)V.shape[r - 1];
+    if (K.shape[r - 2] != a.n || K.shape[r - 1] != a.dk || V.shape[r - 2] != a.n) return err(AMC_ERR_INVALID, "attention shape mismatch");
+    a.blocks = 1;
+    for (int d = 0; d < r - 2; ++d) a.blocks *= Q.shape[d];
+    a.dtype = Q.dtype;
+    a.scale = nd.fparam[0];
+    // per-block base = offset + b * stride[rank-3] (execute-fused-attention, :366-373)
+    a.Q = (const char*)ptr_of(Q.buf) + Q.offset * (int64_t)dtype_size(Q.dtype);
+    a.K = (const char*)ptr_of(K.buf) + K.offset * (int64_t)dtype_size(K.dtype);
+    a.V = (const char*)ptr_of(V.buf) + V.offset * (int64_t)dtype_size(V.dtype);
+    a.qb = r > 2 ? Q.strides[r - 3] : 0; a.q0 = Q.strides[r - 2]; a.q1 = Q.strides[r - 1];
+    a.kb = r > 2 ? K.strides[r - 3] : 0; a.k0 = K.strides[r - 2]; a.k1 = K.strides[r - 1];
+    a.vb = r > 2 ? V.strides[r - 3] : 0; a.v0 = V.strides[r - 2]; a.v1 = V.strides[r - 1];
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, {Q.buf, K.buf, V.buf}, o);
+    if (rc) return rc;
+    a.O = ptr_of(o.buf);
+    plan->steps.push_back([a](cudaStream_t s) { return launch_attention_generic(a, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
+  // ----------------------------------------------------------- dispatch
+  int get(int i, Val& out) {
+    if (i < 0 || i >= n) return err(AMC_ERR_INVALID, "operand index out of range");
+    if (memo[i]) { out = *memo[i]; return AMC_OK; }
+    const amc_node& nd = nodes[i];
+    if (!dtype_valid(nd.dtype)) return err(AMC_ERR_INVALID, "invalid dtype");
+    if (nd.rank < 0 || nd.rank > AMC_MAX_RANK) return err(AMC_ERR_INVALID, "rank out of range");
+    for (int d = 0; d < nd.rank; ++d)
+      if (nd.shape[d] < 0) return err(AMC_ERR_INVALID, "negative extent");
+    if (nd.kind != AMC_N_LEAF && nd.n_in <= AMC_NODE_MAX_IN)
+      for (int k = 0; k < nd.n_in; ++k)
+        if (nd.in[k] < 0 || nd.in[k] >= i) return err(AMC_ERR_INVALID, "operands must precede their node");
+    if (nd.kind != AMC_N_LEAF && nd.n_in > AMC_NODE_MAX_IN) {
+      if (!nd.in_ext) return err(AMC_ERR_INVALID, "missing operand table");
+      for (int k = 0; k < nd.n_in; ++k)
+        if (nd.in_ext[k] < 0 || nd.in_ext[k] >= i) return err(AMC_ERR_INVALID, "operands must precede their node");
+    }
+    Val v;
+    int rc = AMC_OK;
+    switch (nd.kind) {
+      case AMC_N_LEAF: rc = leaf_view(nd, v.view); break;
+      case AMC_N_RESHAPE: rc = node_reshape(nd, v); break;
+      case AMC_N_TRANSPOSE:
+      case AMC_N_SLICE: rc = node_view(nd, v); break;
+      case AMC_N_MAP: rc = node_map(nd, v); break;
+      case AMC_N_REDUCE: rc = node_reduce(nd, v); break;
+      case AMC_N_PAD: rc = node_pad(nd, v); break;
+      case AMC_N_IM2COL: rc = node_im2col(nd, v); break;
+      case AMC_N_COL2IM: rc = node_col2im(nd, v); break;
+      case AMC_N_STACK:
+      case AMC_N_CONCAT: rc = node_route(nd, v); break;
+      case AMC_N_MATMUL:
+      case AMC_N_MATVEC:
+      case AMC_N_DOT: rc = node_gemm(nd, v); break;
+      case AMC_N_ATTENTION: rc = node_attention(nd, v); break;
+      default: return err(AMC_ERR_INVALID, "unknown node kind");
+    }
+    if (rc) return rc;
+    memo[i] = v;
+    out = v;
+    return AMC_OK;
+  }
+};
+
+static std::mutex g_plans_mu;
+static std::unordered_map<uint64_t, Plan*> g_plans;
+static uint64_t g_next_plan = 1;
+
+Plan* plan_get(uint64_t h) {
+  std::lock_guard<std::mutex> l(g_plans_mu);
+  auto it = g_plans.find(h);
+  return it == g_plans.end() ? nullptr : it->second;
+}
+
+int plan_create(void* ctx, const amc_node* nodes, int32_t n, uint64_t* out) {
+  if (!nodes || n <= 0 || !out) return fail(AMC_ERR_INVALID, "amc_plan_create: empty tree");
+  if (fault_injected("plan")) return fail(AMC_ERR_INJECTED, "plan: injected failure (AMC_FAULT=plan)");
+  Plan* p = new Plan();
+  p->ctx = ctx;
+  Builder b{nodes, n, p, std::vector<std::optional<Val>>(n)};
+  Val root;
+  int rc = b.get(n - 1, root);
+  if (!rc) {
+    View res;
+    if (root.expr) rc = b.materialize(root, res);
+    else res = root.view;
+    if (!rc) {
+      amc_view& r = p->result;
+      r.buf = res.buf;
+      r.dtype = res.dtype;
+      r.rank = res.rank;
+      for (int d = 0; d < res.rank; ++d) { r.shape[d] = res.shape[d]; r.strides[d] = res.strides[d]; }
+      r.offset = res.offset;
+      buf_retain(res.buf);
+      p->result_owned = true;
+      // hold leaf buffers for the plan's lifetime
+      for (int i = 0; i < n; ++i)
+        if (nodes[i].kind == AMC_N_LEAF) { buf_retain(nodes[i].leaf.buf); p->held.push_back(nodes[i].leaf.buf); }
+    }
+  }
+  if (rc) {
+    delete p;
+    return rc;
+  }
+  std::lock_guard<std::mutex> l(g_plans_mu);
+  *out = g_next_plan++;
+  g_plans[*out] = p;
+  return AMC_OK;
+}
+
+int plan_execute(Plan* p, cudaStream_t s) {
+  if (p->graph_exec) {
+    AMC_CUDA(cudaGraphLaunch(p->graph_exec, s));
+    return AMC_OK;
+  }
+  for (auto& st : p->steps) {
+    int rc = st(s);
+    if (rc) return rc;
+  }
+  return AMC_OK;
+}
+
+}  // namespace amc
+
+using namespace amc;
+
+extern "C" {
+
+int amc_plan_create(const amc_node* nodes, int32_t n, uint64_t* plan) { return plan_create(nullptr, nodes, n, plan); }
+
+int amc_plan_execute(uint64_t h, void* stream) {
+  Plan* p = plan_get(h);
+  if (!p) return fail(AMC_ERR_INVALID, "amc_plan_execute: unknown plan");
+  return plan_execute(p, pick_stream(stream));
+}
+
+int amc_plan_result(uint64_t h, amc_view* out) {
+  Plan* p = plan_get(h);
+  if (!p || !out) return fail(AMC_ERR_INVALID, "amc_plan_result: unknown plan");
+  *out = p->result;
+  buf_retain(p->result.buf);  // the caller owns one reference
+  return AMC_OK;
+}
+
+int amc_plan_stats(uint64_t h, int32_t* launches, int32_t* buffers, int64_t* bytes) {
+  Plan* p = plan_get(h);
+  if (!p) return fail(AMC_ERR_INVALID, "amc_plan_stats: unknown plan");
+  if (launches) *launches = p->launches;
+  if (buffers) *buffers = (int32_t)p->slots.size();
+  if (bytes) *bytes = p->bytes;
+  return AMC_OK;
+}
+
+int amc_plan_capture_graph(uint64_t h, void* stream) {
+  Plan* p = plan_get(h);
+  if (!p) return fail(AMC_ERR_INVALID, "amc_plan_capture_graph: unknown plan");
+  if (p->graph_exec) return AMC_OK;
+  cudaStream_t s = pick_stream(stream);
+  AMC_CUDA(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+  int rc = AMC_OK;
+  for (auto& st : p->steps) {
+    rc = st(s);
+    if (rc) break;
+  }
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(s, &g);
+  if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamEndCapture");
+  e = cudaGraphInstantiate(&p->graph_exec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) { p->graph_exec = nullptr; return cuda_fail(e, "cudaGraphInstantiate"); }
+  return AMC_OK;
+}
+
+int amc_plan_destroy(uint64_t h) {
+  Plan* p = nullptr;
+  {
+    std::lock_guard<std::mutex> l(g_plans_mu);
+    auto it = g_plans.find(h);
+    if (it == g_plans.end()) return fail(AMC_ERR_INVALID, "amc_plan_destroy: unknown plan");
+    p = it->second;
+    g_plans.erase(it);
+  }
+  delete p;
+  return AMC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,153 @@
+// Windowed FIR reduction: the polyphase filter-bank tree
+//   morph-reduce 'sum (morph* (transpose (reshape (im2col x (1 KW) (1 S)))) h) over taps
+// lowered to one kernel.  With hop S equal to the branch count M the window of
+// frame f+1 is the window of frame f shifted by one M-wide row, so
+//   out[b, f, m] = sum_{t<16} h[t, m] * x[b, (f + t) * M + m]
+// is a 16-tap FIR along the row axis of the (rows, M) matrix view of x.
+//
+// Each warp streams the rows of one chunk of frames once.  Row j contributes
+// tap t to frame j - t; the 16 frames in flight live in a register ring,
+// indexed statically by unrolling 16 rows at a time, and frame j - 15 is
+// complete (all taps added, in ascending t) after row j.  Arithmetic is
+// packed f32x2 (two branches per lane) with separate multiply and add
+// roundings: acc = fl(acc + fl(h * x)) from +0.0, which is bit-identical to
+// the reference's per-node materialisation (f32 product node, then f32
+// partial sums re-read from the typed output, realization.scm:1309-1388).
+#include "amc_internal.h"
+
+namespace amc {
+
+constexpr int kTaps = 16;
+constexpr int kChunk = 256;  // frames per warp (multiple of 16)
+
+__device__ __forceinline__ float2 ldg2(const float2* p) { return __ldg(p); }
+
+template <int PHASE>  // 0: rows 0..15 of the chunk; 1: interior; 2: rows chunk..chunk+14
+__device__ __forceinline__ void fir_rows16(float2 (&acc)[kTaps], const float2 (&h)[kTaps],
+                                           const float2* __restrict__ xrow, long long xs,
+                                           float2* __restrict__ orow, long long os, bool store_ok) {
+  float2 xv[16];
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    if (PHASE == 2 && jj == 15) continue;
+    xv[jj] = ldg2(xrow + jj * xs);
+  }
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    if (PHASE == 2 && jj == 15) continue;
+#pragma unroll
+    for (int t = 0; t < kTaps; ++t) {
+      const bool valid = PHASE == 0 ? (t <= jj) : PHASE == 2 ? (t > jj) : true;
+      if (valid) {
+        const int slot = (jj - t) & 15;
+        acc[slot] = __fadd2_rn(acc[slot], __fmul2_rn(h[t], xv[jj]));
+      }
+    }
+    const bool done = PHASE == 0 ? (jj == 15) : true;
+    if (done) {
+      const int slot = (jj + 1) & 15;
+      // frame (row - 15): orow points at the frame of row index 0 of this group minus 15
+      if (store_ok) __stcs(orow + jj * os, acc[slot]);
+      acc[slot] = make_float2(0.f, 0.f);
+    }
+  }
+}
+
+// One warp per (signal, chunk of kChunk frames); lane q owns branches 2q, 2q+1.
+__global__ void __launch_bounds__(256, 2) k_fir_chunks(const __grid_constant__ FirArgs a, long long chunks_per_sig) {
+  const int lane = threadIdx.x & 31;
+  const long long warp = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const long long items = a.batch * chunks_per_sig;
+  if (warp >= items) return;
+  const int pairs = a.branches >> 1;
+  const bool active = lane < pairs;
+  const int q = active ? lane : 0;
+  const long long b = warp / chunks_per_sig, c = warp % chunks_per_sig;
+  const long long f0 = c * kChunk;
+  const long long xs = a.hop >> 1, os = a.o_fstride >> 1;  // strides in float2 units
+  const float2* xbase = reinterpret_cast<const float2*>(a.x + b * a.x_bstride + f0 * a.hop) + q;
+  float2* obase = reinterpret_cast<float2*>(a.out + b * a.o_bstride + f0 * a.o_fstride) + q;
+  float2 h[kTaps], acc[kTaps];
+#pragma unroll
+  for (int t = 0; t < kTaps; ++t) {
+    h[t] = ldg2(reinterpret_cast<const float2*>(a.h + t * a.h_tstride) + q);
+    acc[t] = make_float2(0.f, 0.f);
+  }
+  // group 0: rows 0..15, completes frame 0 at row 15
+  fir_rows16<0>(acc, h, xbase, xs, obase - 15 * os, os, active);
+#pragma unroll 1
+  for (int g = 1; g < kChunk / 16; ++g)
+    fir_rows16<1>(acc, h, xbase + (long long)g * 16 * xs, xs, obase + ((long long)g * 16 - 15) * os, os, active);
+  fir_rows16<2>(acc, h, xbase + (long long)kChunk * xs, xs, obase + ((long long)kChunk - 15) * os, os, active);
+}
+
+// Frames past the last full chunk: one thread per (signal, frame, branch pair),
+// taps added in ascending order.
+__global__ void k_fir_tail(const __grid_constant__ FirArgs a, long long fstart) {
+  const int pairs = a.branches >> 1;
+  const long long nf = a.frames - fstart;
+  const long long total = a.batch * nf * pairs;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int q = (int)(i % pairs);
+  const long long f = fstart + (i / pairs) % nf, b = i / (pairs * nf);
+  const float2* xr = reinterpret_cast<const float2*>(a.x + b * a.x_bstride + f * a.hop) + q;
+  float2 acc = make_float2(0.f, 0.f);
+  for (int t = 0; t < a.taps; ++t) {
+    float2 hv = ldg2(reinterpret_cast<const float2*>(a.h + t * a.h_tstride) + q);
+    acc = __fadd2_rn(acc, __fmul2_rn(hv, ldg2(xr + (long long)t * (a.x_tstride >> 1))));
+  }
+  reinterpret_cast<float2*>(a.out + b * a.o_bstride + f * a.o_fstride)[q] = acc;
+}
+
+static bool aligned8(const void* p) { return ((uintptr_t)p & 7) == 0; }
+
+bool fir_supported(const FirArgs& a) {
+  return a.taps == kTaps && a.branches >= 2 && a.branches <= 64 && (a.branches % 2) == 0 && a.hop == a.x_tstride &&
+         (a.hop % 2) == 0 && (a.x_bstride % 2) == 0 && (a.h_tstride % 2) == 0 && (a.o_fstride % 2) == 0 &&
+         (a.o_bstride % 2) == 0 && aligned8(a.x) && aligned8(a.h) && aligned8(a.out) && a.hop >= a.branches;
+}
+
+int launch_fir(const FirArgs& a, cudaStream_t s) {
+  if (!fir_supported(a)) return fail(AMC_ERR_UNSUPPORTED, "window FIR: layout not supported by the streaming kernel");
+  if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "window FIR: injected launch failure (AMC_FAULT=launch)");
+  if (a.batch == 0 || a.frames == 0) return AMC_OK;
+  const long long chunks = a.frames / kChunk;
+  if (chunks > 0) {
+    const long long warps = a.batch * chunks;
+    const unsigned blocks = (unsigned)((warps + 7) / 8);
+    k_fir_chunks<<<blocks, 256, 0, s>>>(a, chunks);
+    AMC_CUDA(cudaGetLastError());
+  }
+  const long long fstart = chunks * kChunk;
+  if (fstart < a.frames) {
+    const long long total = a.batch * (a.frames - fstart) * (a.branches / 2);
+    k_fir_tail<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(a, fstart);
+    AMC_CUDA(cudaGetLastError());
+  }
+  return AMC_OK;
+}
+
+}  // namespace amc
+
+using namespace amc;
+
+extern "C" int amc_window_fir_f32(const float* x, int64_t batch, int64_t x_batch_stride, int64_t frames, int64_t hop,
+                                  int32_t taps, int32_t branches, const float* h, float* out, void* stream) {
+  if (!x || !h || !out || batch < 0 || frames < 0) return fail(AMC_ERR_INVALID, "amc_window_fir_f32: bad arguments");
+  FirArgs a;
+  a.x = x;
+  a.batch = batch;
+  a.x_bstride = x_batch_stride;
+  a.frames = frames;
+  a.hop = hop;
+  a.taps = taps;
+  a.branches = branches;
+  a.x_tstride = branches;
+  a.h = h;
+  a.h_tstride = branches;
+  a.out = out;
+  a.o_fstride = branches;
+  a.o_bstride = frames * branches;
+  return launch_fir(a, pick_stream(stream));
+}

@@ -1,0 +1,190 @@
+"""Parity of the device realize path (libamcuda through its C ABI) with the
+oracle and with the reference's known answers."""
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+from golden_dsl import build
+
+pytestmark = pytest.mark.gpu
+
+CASES = json.loads((Path(__file__).parent / "golden" / "known_answers.json").read_text())["cases"]
+
+
+@pytest.mark.parametrize("c", CASES, ids=[c["name"] for c in CASES])
+def test_device_known_answer(amc, c):
+    res = amc.realize(build(c["expr"]))
+    if c["shape"] is not None:
+        assert list(res.shape) == c["shape"]
+    if c["dtype"] is not None:
+        assert res.dtype == c["dtype"]
+    if c["values"] is not None:
+        got = np.asarray(res.values(), dtype=np.float64).reshape(-1)
+        exp = np.asarray(c["values"], dtype=np.float64).reshape(-1)
+        np.testing.assert_allclose(got, exp, rtol=0, atol=c["tol"] if c["tol"] else 0)
+    # and bit-for-bit (or within the case tolerance) equal to the oracle
+    ref = oracle.realize(build(c["expr"]))
+    np.testing.assert_allclose(np.asarray(res.values(), np.float64), np.asarray(ref.values(), np.float64),
+                               rtol=c["tol"] if c["tol"] else 0, atol=0)
+
+
+def _same(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    assert a.shape == b.shape and a.dtype == b.dtype
+    assert np.array_equal(a.view(np.uint8), b.view(np.uint8)), np.max(np.abs(a.astype(np.float64) - b))
+
+
+@pytest.mark.parametrize("dtype", ["f64", "s32"])
+def test_c1_fused_view_map_reduce_bit_exact(amc, dtype):
+    """Config 1 at full size: sum_j x[2048j+i]^2 + y[2048j+i] (1024 outputs)."""
+    from amcuda import workloads as W
+    xm, ym = W.c1_inputs_morph(dtype)
+    tree = W.c1_tree(xm, ym)
+    dev = amc.realize(tree).values()
+    ref = oracle.realize(W.c1_tree(xm, ym)).values()
+    _same(dev, ref)
+    assert dev.shape == (1024,)
+
+
+def test_c1_plan_is_one_fused_launch(amc):
+    from amcuda import workloads as W
+    xm, ym = W.c1_inputs_morph("f64")
+    p = amc.Plan(W.c1_tree(xm, ym))
+    st = p.stats()
+    assert st["launches"] == 1 and st["buffers"] == 1
+
+
+@pytest.mark.parametrize("batch,length", [(2, 1 << 14), (3, 4096 + 64 * 37)])
+def test_c2_filter_bank_bit_exact_small(amc, batch, length):
+    from amcuda import workloads as W
+    x = np.stack([W.c2_signal(s, length) for s in range(batch)])
+    h = W.c2_prototype()
+    xm, hm = amc.morph_from_numpy(x), amc.morph_from_numpy(h)
+    tree = W.c2_tree(xm, hm)
+    p = amc.Plan(tree)
+    p.execute()
+    dev = p.result().values()
+    ref = oracle.realize(W.c2_tree(xm, hm)).values()
+    _same(dev, ref)
+    assert dev.shape == (batch, W.c2_frames(length), 64)
+
+
+def test_c2_streaming_kernel_matches_generic_reduction(amc):
+    """The FIR kernel against the generic ordered reduction of the same tree
+    (forced by an identity map that hides the pattern): bitwise equal."""
+    from amcuda import workloads as W
+    L = 1 << 17
+    x = np.stack([W.c2_signal(s, L) for s in range(2)])
+    h = W.c2_prototype()
+    xm, hm = amc.morph_from_numpy(x), amc.morph_from_numpy(h)
+    fast = W.c2_tree(xm, hm)
+    prod = fast.operands[0]
+    slow = amc.morph_reduce("sum", amc.morph_map(lambda v: v * 1.0, prod), (2,))
+    pf, ps = amc.Plan(fast), amc.Plan(slow)
+    pf.execute(), ps.execute()
+    _same(pf.result().values(), ps.result().values())
+
+
+def _rand(rng, shape, dtype):
+    if dtype in ("f32", "f64"):
+        return rng.standard_normal(shape).astype(np.float32 if dtype == "f32" else np.float64)
+    return rng.integers(-50, 50, size=shape).astype(np.int32 if dtype == "s32" else np.int64)
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f64", "s32", "s64"])
+def test_fused_chains_match_oracle_bitwise(amc, dtype):
+    rng = np.random.default_rng(3)
+    a = amc.morph_from_numpy(_rand(rng, (37, 19), dtype))
+    b = amc.morph_from_numpy(_rand(rng, (19,), dtype))
+    c = amc.morph_from_numpy(_rand(rng, (37, 1), dtype))
+    exprs = [
+        amc.morph_add(amc.morph_mul(a, b), c),
+        amc.morph_sub(amc.morph_transpose(amc.morph_mul(a, a)), amc.morph_transpose(a)),
+        amc.morph_reduce("sum", amc.morph_mul(amc.morph_add(a, b), c), (0,)),
+        amc.morph_reduce("sum", amc.morph_slice(amc.morph_add(a, c), (1, 2), (37, 19), (3, 2)), (1,), True),
+        amc.morph_reduce("prod", amc.morph_slice(a, (0, 0), (37, 19), (9, 5)), (0, 1)),
+        amc.morph_reduce("mean", amc.morph_abs(a), (1,)),
+        amc.morph_map(lambda v: v * v - 3 * v + 1, amc.morph_transpose(a)),
+        amc.morph_gt(a, b),
+        amc.morph_reshape(amc.morph_transpose(a), (19 * 37,)),
+        amc.morph_reduce("sum", amc.morph_pad(a, [(1, 2), (3, 0)], "reflect"), (0,)),
+    ]
+    if dtype in ("f32", "f64"):
+        exprs.append(amc.morph_reduce("max", amc.morph_div(a, amc.morph_add(amc.morph_abs(c), c)), (0,)))
+        exprs.append(amc.morph_reduce("min", a, (0, 1), True))
+    for e in exprs:
+        _same(amc.realize(e).values(), oracle.realize(e).values())
+
+
+def test_transcendentals_within_f64_tolerance(amc):
+    rng = np.random.default_rng(5)
+    a = amc.morph_from_numpy(rng.uniform(0.1, 3.0, (64, 33)))
+    for f in (amc.morph_sqrt, amc.morph_exp, amc.morph_log, amc.morph_sin, amc.morph_cos, amc.morph_tan,
+              amc.morph_sigmoid, amc.morph_tanh, amc.morph_relu):
+        e = amc.morph_reduce("sum", f(a), (1,))
+        np.testing.assert_allclose(amc.realize(e).values(), oracle.realize(e).values(), rtol=1e-12, atol=0)
+
+
+def test_integer_max_reduction_is_rejected(amc):
+    a = amc.morph_from_numpy(np.arange(6, dtype=np.int32))
+    with pytest.raises(amc.AmcError):
+        amc.realize(amc.morph_reduce("max", a))
+
+
+def test_long_reduction_tree_path(amc):
+    rng = np.random.default_rng(9)
+    x = rng.standard_normal(1 << 21)
+    e = amc.morph_reduce("sum", amc.morph_map(lambda v: v * v, amc.morph_from_numpy(x)))
+    got = float(amc.realize(e).values())
+    ref = float(oracle.realize(e).values())
+    assert abs(got - ref) <= 1e-12 * abs(ref)
+
+
+def test_structural_gathers_match_oracle(amc):
+    rng = np.random.default_rng(11)
+    img = amc.morph_from_numpy(rng.standard_normal((2, 3, 7, 6)))
+    for e in [
+        amc.im2col_morph(img, (3, 2), (2, 1), (1, 2)),
+        amc.col2im_morph(amc.im2col_morph(img, (3, 3), 1, 1), (2, 3, 7, 6), (3, 3), 1, 1),
+        amc.morph_pad(amc.morph_transpose(img, (0, 2, 1, 3)), [(0, 0), (2, 1), (1, 1), (0, 3)], "edge"),
+        amc.morph_pad(img, [(0, 0), (1, 0), (0, 2), (3, 3)], "constant", -7.5),
+        amc.morph_stack([amc.morph_slice(img, (0, 0, 0, 0), (2, 3, 7, 6), (1, 1, 2, 3)),
+                         amc.morph_slice(img, (0, 0, 1, 1), (2, 3, 7, 6), (1, 1, 2, 3))], 2),
+        amc.morph_concat([img, amc.morph_mul(img, img)], 3),
+    ]:
+        _same(amc.realize(e).values(), oracle.realize(e).values())
+
+
+def test_matmul_family_matches_oracle_bitwise(amc):
+    rng = np.random.default_rng(13)
+    for dt in ("f64", "f32"):
+        A = amc.morph_from_numpy(_rand(rng, (70, 45), dt))
+        B = amc.morph_from_numpy(_rand(rng, (45, 66), dt))
+        v = amc.morph_from_numpy(_rand(rng, (45,), dt))
+        for e in [amc.morph_matmul(A, B), amc.morph_matmul(amc.morph_transpose(B), amc.morph_transpose(A)),
+                  amc.morph_matvec(A, v), amc.morph_dot(v, v)]:
+            _same(amc.realize(e).values(), oracle.realize(e).values())
+
+
+def test_attention_node_matches_oracle(amc):
+    rng = np.random.default_rng(17)
+    for dt, tol in (("f64", 1e-12), ("f32", 1e-5)):
+        q = amc.morph_from_numpy(_rand(rng, (2, 3, 40, 8), dt))
+        k = amc.morph_from_numpy(_rand(rng, (2, 3, 40, 8), dt))
+        v = amc.morph_from_numpy(_rand(rng, (2, 3, 40, 5), dt))
+        e = amc.attention_morphism(q, k, v)
+        got, ref = amc.realize(e).values(), oracle.realize(e).values()
+        assert np.max(np.abs(got.astype(np.float64) - ref)) <= tol * np.max(np.abs(ref))
+
+
+def test_plan_rejects_bad_trees(amc):
+    a = amc.morph_from_numpy(np.zeros((4, 4)))
+    with pytest.raises(ValueError):
+        amc.morph_slice(a, (0, 0), (5, 4))
+    bad = amc.morph_reshape(a, (16,))
+    bad.shape = (17,)  # corrupt the node: the planner must refuse it
+    with pytest.raises(amc.AmcError):
+        amc.realize(bad)
