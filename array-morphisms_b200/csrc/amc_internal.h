@@ -175,5 +175,6 @@ struct FirArgs {
 };
 bool fir_supported(const FirArgs& a);
 int launch_fir(const FirArgs& a, cudaStream_t s);
+int fir_launches(const FirArgs& a);
 
 }  // namespace amc

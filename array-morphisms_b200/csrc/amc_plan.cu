@@ -630,7 +630,7 @@ struct Builder {
     f.o_bstride = f.frames * f.branches;
     if (!fir_supported(f)) return false;
     plan->steps.push_back([f](cudaStream_t s) { return launch_fir(f, s); });
-    plan->launches += 1;
+    plan->launches += fir_launches(f);
     plan->used_fir = true;
     return true;
   }

@@ -123,8 +123,10 @@ cudaStream_t default_stream() {
   std::lock_guard<std::mutex> l(g_dev_mu);
   auto it = g_streams.find(dev);
   if (it != g_streams.end()) return it->second;
+  // A blocking stream: it orders with the legacy default stream, so work a
+  // host enqueued there (uploads, other libraries) completes first.
   cudaStream_t s = nullptr;
-  cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  cudaStreamCreateWithFlags(&s, cudaStreamDefault);
   g_streams[dev] = s;
   return s;
 }

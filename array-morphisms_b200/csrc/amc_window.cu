@@ -8,9 +8,9 @@
 // Each warp streams the rows of one chunk of frames once.  Row j contributes
 // tap t to frame j - t; the 16 frames in flight live in a register ring,
 // indexed statically by unrolling 16 rows at a time, and frame j - 15 is
-// complete (all taps added, in ascending t) after row j.  Arithmetic is
-// packed f32x2 (two branches per lane) with separate multiply and add
-// roundings: acc = fl(acc + fl(h * x)) from +0.0, which is bit-identical to
+// complete (all taps added, in ascending t) after row j.  Each lane owns two
+// branches (8-byte loads and stores); arithmetic keeps separate multiply and
+// add roundings: acc = fl(acc + fl(h * x)) from +0.0, which is bit-identical to
 // the reference's per-node materialisation (f32 product node, then f32
 // partial sums re-read from the typed output, realization.scm:1309-1388).
 #include "amc_internal.h"
@@ -21,6 +21,14 @@ constexpr int kTaps = 16;
 constexpr int kChunk = 256;  // frames per warp (multiple of 16)
 
 __device__ __forceinline__ float2 ldg2(const float2* p) { return __ldg(p); }
+
+// One tap of two branches: acc = fl(acc + fl(h * x)) per component.  Scalar
+// mul.rn / add.rn are never contracted; the packed f32x2 forms (intrinsics or
+// explicit .rn PTX) were measured to come out fused on this toolchain, which
+// changes the rounding, so they are not used here.
+__device__ __forceinline__ float2 tap2(float2 acc, float2 h, float2 x) {
+  return make_float2(__fadd_rn(acc.x, __fmul_rn(h.x, x.x)), __fadd_rn(acc.y, __fmul_rn(h.y, x.y)));
+}
 
 template <int PHASE>  // 0: rows 0..15 of the chunk; 1: interior; 2: rows chunk..chunk+14
 __device__ __forceinline__ void fir_rows16(float2 (&acc)[kTaps], const float2 (&h)[kTaps],
@@ -40,7 +48,7 @@ __device__ __forceinline__ void fir_rows16(float2 (&acc)[kTaps], const float2 (&
       const bool valid = PHASE == 0 ? (t <= jj) : PHASE == 2 ? (t > jj) : true;
       if (valid) {
         const int slot = (jj - t) & 15;
-        acc[slot] = __fadd2_rn(acc[slot], __fmul2_rn(h[t], xv[jj]));
+        acc[slot] = tap2(acc[slot], h[t], xv[jj]);
       }
     }
     const bool done = PHASE == 0 ? (jj == 15) : true;
@@ -95,7 +103,7 @@ __global__ void k_fir_tail(const __grid_constant__ FirArgs a, long long fstart) 
   float2 acc = make_float2(0.f, 0.f);
   for (int t = 0; t < a.taps; ++t) {
     float2 hv = ldg2(reinterpret_cast<const float2*>(a.h + t * a.h_tstride) + q);
-    acc = __fadd2_rn(acc, __fmul2_rn(hv, ldg2(xr + (long long)t * (a.x_tstride >> 1))));
+    acc = tap2(acc, hv, ldg2(xr + (long long)t * (a.x_tstride >> 1)));
   }
   reinterpret_cast<float2*>(a.out + b * a.o_bstride + f * a.o_fstride)[q] = acc;
 }
@@ -106,6 +114,11 @@ bool fir_supported(const FirArgs& a) {
   return a.taps == kTaps && a.branches >= 2 && a.branches <= 64 && (a.branches % 2) == 0 && a.hop == a.x_tstride &&
          (a.hop % 2) == 0 && (a.x_bstride % 2) == 0 && (a.h_tstride % 2) == 0 && (a.o_fstride % 2) == 0 &&
          (a.o_bstride % 2) == 0 && aligned8(a.x) && aligned8(a.h) && aligned8(a.out) && a.hop >= a.branches;
+}
+
+int fir_launches(const FirArgs& a) {
+  if (a.batch == 0 || a.frames == 0) return 0;
+  return (a.frames / kChunk > 0 ? 1 : 0) + (a.frames % kChunk ? 1 : 0);
 }
 
 int launch_fir(const FirArgs& a, cudaStream_t s) {

@@ -227,7 +227,9 @@ def bench_filterbank(args, ws, rank, local):
     hm = am.Concrete(None, (W.PROTO,), dtype="f32", dev=hb)
     plan = am.Plan(W.c2_tree(xm, hm))
     st = plan.stats()
-    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()  # an explicit stream: events and launches share it
+    torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     for _ in range(args.warmup):
         plan.execute(sptr)
@@ -351,7 +353,8 @@ def bench_other(args, ws, rank, local):
     from amcuda import workloads as W
     am.init(local)
     torch.cuda.set_device(local)
-    stream = torch.cuda.current_stream()
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
     hbm, bf16, kind = peaks()
     wl = args.workload
