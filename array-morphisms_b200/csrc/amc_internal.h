@@ -176,5 +176,6 @@ struct FirArgs {
 bool fir_supported(const FirArgs& a);
 int launch_fir(const FirArgs& a, cudaStream_t s);
 int fir_launches(const FirArgs& a);
+int fir_check_error();   // reads and clears the device-side wait-timeout flag
 
 }  // namespace amc

@@ -207,7 +207,7 @@ int amc_shutdown(void) {
 
 int amc_synchronize(void) {
   AMC_CUDA(cudaStreamSynchronize(default_stream()));
-  return AMC_OK;
+  return fir_check_error();
 }
 
 int amc_buf_create(int32_t dtype, int64_t nelem, uint64_t* out) {
@@ -254,7 +254,7 @@ int amc_buf_download(uint64_t h, void* host, int64_t bytes, int64_t off) {
   cudaStream_t s = default_stream();
   AMC_CUDA(cudaMemcpyAsync(host, (char*)b->ptr + off, (size_t)bytes, cudaMemcpyDeviceToHost, s));
   AMC_CUDA(cudaStreamSynchronize(s));
-  return AMC_OK;
+  return fir_check_error();
 }
 
 int amc_buf_upload_async(uint64_t h, const void* host, int64_t bytes, int64_t off, void* stream) {

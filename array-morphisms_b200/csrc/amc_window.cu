@@ -61,6 +61,132 @@ __device__ __forceinline__ void fir_rows16(float2 (&acc)[kTaps], const float2 (&
   }
 }
 
+// ------------------------------------------------------------------ TMA-staged variant
+// Rows are contiguous when hop == branches, so the rows of a chunk form one
+// contiguous span of global memory.  Each warp keeps a ring of kStages tiles
+// of 16 rows in shared memory; lane 0 fills them with 1-D bulk async copies
+// (cp.async.bulk, completion counted on an mbarrier per stage, no multicast)
+// kStages groups ahead of the arithmetic, so the memory pipeline never waits
+// for registers.  Every mbarrier wait is bounded: on expiry the kernel records
+// an error code, drains its own copies (also bounded) and returns.
+constexpr int kStages = 4;
+constexpr int kWarpsPerCta = 4;
+constexpr int kWaitLimit = 1 << 20;
+
+static __device__ int g_fir_error;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t phase) {
+  for (int i = 0; i < kWaitLimit; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(phase) : "memory");
+    if (ok) return true;
+  }
+  return false;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
+}
+
+template <int PHASE>
+__device__ __forceinline__ void fir_rows16_smem(float2 (&acc)[kTaps], const float2 (&h)[kTaps],
+                                                const float2* __restrict__ srow, int rs,
+                                                float2* __restrict__ orow, long long os, bool store_ok) {
+  float2 xv[16];
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    if (PHASE == 2 && jj == 15) continue;
+    xv[jj] = srow[jj * rs];
+  }
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    if (PHASE == 2 && jj == 15) continue;
+#pragma unroll
+    for (int t = 0; t < kTaps; ++t) {
+      const bool valid = PHASE == 0 ? (t <= jj) : PHASE == 2 ? (t > jj) : true;
+      if (valid) {
+        const int slot = (jj - t) & 15;
+        acc[slot] = tap2(acc[slot], h[t], xv[jj]);
+      }
+    }
+    const bool done = PHASE == 0 ? (jj == 15) : true;
+    if (done) {
+      const int slot = (jj + 1) & 15;
+      if (store_ok) __stcs(orow + jj * os, acc[slot]);
+      acc[slot] = make_float2(0.f, 0.f);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kWarpsPerCta * 32) k_fir_tma(const __grid_constant__ FirArgs a, long long chunks_per_sig) {
+  extern __shared__ __align__(128) unsigned char fir_sm[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const long long warp = (long long)blockIdx.x * kWarpsPerCta + w;
+  const long long items = a.batch * chunks_per_sig;
+  if (warp >= items) return;
+  const int RB = a.branches * 4;          // bytes per row
+  const int SB = 16 * RB;                 // bytes per stage
+  const int rs = a.branches >> 1;         // row stride in float2
+  unsigned char* ring = fir_sm + (size_t)w * kStages * SB;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fir_sm + (size_t)kWarpsPerCta * kStages * SB) + w * kStages;
+  const int pairs = a.branches >> 1;
+  const bool active = lane < pairs;
+  const int q = active ? lane : 0;
+  const long long b = warp / chunks_per_sig, c = warp % chunks_per_sig;
+  const long long f0 = c * kChunk;
+  const char* src = reinterpret_cast<const char*>(a.x + b * a.x_bstride + f0 * a.hop);
+  constexpr int kRows = kChunk + kTaps - 1;
+  constexpr int kGroups = (kRows + 15) / 16;
+  if (lane == 0) {
+    for (int s = 0; s < kStages; ++s)
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bars[s])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int g = 0; g < kStages && g < kGroups; ++g) {
+      const int rows = (g == kGroups - 1) ? kRows - 16 * g : 16;
+      bulk_load(smem_u32(ring + (size_t)g * SB), src + (size_t)g * 16 * RB, (uint32_t)(rows * RB), smem_u32(&bars[g]));
+    }
+  }
+  __syncwarp();
+  const long long os = a.o_fstride >> 1;
+  float2* obase = reinterpret_cast<float2*>(a.out + b * a.o_bstride + f0 * a.o_fstride) + q;
+  float2 h[kTaps], acc[kTaps];
+#pragma unroll
+  for (int t = 0; t < kTaps; ++t) {
+    h[t] = ldg2(reinterpret_cast<const float2*>(a.h + t * a.h_tstride) + q);
+    acc[t] = make_float2(0.f, 0.f);
+  }
+#pragma unroll 1
+  for (int g = 0; g < kGroups; ++g) {
+    const int s = g % kStages;
+    const uint32_t phase = (uint32_t)(g / kStages) & 1u;
+    if (!mbar_wait(smem_u32(&bars[s]), phase)) {
+      if (lane == 0) atomicExch(&g_fir_error, AMC_ERR_TIMEOUT);
+      // drain this warp's other copies in flight (bounded), then leave
+      for (int k = g + 1; k < g + kStages && k < kGroups; ++k)
+        mbar_wait(smem_u32(&bars[k % kStages]), (uint32_t)(k / kStages) & 1u);
+      return;
+    }
+    const float2* srow = reinterpret_cast<const float2*>(ring + (size_t)s * SB) + q;
+    float2* orow = obase + ((long long)g * 16 - 15) * os;
+    if (g == 0) fir_rows16_smem<0>(acc, h, srow, rs, orow, os, active);
+    else if (g < kGroups - 1) fir_rows16_smem<1>(acc, h, srow, rs, orow, os, active);
+    else fir_rows16_smem<2>(acc, h, srow, rs, orow, os, active);
+    __syncwarp();
+    if (lane == 0 && g + kStages < kGroups) {
+      const int gn = g + kStages;
+      const int rows = (gn == kGroups - 1) ? kRows - 16 * gn : 16;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bulk_load(smem_u32(ring + (size_t)s * SB), src + (size_t)gn * 16 * RB, (uint32_t)(rows * RB), smem_u32(&bars[s]));
+    }
+  }
+}
+
 // One warp per (signal, chunk of kChunk frames); lane q owns branches 2q, 2q+1.
 __global__ void __launch_bounds__(256, 2) k_fir_chunks(const __grid_constant__ FirArgs a, long long chunks_per_sig) {
   const int lane = threadIdx.x & 31;
@@ -121,6 +247,25 @@ int fir_launches(const FirArgs& a) {
   return (a.frames / kChunk > 0 ? 1 : 0) + (a.frames % kChunk ? 1 : 0);
 }
 
+// The bulk-copy kernel needs contiguous rows (hop == branches), rows of a
+// multiple of 16 bytes and 16-byte aligned chunk starts.
+static bool fir_tma_ok(const FirArgs& a) {
+  const uintptr_t x = (uintptr_t)a.x;
+  return a.hop == a.branches && (a.branches * 4) % 16 == 0 && (x % 16) == 0 && ((a.x_bstride * 4) % 16) == 0 &&
+         ((kChunk * a.hop * 4) % 16) == 0;
+}
+
+int fir_check_error() {
+  int e = 0;
+  AMC_CUDA(cudaMemcpyFromSymbol(&e, g_fir_error, sizeof(int)));
+  if (e) {
+    int z = 0;
+    AMC_CUDA(cudaMemcpyToSymbol(g_fir_error, &z, sizeof(int)));
+    return fail(e, "window FIR: a bounded wait for a staged tile gave up");
+  }
+  return AMC_OK;
+}
+
 int launch_fir(const FirArgs& a, cudaStream_t s) {
   if (!fir_supported(a)) return fail(AMC_ERR_UNSUPPORTED, "window FIR: layout not supported by the streaming kernel");
   if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "window FIR: injected launch failure (AMC_FAULT=launch)");
@@ -128,8 +273,19 @@ int launch_fir(const FirArgs& a, cudaStream_t s) {
   const long long chunks = a.frames / kChunk;
   if (chunks > 0) {
     const long long warps = a.batch * chunks;
-    const unsigned blocks = (unsigned)((warps + 7) / 8);
-    k_fir_chunks<<<blocks, 256, 0, s>>>(a, chunks);
+    if (fir_tma_ok(a)) {
+      const size_t sm = (size_t)kWarpsPerCta * kStages * 16 * a.branches * 4 + (size_t)kWarpsPerCta * kStages * 8;
+      static bool attr_set = false;
+      if (!attr_set) {
+        AMC_CUDA(cudaFuncSetAttribute(k_fir_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        attr_set = true;
+      }
+      const unsigned blocks = (unsigned)((warps + kWarpsPerCta - 1) / kWarpsPerCta);
+      k_fir_tma<<<blocks, kWarpsPerCta * 32, sm, s>>>(a, chunks);
+    } else {
+      const unsigned blocks = (unsigned)((warps + 7) / 8);
+      k_fir_chunks<<<blocks, 256, 0, s>>>(a, chunks);
+    }
     AMC_CUDA(cudaGetLastError());
   }
   const long long fstart = chunks * kChunk;
