@@ -1,0 +1,79 @@
+"""Batch-axis sharding across the GPUs of one node (one process per GPU).
+
+The reference has one notion of parallelism, the batch axis of a morphism
+(core.scm:247-269, batch-ops.scm:217-239).  Here batched work is partitioned
+across ranks:
+  - independent items (filter-bank signals, attention batch entries, conv
+    images for Y and dX) need no exchange;
+  - a reduction that crosses the batch axis (the linear-regression gradient,
+    the conv weight gradient) is combined with a deterministic all-reduce:
+    an all-gather of each rank's partial followed by a sum in rank order, so
+    results do not depend on the collective's internal reduction order.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+
+def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Contiguous [start, stop) of n items for `rank` of `world` (sizes differ by at most 1)."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad world/rank")
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def allreduce_fixed_order(t, group=None):
+    """In-place sum of `t` over ranks, added in rank order 0..world-1."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    if world == 1:
+        return t
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    acc = parts[0].clone()
+    for p in parts[1:]:
+        acc += p
+    t.copy_(acc)
+    return t
+
+
+class ShardedLinearRegression:
+    """Gradient descent on rows sharded across ranks.
+
+    Each step: every rank forms the (d+1) row of gradient sums and squared
+    residual sum over its rows (partials_fn), the rows are all-reduced in rank
+    order, and every rank applies the same update, so w stays replicated.
+    partials_fn(X, y, w, n_total, out) fills `out` (d+1); update_fn(w, gl,
+    n_total, lr, loss) applies w -= lr * gl[:d] and writes gl[d] / n_total to
+    loss.  The defaults run the device kernels of libamcuda."""
+
+    def __init__(self, X, y, n_total: int, lr: float, partials_fn: Callable | None = None,
+                 update_fn: Callable | None = None, group=None):
+        import torch
+        self.X, self.y, self.n_total, self.lr, self.group = X, y, n_total, lr, group
+        d = X.shape[1]
+        self.w = torch.zeros(d, dtype=torch.float64, device=X.device)
+        self.gl = torch.empty(d + 1, dtype=torch.float64, device=X.device)
+        self.loss = torch.empty(1, dtype=torch.float64, device=X.device)
+        if partials_fn is None:
+            from . import workloads as W
+            npart = W.linreg_partials_count(X.shape[0], d)
+            part = torch.empty(npart * (d + 1), dtype=torch.float64, device=X.device)
+
+            def partials_fn(X, y, w, n_total, out):
+                W.linreg_partials(X, y, w, part, n_total)
+                W.linreg_reduce(part, npart, d, out)
+        if update_fn is None:
+            from . import workloads as W
+
+            def update_fn(w, gl, n_total, lr, loss):
+                W.linreg_update(w, gl, n_total, lr, loss)
+        self.partials_fn, self.update_fn = partials_fn, update_fn
+
+    def step(self) -> None:
+        self.partials_fn(self.X, self.y, self.w, self.n_total, self.gl)
+        allreduce_fixed_order(self.gl, self.group)
+        self.update_fn(self.w, self.gl, self.n_total, self.lr, self.loss)
