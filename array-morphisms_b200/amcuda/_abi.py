@@ -104,6 +104,7 @@ SIGNATURES = {
     "amc_linreg_reduce": [_P, _I32, _I32, _P, _P],
     "amc_linreg_update": [_P, _P, _I32, _I64, _D, _P, _P],
     "amc_linreg_step": [_P, _P, _P, _I64, _I32, _D, _P, _P, _P, _P],
+    "amc_linreg_step_noalloc": [_P, _P, _P, _I64, _I32, _D, _P, _P],
     "amc_attention_fwd_f32": [_P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _F, _P],
     "amc_attention_bwd_f32": [_P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I32, _I32, _I32, _F, _P],
     "amc_conv2d_fwd_f32": [_P, _P, _P] + [_I32] * 11 + [_P],

@@ -292,6 +292,24 @@ int amc_linreg_update(double* w, const double* grad_loss_sum, int32_t d, int64_t
 int amc_linreg_step(const double* X, const double* y, double* w, int64_t rows, int32_t d, double lr,
                     double* partials, double* grad_loss, double* loss_out, void* stream);
 
+/* Linear-regression step that allocates nothing.  No counterpart in the
+ * reference: it exists for callers that cannot allocate device memory —
+ * hosts whose device memory belongs to another allocator (a framework's
+ * caching allocator, a fixed per-process budget) or that must not call
+ * cudaMalloc, which can synchronise the device, inside a timed loop.
+ * Same arithmetic as amc_linreg_step, but the partial sums live in a static
+ * device array of 262144 doubles (2 MiB, held by every GPU that loads the
+ * library until exit); calls needing more, (partials + 1) * (d + 1) doubles
+ * with partials = amc_linreg_partials_count(rows, d), are rejected with
+ * AMC_ERR_INVALID.  The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  Every call shares the one array and every
+ * scratch entry is written before it is read; calls that overlap on the GPU
+ * (different streams, or different host threads on one device) race.
+ * Pass a stream, or call amc_init first, so no library stream is created here. */
+int amc_linreg_step_noalloc(const double* X, const double* y, double* w, int64_t rows, int32_t d, double lr,
+                            double* loss_out, void* stream);
+
 /* Scaled dot-product attention, streaming softmax (realization.scm:279-396):
  * Q (B, n, dk), K (B, n, dk), V (B, n, dv) row-major contiguous per block. */
 int amc_attention_fwd_f32(const float* Q, const float* K, const float* V, float* O, float* lse,
