@@ -1,0 +1,499 @@
+// Tensor-core attention forward (sm_100a, tcgen05 kind::tf32).
+//
+// One CTA computes 128 query rows of one (batch, head) block, one thread per
+// row.  For each 128-key tile:
+//   S  = Q K^T      tcgen05.mma M=128 N=128 K=64, operands K-major in shared
+//                   memory (TMA, 128-byte swizzle), accumulator in TMEM
+//   P  = exp(scale*S - m) with the running row max m and sum l (online
+//        softmax of the reference's 3-pass %attn-2d!, realization.scm:279-326)
+//   O_t = P V       tcgen05.mma M=128 N=64 K=128; P is written by the threads
+//                   into shared memory in the K-major swizzled layout, V comes
+//                   pre-transposed (V^T, keys contiguous) so it is K-major too
+//   O  = O * exp(m_old - m) + O_t   in registers
+// K and V^T tiles are double-buffered: the TMA for tile j+2 is issued as soon
+// as the P V product of tile j has consumed its buffer.  Every mbarrier wait is
+// bounded; on expiry the CTA records AMC_ERR_TIMEOUT and leaves after its MMAs
+// and copies have drained.
+#include <cmath>
+
+#include "amc_internal.h"
+#include "amc_tc.cuh"
+
+namespace amc {
+
+using namespace tc;
+
+namespace {
+
+constexpr int kBM = 128;   // query rows per CTA
+constexpr int kBN = 128;   // keys per tile
+constexpr int kD = 64;     // head dim
+
+// shared memory map (bytes, from a 1024-aligned base)
+constexpr int kQOff = 0;                         // 2 x 16 KB   (dims 0-31, 32-63)
+constexpr int kKOff = kQOff + 2 * 16384;         // 2 bufs x 2 x 16 KB
+constexpr int kVOff = kKOff + 2 * 2 * 16384;     // 2 bufs x 4 x 8 KB (keys 0-31 .. 96-127), 64 dim rows each
+constexpr int kPOff = kVOff + 2 * 4 * 8192;      // 4 x 16 KB   (keys 0-31 .. 96-127)
+constexpr int kBarOff = kPOff + 4 * 16384;
+constexpr int kSmemBytes = kBarOff + 128 + 1024; // barriers, tmem slot, alignment slack
+
+__device__ int g_attn_error;
+
+__device__ __forceinline__ void fail_timeout() { atomicExch(&g_attn_error, AMC_ERR_TIMEOUT); }
+
+}  // namespace
+
+__global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ CUtensorMap mQ,
+                                                       const __grid_constant__ CUtensorMap mK,
+                                                       const __grid_constant__ CUtensorMap mVt, float* __restrict__ O,
+                                                       float* __restrict__ lse, int n, float scale_log2) {
+  extern __shared__ unsigned char attn_sm_raw[];
+  unsigned char* sm = (unsigned char*)(((uintptr_t)attn_sm_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bar_q = (uint64_t*)(sm + kBarOff);
+  uint64_t* bar_kv = bar_q + 1;   // [2]
+  uint64_t* bar_s = bar_q + 3;
+  uint64_t* bar_o = bar_q + 4;
+  uint32_t* tslot = (uint32_t*)(sm + kBarOff + 64);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int qtile = blockIdx.x, bh = blockIdx.y;
+  const int row0 = bh * n + qtile * kBM;   // row in the (B*H*n, 64) view of Q / O
+  const int ntiles = n / kBN;
+  if (tid == 0) {
+    mbar_init(bar_q, 1);
+    mbar_init(&bar_kv[0], 1);
+    mbar_init(&bar_kv[1], 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 0) tmem_alloc(tslot, 256);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+
+  auto load_kv = [&](int j, int b) {
+    mbar_expect_tx(&bar_kv[b], 2 * 16384 + 4 * 8192);
+    for (int r = 0; r < 2; ++r) tma_load_2d(sm + kKOff + b * 32768 + r * 16384, &mK, 32 * r, bh * n + j * kBN, &bar_kv[b]);
+    for (int r = 0; r < 4; ++r) tma_load_2d(sm + kVOff + b * 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &bar_kv[b]);
+  };
+  if (tid == 0) {
+    mbar_expect_tx(bar_q, 2 * 16384);
+    for (int r = 0; r < 2; ++r) tma_load_2d(sm + kQOff + r * 16384, &mQ, 32 * r, row0, bar_q);
+    load_kv(0, 0);
+    if (ntiles > 1) load_kv(1, 1);
+  }
+  bool ok = __syncthreads_and(mbar_wait(bar_q, 0));
+
+  const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
+  const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
+  float m = -INFINITY, l = 0.f;
+  float o[kD];
+#pragma unroll
+  for (int i = 0; i < kD; ++i) o[i] = 0.f;
+  // P row of this thread in the swizzled K-major layout: region r (keys 32r..32r+31),
+  // row `tid` at 128 B, 16-byte chunk c stored at chunk c ^ (tid & 7).
+  unsigned char* prow = sm + kPOff + tid * 128;
+
+  for (int j = 0; j < ntiles && ok; ++j) {
+    const int b = j & 1;
+    ok = __syncthreads_and(mbar_wait(&bar_kv[b], (uint32_t)(j >> 1) & 1u));
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int k = 0; k < kD / 8; ++k) {
+        const uint64_t ad = sdesc(smem_addr(sm + kQOff + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
+        const uint64_t bd = sdesc(smem_addr(sm + kKOff + b * 32768 + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
+        mma_tf32(t_s, ad, bd, id_s, k > 0);
+      }
+      mma_commit(bar_s);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_s, (uint32_t)j & 1u));
+    if (!ok) break;
+    tc_fence_after();
+    // ---- online softmax on this thread's row, 32 columns at a time:
+    // pass 1 finds the new row max, pass 2 forms P = exp2(s*scale*log2e - max),
+    // its row sum, and writes P into the swizzled K-major tile.
+    float mx = m;
+#pragma unroll
+    for (int c = 0; c < kBN; c += 32) {
+      float v[32];
+      tmem_ld32(t_s + lane_base + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) mx = fmaxf(mx, v[i] * scale_log2);
+    }
+    const float corr = exp2f(m - mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int c = 0; c < kBN; c += 32) {
+      float v[32];
+      tmem_ld32(t_s + lane_base + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        v[i] = exp2f(fmaf(v[i], scale_log2, -mx));
+        sum += v[i];
+      }
+      unsigned char* region = prow + (c >> 5) * 16384;
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(region + ((q ^ (tid & 7)) << 4)) =
+            make_float4(round_tf32(v[4 * q]), round_tf32(v[4 * q + 1]), round_tf32(v[4 * q + 2]),
+                        round_tf32(v[4 * q + 3]));
+    }
+    l = l * corr + sum;
+    m = mx;
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+#pragma unroll
+      for (int k = 0; k < kBN / 8; ++k) {
+        const uint64_t ad = sdesc(smem_addr(sm + kPOff + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
+        const uint64_t bd = sdesc(smem_addr(sm + kVOff + b * 32768 + (k / 4) * 8192 + (k % 4) * 32), 16, 1024);
+        mma_tf32(t_o, ad, bd, id_o, k > 0);
+      }
+      mma_commit(bar_o);
+    }
+    ok = __syncthreads_and(mbar_wait(bar_o, (uint32_t)j & 1u));
+    if (!ok) break;
+    tc_fence_after();
+    if (tid == 0 && j + 2 < ntiles) load_kv(j + 2, b);
+#pragma unroll
+    for (int c = 0; c < kD; c += 32) {
+      float v[32];
+      tmem_ld32(t_o + lane_base + c, v);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[c + i] = fmaf(o[c + i], corr, v[i]);
+    }
+    tc_fence_before();
+    __syncthreads();   // every thread has read S and O_t before the next tile's MMAs overwrite them
+    tc_fence_after();
+  }
+  if (!ok) {
+    // record the failure, then give the copies and MMAs already issued a
+    // bounded chance to land before the shared and tensor memory go away
+    if (tid == 0) fail_timeout();
+    mbar_wait(&bar_kv[0], 0, 1 << 16);
+    mbar_wait(&bar_kv[1], 0, 1 << 16);
+    mbar_wait(bar_s, 0, 1 << 16);
+    mbar_wait(bar_o, 0, 1 << 16);
+  } else {
+    const float inv = 1.f / l;
+    float* orow = O + (size_t)(row0 + tid) * kD;
+#pragma unroll
+    for (int c = 0; c < kD; c += 4)
+      *reinterpret_cast<float4*>(orow + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+    if (lse) lse[row0 + tid] = (m + log2f(l)) * 0.69314718055994530942f;  // natural-log units
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ------------------------------------------------------------------ two-warpgroup kernel
+// 256 query rows per CTA in two warpgroups (128 rows each) that share the K
+// and V^T tiles; warp 8 is the TMA producer.  Each warpgroup runs its own
+// S -> softmax -> P V chain, so one group's softmax overlaps the other's
+// tensor-core work.  P is written back over S in tensor memory (rounded to
+// tf32) and is the A operand of the P V product straight from TMEM.
+// A K/V buffer is released to the producer by a tcgen05.commit from each
+// warpgroup once its MMAs on that buffer have completed.
+namespace {
+constexpr int kQ2Off = 0;                        // 2 groups x 2 x 16 KB
+constexpr int kKV2Off = 2 * 32768;               // 2 bufs x (K 32 KB + V^T 32 KB)
+constexpr int kBar2Off = kKV2Off + 2 * 65536;
+constexpr int kSmem2Bytes = kBar2Off + 256 + 1024;
+constexpr int kThreads2 = 288;
+}  // namespace
+
+__global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_constant__ CUtensorMap mQ,
+                                                              const __grid_constant__ CUtensorMap mK,
+                                                              const __grid_constant__ CUtensorMap mVt,
+                                                              float* __restrict__ O, float* __restrict__ lse, int n,
+                                                              float scale_log2) {
+  extern __shared__ unsigned char attn2_sm_raw[];
+  unsigned char* sm = (unsigned char*)(((uintptr_t)attn2_sm_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(sm + kBar2Off);      // [2] K tile rounded, V^T landed: consumers may start
+  uint64_t* empty = full + 2;                       // [2]
+  uint64_t* bar_q = full + 4;
+  uint64_t* bar_s = full + 5;                       // [2] per group
+  uint64_t* bar_o = full + 7;                       // [2] per group
+  uint64_t* landed = full + 9;                      // [2] TMA of the K / V^T tile complete
+  uint32_t* tslot = (uint32_t*)(sm + kBar2Off + 128);
+  volatile int* abort_flag = (volatile int*)(sm + kBar2Off + 132);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int bh = blockIdx.y;
+  const int row0 = bh * n + blockIdx.x * 256;
+  const int ntiles = n / kBN;
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&landed[i], 1);
+      mbar_init(&empty[i], 2);
+      mbar_init(&bar_s[i], 1);
+      mbar_init(&bar_o[i], 1);
+    }
+    mbar_init(bar_q, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 8) {
+    // ---------------- producer: TMA the K and V^T tiles, then round the K
+    // tile to the nearest tf32 in place (the tensor core would truncate it)
+    const int lane = tid & 31;
+    if (lane == 0) {
+      mbar_expect_tx(bar_q, 4 * 16384);
+      for (int g = 0; g < 2; ++g)
+        for (int r = 0; r < 2; ++r) tma_load_2d(sm + kQ2Off + g * 32768 + r * 16384, &mQ, 32 * r, row0 + g * 128, bar_q);
+    }
+    for (int j = 0; j < ntiles; ++j) {
+      const int b = j & 1;
+      unsigned char* kb = sm + kKV2Off + b * 65536;
+      bool ok = true;
+      if (j >= 2) ok = mbar_wait(&empty[b], (uint32_t)((j - 2) >> 1) & 1u);
+      if (!__all_sync(0xffffffffu, ok) || *abort_flag) { *abort_flag = 1; break; }
+      if (lane == 0) {
+        mbar_expect_tx(&landed[b], 2 * 16384 + 4 * 8192);
+        for (int r = 0; r < 2; ++r) tma_load_2d(kb + r * 16384, &mK, 32 * r, bh * n + j * kBN, &landed[b]);
+        for (int r = 0; r < 4; ++r) tma_load_2d(kb + 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &landed[b]);
+      }
+      ok = mbar_wait(&landed[b], (uint32_t)(j >> 1) & 1u);
+      if (!__all_sync(0xffffffffu, ok)) { *abort_flag = 1; break; }
+      float4* kt = reinterpret_cast<float4*>(kb);
+#pragma unroll 4
+      for (int i = lane; i < 2 * 16384 / 16; i += 32) {
+        float4 v = kt[i];
+        kt[i] = make_float4(round_tf32_int(v.x), round_tf32_int(v.y), round_tf32_int(v.z), round_tf32_int(v.w));
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[b]);
+    }
+  } else {
+    // ---------------- consumer warpgroup g
+    const int g = tid >> 7, t = tid & 127;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t t_s = tmem + g * 128, t_o = tmem + 256 + g * 64;
+    unsigned char* qg = sm + kQ2Off + g * 32768;
+    bool ok = mbar_wait(bar_q, 0);
+    if (ok) {
+      // round this thread's Q row to the nearest tf32 in place (both 128 B halves)
+      for (int r = 0; r < 2; ++r) {
+        float4* row = reinterpret_cast<float4*>(qg + r * 16384 + t * 128);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float4 v = row[c];
+          row[c] = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+        }
+      }
+      fence_proxy_async();
+    } else {
+      *abort_flag = 1;
+    }
+    const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
+    const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
+    // m: the exponent offset in use (log2 units); it is raised only when a
+    // score exceeds it by more than 8, so p = 2^(s*c - m) <= 256 and O, which
+    // accumulates in TMEM across tiles, is rescaled only on those raises.
+    float m = -INFINITY, l = 0.f;
+    ok = named_bar_and(1 + g, 128, ok);
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int b = j & 1;
+      unsigned char* kb = sm + kKV2Off + b * 65536;
+      if (!named_bar_and(1 + g, 128, mbar_wait(&full[b], (uint32_t)(j >> 1) & 1u))) { *abort_flag = 1; ok = false; break; }
+      tc_fence_after();
+      if (t == 0) {
+#pragma unroll
+        for (int k = 0; k < kD / 8; ++k) {
+          const uint64_t ad = sdesc(smem_addr(qg + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
+          const uint64_t bd = sdesc(smem_addr(kb + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
+          mma_tf32(t_s, ad, bd, id_s, k > 0);
+        }
+        mma_commit(&bar_s[g]);
+      }
+      if (!named_bar_and(1 + g, 128, mbar_wait(&bar_s[g], (uint32_t)j & 1u))) { *abort_flag = 1; ok = false; break; }
+      tc_fence_after();
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + lane_base + 32 * c, sr[c]);
+      tmem_ld_wait();
+      float mraw = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(sr[c][i]));
+      const float mt = mraw * scale_log2;
+      if (mt > m + 8.f) {
+        const float corr = ex2_approx(m - mt);   // 0 on the first tile
+        l *= corr;
+        if (j > 0) {   // rescale the accumulated O held in TMEM
+#pragma unroll 1
+          for (int c = 0; c < kD; c += 16) {
+            float v[16];
+            tmem_ld16(t_o + lane_base + c, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) v[i] *= corr;
+            tmem_st16(t_o + lane_base + c, v);
+          }
+        }
+        m = mt;
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float p = ex2_approx(fmaf(__uint_as_float(sr[c][i]), scale_log2, -m));
+          sum += p;
+          v[i] = round_tf32_int(p);
+        }
+        tmem_st32(t_s + lane_base + 32 * c, v);
+      }
+      tmem_st_wait();
+      l += sum;
+      tc_fence_before();
+      named_bar(1 + g, 128);
+      tc_fence_after();
+      if (t == 0) {
+#pragma unroll
+        for (int k = 0; k < kBN / 8; ++k) {
+          const uint64_t bd = sdesc(smem_addr(kb + 32768 + (k / 4) * 8192 + (k % 4) * 32), 16, 1024);
+          mma_tf32_ts(t_o, t_s + k * 8, bd, id_o, j > 0 || k > 0);
+        }
+        mma_commit(&bar_o[g]);
+        mma_commit(&empty[b]);
+      }
+      // P (in the S columns) and O must be settled before the next tile's S
+      // product and any rescale of O
+      if (!named_bar_and(1 + g, 128, mbar_wait(&bar_o[g], (uint32_t)j & 1u))) { *abort_flag = 1; ok = false; break; }
+      tc_fence_after();
+    }
+    if (ok) {
+      const float inv = 1.f / l;
+      float* orow = O + (size_t)(row0 + g * 128 + t) * kD;
+#pragma unroll
+      for (int c = 0; c < kD; c += 32) {
+        float v[32];
+        tmem_ld32(t_o + lane_base + c, v);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4)
+          *reinterpret_cast<float4*>(orow + c + i) = make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
+      }
+      if (lse) lse[row0 + g * 128 + t] = (m + log2f(l)) * 0.69314718055994530942f;
+    } else if (t == 0) {
+      fail_timeout();
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    // bounded drain of anything still in flight before the memory is released
+    for (int i = 0; i < 2; ++i) {
+      mbar_wait(&landed[i], 0, 1 << 14);
+      mbar_wait(&full[i], 0, 1 << 14);
+      mbar_wait(&bar_s[i], 0, 1 << 14);
+      mbar_wait(&bar_o[i], 0, 1 << 14);
+    }
+  }
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// V (rows = blocks*n, 64) -> V^T per block: (blocks*64, n), keys contiguous,
+// rounded to the nearest tf32.
+__global__ void k_transpose_v(const float* __restrict__ V, float* __restrict__ Vt, int n) {
+  __shared__ float t[32][33];
+  const int bh = blockIdx.z, k0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const float* src = V + (size_t)bh * n * kD;
+  float* dst = Vt + (size_t)bh * kD * n;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) t[i][threadIdx.x] = src[(size_t)(k0 + i) * kD + d0 + threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y)
+    dst[(size_t)(d0 + i) * n + k0 + threadIdx.x] = round_tf32(t[threadIdx.x][i]);
+}
+
+// Per-device V^T scratch, grown on demand and kept (it is reused by every call
+// on that device; calls on one device are stream-ordered by the caller).
+static int vt_scratch(size_t bytes, void** out) {
+  static std::mutex mu;
+  static std::unordered_map<int, std::pair<void*, size_t>> bufs;
+  int dev = 0;
+  AMC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> l(mu);
+  auto& e = bufs[dev];
+  if (e.second < bytes) {
+    if (e.first) {
+      AMC_CUDA(cudaDeviceSynchronize());
+      cudaFree(e.first);
+      e = {nullptr, 0};
+    }
+    AMC_CUDA(cudaMalloc(&e.first, bytes));
+    e.second = bytes;
+  }
+  *out = e.first;
+  return AMC_OK;
+}
+
+int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, float* lse, long long blocks, int n,
+                     int dk, int dv, float scale, cudaStream_t s, bool* handled) {
+  *handled = false;
+  if (dk != kD || dv != kD || n < kBN || (n % kBN) != 0 || blocks <= 0 || blocks > 65535) return AMC_OK;
+  if (((uintptr_t)Q | (uintptr_t)K | (uintptr_t)V | (uintptr_t)O) & 15) return AMC_OK;
+  const uint64_t rows = (uint64_t)blocks * n;
+  if (rows > 0x7fffffffull) return AMC_OK;
+  *handled = true;
+  float* Vt = nullptr;
+  int rc0 = vt_scratch((size_t)rows * kD * sizeof(float), (void**)&Vt);
+  if (rc0) return rc0;
+  k_transpose_v<<<dim3(n / 32, kD / 32, (unsigned)blocks), dim3(32, 8), 0, s>>>(V, Vt, n);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "k_transpose_v");
+  CUtensorMap mQ, mK, mVt;
+  int rc = make_tmap_2d_f32(&mQ, Q, rows, kD, kD, 128);
+  if (!rc) rc = make_tmap_2d_f32(&mK, K, rows, kD, kD, 128);
+  if (!rc) rc = make_tmap_2d_f32(&mVt, Vt, (uint64_t)blocks * kD, (uint64_t)n, (uint64_t)n, 64);
+  if (rc) return rc;
+  const float scale_log2 = scale * 1.4426950408889634f;
+  static bool attr2 = false, attr1 = false;
+  if (n % 256 == 0) {
+    if (!attr2) {
+      AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2Bytes));
+      attr2 = true;
+    }
+    k_attn_fwd_tc2<<<dim3(n / 256, (unsigned)blocks), kThreads2, kSmem2Bytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
+  } else {
+    if (!attr1) {
+      AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+      attr1 = true;
+    }
+    k_attn_fwd_tc<<<dim3(n / kBM, (unsigned)blocks), 128, kSmemBytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
+  }
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "k_attn_fwd_tc");
+  return AMC_OK;
+}
+
+int attention_check_error() {
+  int e = 0;
+  AMC_CUDA(cudaMemcpyFromSymbol(&e, g_attn_error, sizeof(int)));
+  if (e) {
+    int z = 0;
+    AMC_CUDA(cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int)));
+    return fail(e, "attention: a bounded wait on the tensor-core pipeline gave up");
+  }
+  return AMC_OK;
+}
+
+}  // namespace amc

@@ -177,5 +177,7 @@ bool fir_supported(const FirArgs& a);
 int launch_fir(const FirArgs& a, cudaStream_t s);
 int fir_launches(const FirArgs& a);
 int fir_check_error();   // reads and clears the device-side wait-timeout flag
+int attention_check_error();
+int device_check_errors();  // all kernels' bounded-wait flags
 
 }  // namespace amc

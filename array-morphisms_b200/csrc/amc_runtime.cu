@@ -144,6 +144,12 @@ int num_sms() {
   return n;
 }
 
+int device_check_errors() {
+  int rc = fir_check_error();
+  if (rc) return rc;
+  return attention_check_error();
+}
+
 }  // namespace amc
 
 using namespace amc;
@@ -207,7 +213,7 @@ int amc_shutdown(void) {
 
 int amc_synchronize(void) {
   AMC_CUDA(cudaStreamSynchronize(default_stream()));
-  return fir_check_error();
+  return device_check_errors();
 }
 
 int amc_buf_create(int32_t dtype, int64_t nelem, uint64_t* out) {
@@ -254,7 +260,7 @@ int amc_buf_download(uint64_t h, void* host, int64_t bytes, int64_t off) {
   cudaStream_t s = default_stream();
   AMC_CUDA(cudaMemcpyAsync(host, (char*)b->ptr + off, (size_t)bytes, cudaMemcpyDeviceToHost, s));
   AMC_CUDA(cudaStreamSynchronize(s));
-  return fir_check_error();
+  return device_check_errors();
 }
 
 int amc_buf_upload_async(uint64_t h, const void* host, int64_t bytes, int64_t off, void* stream) {

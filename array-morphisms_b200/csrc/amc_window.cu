@@ -29,6 +29,11 @@ __device__ __forceinline__ float2 ldg2(const float2* p) { return __ldg(p); }
 __device__ __forceinline__ float2 tap2(float2 acc, float2 h, float2 x) {
   return make_float2(__fadd_rn(acc.x, __fmul_rn(h.x, x.x)), __fadd_rn(acc.y, __fmul_rn(h.y, x.y)));
 }
+// First tap of a frame: the reference's output starts at +0.0, so the first
+// partial is fl(+0.0 + fl(h * x)) (which turns a -0.0 product into +0.0).
+__device__ __forceinline__ float2 tap2_first(float2 h, float2 x) {
+  return make_float2(__fadd_rn(0.f, __fmul_rn(h.x, x.x)), __fadd_rn(0.f, __fmul_rn(h.y, x.y)));
+}
 
 template <int PHASE>  // 0: rows 0..15 of the chunk; 1: interior; 2: rows chunk..chunk+14
 __device__ __forceinline__ void fir_rows16(float2 (&acc)[kTaps], const float2 (&h)[kTaps],
@@ -94,10 +99,14 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                ::"r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
-template <int PHASE>
+// RS: row stride of the staged tile and frame stride of the output, in float2
+// (compile-time for the 64-branch bank so every access uses an immediate offset).
+template <int PHASE, int RS>
 __device__ __forceinline__ void fir_rows16_smem(float2 (&acc)[kTaps], const float2 (&h)[kTaps],
-                                                const float2* __restrict__ srow, int rs,
-                                                float2* __restrict__ orow, long long os, bool store_ok) {
+                                                const float2* __restrict__ srow, int rs_rt,
+                                                float2* __restrict__ orow, long long os_rt, bool store_ok) {
+  const int rs = RS ? RS : rs_rt;
+  const long long os = RS ? RS : os_rt;
   float2 xv[16];
 #pragma unroll
   for (int jj = 0; jj < 16; ++jj) {
@@ -112,18 +121,15 @@ __device__ __forceinline__ void fir_rows16_smem(float2 (&acc)[kTaps], const floa
       const bool valid = PHASE == 0 ? (t <= jj) : PHASE == 2 ? (t > jj) : true;
       if (valid) {
         const int slot = (jj - t) & 15;
-        acc[slot] = tap2(acc[slot], h[t], xv[jj]);
+        acc[slot] = t == 0 ? tap2_first(h[t], xv[jj]) : tap2(acc[slot], h[t], xv[jj]);
       }
     }
     const bool done = PHASE == 0 ? (jj == 15) : true;
-    if (done) {
-      const int slot = (jj + 1) & 15;
-      if (store_ok) __stcs(orow + jj * os, acc[slot]);
-      acc[slot] = make_float2(0.f, 0.f);
-    }
+    if (done && store_ok) __stcs(orow + jj * os, acc[(jj + 1) & 15]);
   }
 }
 
+template <int RS>
 __global__ void __launch_bounds__(kWarpsPerCta * 32) k_fir_tma(const __grid_constant__ FirArgs a, long long chunks_per_sig) {
   extern __shared__ __align__(128) unsigned char fir_sm[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
@@ -174,9 +180,9 @@ __global__ void __launch_bounds__(kWarpsPerCta * 32) k_fir_tma(const __grid_cons
     }
     const float2* srow = reinterpret_cast<const float2*>(ring + (size_t)s * SB) + q;
     float2* orow = obase + ((long long)g * 16 - 15) * os;
-    if (g == 0) fir_rows16_smem<0>(acc, h, srow, rs, orow, os, active);
-    else if (g < kGroups - 1) fir_rows16_smem<1>(acc, h, srow, rs, orow, os, active);
-    else fir_rows16_smem<2>(acc, h, srow, rs, orow, os, active);
+    if (g == 0) fir_rows16_smem<0, RS>(acc, h, srow, rs, orow, os, active);
+    else if (g < kGroups - 1) fir_rows16_smem<1, RS>(acc, h, srow, rs, orow, os, active);
+    else fir_rows16_smem<2, RS>(acc, h, srow, rs, orow, os, active);
     __syncwarp();
     if (lane == 0 && g + kStages < kGroups) {
       const int gn = g + kStages;
@@ -275,13 +281,14 @@ int launch_fir(const FirArgs& a, cudaStream_t s) {
     const long long warps = a.batch * chunks;
     if (fir_tma_ok(a)) {
       const size_t sm = (size_t)kWarpsPerCta * kStages * 16 * a.branches * 4 + (size_t)kWarpsPerCta * kStages * 8;
-      static bool attr_set = false;
-      if (!attr_set) {
-        AMC_CUDA(cudaFuncSetAttribute(k_fir_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        attr_set = true;
-      }
       const unsigned blocks = (unsigned)((warps + kWarpsPerCta - 1) / kWarpsPerCta);
-      k_fir_tma<<<blocks, kWarpsPerCta * 32, sm, s>>>(a, chunks);
+      if (a.branches == 64 && a.o_fstride == 64) {
+        AMC_CUDA(cudaFuncSetAttribute(k_fir_tma<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        k_fir_tma<32><<<blocks, kWarpsPerCta * 32, sm, s>>>(a, chunks);
+      } else {
+        AMC_CUDA(cudaFuncSetAttribute(k_fir_tma<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        k_fir_tma<0><<<blocks, kWarpsPerCta * 32, sm, s>>>(a, chunks);
+      }
     } else {
       const unsigned blocks = (unsigned)((warps + 7) / 8);
       k_fir_chunks<<<blocks, 256, 0, s>>>(a, chunks);

@@ -304,7 +304,7 @@ def bench_filterbank(args, ws, rank, local):
             "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG_FB,
-            "roofline": {"bound": "hbm", "kernel": "k_fir_chunks (+ k_fir_tail)", "achieved": achieved, "peak": hbm,
+            "roofline": {"bound": "hbm", "kernel": "k_fir_tma (+ k_fir_tail)", "achieved": achieved, "peak": hbm,
                          "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
                          "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind,
                          "algorithmic_bytes_per_launch": bytes_step},
