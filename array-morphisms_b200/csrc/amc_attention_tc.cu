@@ -218,12 +218,11 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
                                                               float scale_log2) {
   extern __shared__ unsigned char attn2_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)attn2_sm_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(sm + kBar2Off);      // [2] K tile rounded, V^T landed: consumers may start
+  uint64_t* full = (uint64_t*)(sm + kBar2Off);      // [2] K and V^T tile landed
   uint64_t* empty = full + 2;                       // [2]
   uint64_t* bar_q = full + 4;
   uint64_t* bar_s = full + 5;                       // [2] per group
   uint64_t* bar_o = full + 7;                       // [2] per group
-  uint64_t* landed = full + 9;                      // [2] TMA of the K / V^T tile complete
   uint32_t* tslot = (uint32_t*)(sm + kBar2Off + 128);
   volatile int* abort_flag = (volatile int*)(sm + kBar2Off + 132);
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -233,7 +232,6 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
   if (tid == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&landed[i], 1);
       mbar_init(&empty[i], 2);
       mbar_init(&bar_s[i], 1);
       mbar_init(&bar_o[i], 1);
@@ -250,36 +248,23 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
   const uint32_t tmem = *tslot;
 
   if (warp == 8) {
-    // ---------------- producer: TMA the K and V^T tiles, then round the K
-    // tile to the nearest tf32 in place (the tensor core would truncate it)
-    const int lane = tid & 31;
-    if (lane == 0) {
+    // ---------------- producer: TMA the (pre-rounded) K and V^T tiles
+    if ((tid & 31) == 0) {
       mbar_expect_tx(bar_q, 4 * 16384);
       for (int g = 0; g < 2; ++g)
         for (int r = 0; r < 2; ++r) tma_load_2d(sm + kQ2Off + g * 32768 + r * 16384, &mQ, 32 * r, row0 + g * 128, bar_q);
-    }
-    for (int j = 0; j < ntiles; ++j) {
-      const int b = j & 1;
-      unsigned char* kb = sm + kKV2Off + b * 65536;
-      bool ok = true;
-      if (j >= 2) ok = mbar_wait(&empty[b], (uint32_t)((j - 2) >> 1) & 1u);
-      if (!__all_sync(0xffffffffu, ok) || *abort_flag) { *abort_flag = 1; break; }
-      if (lane == 0) {
-        mbar_expect_tx(&landed[b], 2 * 16384 + 4 * 8192);
-        for (int r = 0; r < 2; ++r) tma_load_2d(kb + r * 16384, &mK, 32 * r, bh * n + j * kBN, &landed[b]);
-        for (int r = 0; r < 4; ++r) tma_load_2d(kb + 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &landed[b]);
+      for (int j = 0; j < ntiles; ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&empty[b], (uint32_t)((j - 2) >> 1) & 1u)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        unsigned char* kb = sm + kKV2Off + b * 65536;
+        mbar_expect_tx(&full[b], 2 * 16384 + 4 * 8192);
+        for (int r = 0; r < 2; ++r) tma_load_2d(kb + r * 16384, &mK, 32 * r, bh * n + j * kBN, &full[b]);
+        for (int r = 0; r < 4; ++r) tma_load_2d(kb + 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &full[b]);
       }
-      ok = mbar_wait(&landed[b], (uint32_t)(j >> 1) & 1u);
-      if (!__all_sync(0xffffffffu, ok)) { *abort_flag = 1; break; }
-      float4* kt = reinterpret_cast<float4*>(kb);
-#pragma unroll 4
-      for (int i = lane; i < 2 * 16384 / 16; i += 32) {
-        float4 v = kt[i];
-        kt[i] = make_float4(round_tf32_int(v.x), round_tf32_int(v.y), round_tf32_int(v.z), round_tf32_int(v.w));
-      }
-      fence_proxy_async();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full[b]);
     }
   } else {
     // ---------------- consumer warpgroup g
@@ -402,13 +387,22 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
   if (*abort_flag) {
     // bounded drain of anything still in flight before the memory is released
     for (int i = 0; i < 2; ++i) {
-      mbar_wait(&landed[i], 0, 1 << 14);
       mbar_wait(&full[i], 0, 1 << 14);
       mbar_wait(&bar_s[i], 0, 1 << 14);
       mbar_wait(&bar_o[i], 0, 1 << 14);
     }
   }
   if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// K -> a copy rounded to the nearest tf32 (the tensor core would truncate).
+__global__ void k_round_tf32(const float4* __restrict__ src, float4* __restrict__ dst, long long n4) {
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < n4; i += stride) {
+    const float4 v = src[i];
+    dst[i] = make_float4(round_tf32_int(v.x), round_tf32_int(v.y), round_tf32_int(v.z), round_tf32_int(v.w));
+  }
 }
 
 // V (rows = blocks*n, 64) -> V^T per block: (blocks*64, n), keys contiguous,
@@ -455,14 +449,19 @@ int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, f
   if (rows > 0x7fffffffull) return AMC_OK;
   *handled = true;
   float* Vt = nullptr;
-  int rc0 = vt_scratch((size_t)rows * kD * sizeof(float), (void**)&Vt);
+  const size_t tbytes = (size_t)rows * kD * sizeof(float);
+  int rc0 = vt_scratch(2 * tbytes, (void**)&Vt);
   if (rc0) return rc0;
+  float* Kr = Vt + (size_t)rows * kD;
   k_transpose_v<<<dim3(n / 32, kD / 32, (unsigned)blocks), dim3(32, 8), 0, s>>>(V, Vt, n);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "k_transpose_v");
+  k_round_tf32<<<(unsigned)(num_sms() * 8), 256, 0, s>>>((const float4*)K, (float4*)Kr, (long long)(rows * kD / 4));
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "k_round_tf32");
   CUtensorMap mQ, mK, mVt;
   int rc = make_tmap_2d_f32(&mQ, Q, rows, kD, kD, 128);
-  if (!rc) rc = make_tmap_2d_f32(&mK, K, rows, kD, kD, 128);
+  if (!rc) rc = make_tmap_2d_f32(&mK, Kr, rows, kD, kD, 128);
   if (!rc) rc = make_tmap_2d_f32(&mVt, Vt, (uint64_t)blocks * kD, (uint64_t)n, (uint64_t)n, 64);
   if (rc) return rc;
   const float scale_log2 = scale * 1.4426950408889634f;

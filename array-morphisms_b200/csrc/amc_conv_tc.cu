@@ -1,0 +1,309 @@
+// Tensor-core 3x3 convolution (stride 1, pad 1, 64 -> 64 channels, NCHW),
+// tcgen05 kind::tf32 implicit GEMM; used by the forward and the data-gradient
+// (a forward convolution of dY with the flipped, transposed weights).
+//
+// The reference forms im2col(X) explicitly and multiplies it by the
+// flattened weights per image (execute-conv2d-blas, realization.scm:166-252).
+// Here no column matrix exists:
+//   - a pre-pass writes the input as zero-bordered NHWC rows (N, H+2, W+2, 64),
+//     rounded to the nearest tf32;
+//   - an output tile is 2 output rows x 64 columns (128 positions = MMA M).
+//     The producer TMA-loads the 4 padded input rows it needs, 64 positions
+//     per row, each position's 32 channels a 128-byte row of a K-major,
+//     128-byte-swizzled tile (two tiles: channels 0-31 and 32-63);
+//   - tap (kh, kw) of the tile is the same shared tile read from position
+//     kh*64 + kw on: its A descriptor starts (kh*64 + kw) * 128 bytes in, so
+//     all 9 taps are address offsets of one staged tile;
+//   - B is the tap's (64 out x 64 in) weight block, K-major, resident in
+//     shared memory for the whole kernel;
+//   - 72 MMAs (9 taps x 64 channels / 8) accumulate one 128 x 64 f32 tile in
+//     tensor memory; two accumulators alternate so the epilogue of one tile
+//     overlaps the MMAs of the next.
+// Output columns 56..63 of a tile are computed on zero padding and dropped.
+// Warp roles: warp 0 producer, warp 1 MMA issuer, warps 4-7 epilogue.
+#include <cudaTypedefs.h>
+
+#include "amc_internal.h"
+#include "amc_tc.cuh"
+
+namespace amc {
+
+struct ConvShape {
+  int N, C, H, W, K, KH, KW, SH, SW, PH, PW, OH, OW;
+};
+
+using namespace tc;
+
+namespace {
+
+constexpr int kC = 64;                    // in = out channels
+constexpr int kPosRow = 64;               // positions per staged input row
+constexpr int kRegion = 4 * kPosRow * 128 + 1024;   // 4 input rows + slack (1024-aligned)
+constexpr int kWOff = 0;                  // 9 taps x 2 chunks x 8 KB
+constexpr int kXOff = kWOff + 9 * 2 * 8192;         // 2 chunk regions
+constexpr int kBarOffC = kXOff + 2 * kRegion;
+constexpr int kConvSmem = kBarOffC + 256 + 1024;
+constexpr int kConvThreads = 256;
+
+__device__ int g_conv_error;
+
+}  // namespace
+
+__global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ CUtensorMap mX,
+                                                               const __grid_constant__ CUtensorMap mW,
+                                                               float* __restrict__ Y, int N, int H, int Wd) {
+  extern __shared__ unsigned char conv_sm_raw[];
+  unsigned char* sm = (unsigned char*)(((uintptr_t)conv_sm_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* w_full = (uint64_t*)(sm + kBarOffC);
+  uint64_t* x_full = w_full + 1;      // [2] per channel chunk
+  uint64_t* x_empty = w_full + 3;     // [2]
+  uint64_t* acc_full = w_full + 5;    // [2] per accumulator
+  uint64_t* acc_empty = w_full + 7;   // [2]
+  uint32_t* tslot = (uint32_t*)(sm + kBarOffC + 128);
+  volatile int* abort_flag = (volatile int*)(sm + kBarOffC + 132);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int pairs = H / 2;
+  const int ntiles = N * pairs;
+  const int Hp = H + 2;
+  if (tid == 0) {
+    mbar_init(w_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&x_full[i], 1);
+      mbar_init(&x_empty[i], 1);
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 1);
+    }
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 0) tmem_alloc(tslot, 128);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // weights once: 18 boxes of (32 in-channels x 64 out-channels)
+      mbar_expect_tx(w_full, 18 * 8192);
+      for (int i = 0; i < 18; ++i) tma_load_2d(sm + kWOff + i * 8192, &mW, 0, i * 64, w_full);
+      int li = 0;
+      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++li) {
+        const int n = tile / pairs, oh0 = (tile % pairs) * 2;
+        const int row = n * Hp + oh0;   // padded input rows oh0 .. oh0+3
+        for (int c = 0; c < 2; ++c) {
+          if (li > 0 && !mbar_wait(&x_empty[c], (uint32_t)(li - 1) & 1u)) { *abort_flag = 1; break; }
+          mbar_expect_tx(&x_full[c], 4 * kPosRow * 128);
+          // one 3-D box: 32 channels x 64 positions x 4 rows
+          asm volatile(
+              "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+              ::"r"(smem_addr(sm + kXOff + c * kRegion)), "l"((uint64_t)&mX), "r"(32 * c), "r"(0), "r"(row),
+                "r"(smem_addr(&x_full[c])) : "memory");
+        }
+        if (*abort_flag) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(128, kC, false, false);
+      bool ok = mbar_wait(w_full, 0);
+      int li = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++li) {
+        const int a = li & 1;
+        if (li >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)((li - 2) >> 1) & 1u)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d = tmem + a * kC;
+        for (int c = 0; c < 2; ++c) {
+          if (!mbar_wait(&x_full[c], (uint32_t)li & 1u)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t xbase = smem_addr(sm + kXOff + c * kRegion);
+          for (int tap = 0; tap < 9; ++tap) {
+            const int kh = tap / 3, kw = tap % 3;
+            const uint32_t abase = xbase + (uint32_t)((kh * kPosRow + kw) * 128);
+            const uint32_t bbase = smem_addr(sm + kWOff + (tap * 2 + c) * 8192);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_tf32(d, sdesc(abase + k * 32, 16, 1024), sdesc(bbase + k * 32, 16, 1024), idesc,
+                       (c | tap | k) != 0);
+          }
+          mma_commit(&x_empty[c]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[a]);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp >= 4) {
+    // epilogue warpgroup: TMEM lane q = output position q of the tile
+    const int q = tid - 128;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const int r = q / kPosRow, col = q % kPosRow;
+    int li = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++li) {
+      const int a = li & 1;
+      ok = named_bar_and(1, 128, mbar_wait(&acc_full[a], (uint32_t)(li >> 1) & 1u) && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      float v[2][32];
+      tmem_ld32(tmem + a * kC + lane_base, v[0]);
+      tmem_ld32(tmem + a * kC + lane_base + 32, v[1]);
+      tc_fence_before();
+      named_bar(1, 128);
+      if (q == 0) mbar_arrive(&acc_empty[a]);
+      const int n = tile / pairs, oh = (tile % pairs) * 2 + r;
+      if (col < Wd) {
+        float* yp = Y + ((size_t)n * kC * H + oh) * Wd + col;
+#pragma unroll
+        for (int co = 0; co < kC; ++co) __stcs(yp + (size_t)co * H * Wd, v[co >> 5][co & 31]);
+      }
+    }
+    if (!ok && q == 0) atomicExch(&g_conv_error, AMC_ERR_TIMEOUT);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_wait(&x_full[i], 0, 1 << 14);
+      mbar_wait(&acc_full[i], 0, 1 << 14);
+    }
+  }
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
+// NCHW (N, 64, H, W) -> zero-bordered NHWC (N, H+2, W+2, 64), rounded to tf32.
+// One block per padded row; the border rows / columns are written as zeros.
+__global__ void k_pad_nhwc(const float* __restrict__ X, float* __restrict__ Xp, int H, int Wd) {
+  __shared__ float t[kC][65];
+  const int prow = blockIdx.x;                 // n * (H+2) + hp
+  const int Hp = H + 2, Wp = Wd + 2;
+  const int n = prow / Hp, hp = prow % Hp, h = hp - 1;
+  float* dst = Xp + (size_t)prow * Wp * kC;
+  if (h < 0 || h >= H) {
+    for (int i = threadIdx.x; i < Wp * kC; i += blockDim.x) dst[i] = 0.f;
+    return;
+  }
+  for (int w0 = 0; w0 < Wd; w0 += 64) {
+    const int wn = Wd - w0 < 64 ? Wd - w0 : 64;
+    for (int i = threadIdx.x; i < kC * 64; i += blockDim.x) {
+      const int c = i / 64, w = i % 64;
+      t[c][w] = w < wn ? X[(((size_t)n * kC + c) * H + h) * Wd + w0 + w] : 0.f;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < kC * wn; i += blockDim.x) {
+      const int w = i / kC, c = i % kC;
+      dst[(size_t)(w0 + w + 1) * kC + c] = round_tf32(t[c][w]);
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x < kC) {
+    dst[threadIdx.x] = 0.f;
+    dst[(size_t)(Wp - 1) * kC + threadIdx.x] = 0.f;
+  }
+}
+
+// Weights (64 out, 64 in, 3, 3) -> [tap][in-chunk][out][32 in], rounded to tf32.
+// flip != 0 gives the data-gradient weights W'[in][out][2-kh][2-kw].
+__global__ void k_conv_weights(const float* __restrict__ W, float* __restrict__ Wt, int flip) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= 9 * kC * kC) return;
+  const int ci = i % 32, co = (i / 32) % kC, chunk = (i / (32 * kC)) % 2, tap = i / (2 * 32 * kC);
+  const int kh = tap / 3, kw = tap % 3, cin = chunk * 32 + ci;
+  const float v = flip ? W[(((size_t)cin * kC + co) * 3 + (2 - kh)) * 3 + (2 - kw)]
+                       : W[(((size_t)co * kC + cin) * 3 + kh) * 3 + kw];
+  Wt[i] = round_tf32(v);
+}
+
+static int conv_scratch(size_t bytes, void** out) {
+  static std::mutex mu;
+  static std::unordered_map<int, std::pair<void*, size_t>> bufs;
+  int dev = 0;
+  AMC_CUDA(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> l(mu);
+  auto& e = bufs[dev];
+  if (e.second < bytes) {
+    if (e.first) {
+      AMC_CUDA(cudaDeviceSynchronize());
+      cudaFree(e.first);
+      e = {nullptr, 0};
+    }
+    AMC_CUDA(cudaMalloc(&e.first, bytes));
+    e.second = bytes;
+  }
+  *out = e.first;
+  return AMC_OK;
+}
+
+static bool conv_tc_shape(const ConvShape& s) {
+  return s.C == kC && s.K == kC && s.KH == 3 && s.KW == 3 && s.SH == 1 && s.SW == 1 && s.PH == 1 && s.PW == 1 &&
+         s.H % 2 == 0 && s.W + 2 <= kPosRow + 2 && s.W >= 8 && s.N >= 1 && (size_t)s.N * (s.H + 2) < (1u << 31);
+}
+
+static int conv_run(const float* in, const float* W, float* out, const ConvShape& s, int flip, cudaStream_t st) {
+  const int Hp = s.H + 2, Wp = s.W + 2;
+  const size_t xbytes = (size_t)s.N * Hp * Wp * kC * sizeof(float);
+  void* scratch = nullptr;
+  int rc = conv_scratch(xbytes + 9 * kC * kC * sizeof(float) + 1024, &scratch);
+  if (rc) return rc;
+  float* Xp = (float*)scratch;
+  float* Wt = (float*)(((uintptr_t)((char*)scratch + xbytes) + 1023) & ~(uintptr_t)1023);
+  k_pad_nhwc<<<(unsigned)(s.N * Hp), 256, 0, st>>>(in, Xp, s.H, s.W);
+  AMC_CUDA(cudaGetLastError());
+  k_conv_weights<<<(9 * kC * kC + 255) / 256, 256, 0, st>>>(W, Wt, flip);
+  AMC_CUDA(cudaGetLastError());
+  // X: 3-D (channels, positions of a padded row, padded rows), box 32 x 64 x 4
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
+      return fail(AMC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+    encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  CUtensorMap mX, mW;
+  cuuint64_t dims[3] = {(cuuint64_t)kC, (cuuint64_t)Wp, (cuuint64_t)s.N * Hp};
+  cuuint64_t strides[2] = {(cuuint64_t)kC * 4, (cuuint64_t)Wp * kC * 4};
+  cuuint32_t box[3] = {32, (cuuint32_t)kPosRow, 4};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult cr = encode(&mX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, Xp, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return fail(AMC_ERR_CUDA, "conv: input tensor map failed");
+  rc = make_tmap_2d_f32(&mW, Wt, 9 * 2 * kC, 32, 32, 64);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    AMC_CUDA(cudaFuncSetAttribute(k_conv3x3_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kConvSmem));
+    attr = true;
+  }
+  const int ntiles = s.N * (s.H / 2);
+  const int grid = ntiles < num_sms() ? ntiles : num_sms();
+  k_conv3x3_tc<<<grid, kConvThreads, kConvSmem, st>>>(mX, mW, out, s.N, s.H, s.W);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+int conv_fwd_tc(const float* X, const float* W, float* Y, const ConvShape& s, cudaStream_t st, bool* handled) {
+  *handled = conv_tc_shape(s);
+  if (!*handled) return AMC_OK;
+  return conv_run(X, W, Y, s, 0, st);
+}
+
+int conv_dgrad_tc(const float* dY, const float* W, float* dX, const ConvShape& s, cudaStream_t st, bool* handled) {
+  *handled = conv_tc_shape(s);
+  if (!*handled) return AMC_OK;
+  return conv_run(dY, W, dX, s, 1, st);
+}
+
+int conv_check_error() {
+  int e = 0;
+  AMC_CUDA(cudaMemcpyFromSymbol(&e, g_conv_error, sizeof(int)));
+  if (e) {
+    int z = 0;
+    AMC_CUDA(cudaMemcpyToSymbol(g_conv_error, &z, sizeof(int)));
+    return fail(e, "conv: a bounded wait on the tensor-core pipeline gave up");
+  }
+  return AMC_OK;
+}
+
+}  // namespace amc

@@ -147,7 +147,9 @@ int num_sms() {
 int device_check_errors() {
   int rc = fir_check_error();
   if (rc) return rc;
-  return attention_check_error();
+  rc = attention_check_error();
+  if (rc) return rc;
+  return conv_check_error();
 }
 
 }  // namespace amc
