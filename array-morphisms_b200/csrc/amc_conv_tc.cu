@@ -173,33 +173,38 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
 }
 
 // NCHW (N, 64, H, W) -> zero-bordered NHWC (N, H+2, W+2, 64), rounded to tf32.
-// One block per padded row; the border rows / columns are written as zeros.
-__global__ void k_pad_nhwc(const float* __restrict__ X, float* __restrict__ Xp, int H, int Wd) {
-  __shared__ float t[kC][65];
+// One block per padded row: 16-byte loads of the 64 channel rows into shared
+// memory, then 16-byte stores of 4 channels per position.  Border rows and
+// columns are written as zeros.  Requires W % 4 == 0 and W <= 64.
+__global__ void __launch_bounds__(256) k_pad_nhwc(const float* __restrict__ X, float* __restrict__ Xp, int H, int Wd) {
+  __shared__ float t[kC][kPosRow + 1];
   const int prow = blockIdx.x;                 // n * (H+2) + hp
   const int Hp = H + 2, Wp = Wd + 2;
   const int n = prow / Hp, hp = prow % Hp, h = hp - 1;
-  float* dst = Xp + (size_t)prow * Wp * kC;
+  float4* dst4 = reinterpret_cast<float4*>(Xp + (size_t)prow * Wp * kC);
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
   if (h < 0 || h >= H) {
-    for (int i = threadIdx.x; i < Wp * kC; i += blockDim.x) dst[i] = 0.f;
+    for (int i = threadIdx.x; i < Wp * kC / 4; i += blockDim.x) dst4[i] = z;
     return;
   }
-  for (int w0 = 0; w0 < Wd; w0 += 64) {
-    const int wn = Wd - w0 < 64 ? Wd - w0 : 64;
-    for (int i = threadIdx.x; i < kC * 64; i += blockDim.x) {
-      const int c = i / 64, w = i % 64;
-      t[c][w] = w < wn ? X[(((size_t)n * kC + c) * H + h) * Wd + w0 + w] : 0.f;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < kC * wn; i += blockDim.x) {
-      const int w = i / kC, c = i % kC;
-      dst[(size_t)(w0 + w + 1) * kC + c] = round_tf32(t[c][w]);
-    }
-    __syncthreads();
+  const int w4 = Wd / 4;
+  for (int i = threadIdx.x; i < kC * w4; i += blockDim.x) {
+    const int c = i / w4, q = i % w4;
+    const float4 v = *reinterpret_cast<const float4*>(X + (((size_t)n * kC + c) * H + h) * Wd + 4 * q);
+    t[c][4 * q] = v.x;
+    t[c][4 * q + 1] = v.y;
+    t[c][4 * q + 2] = v.z;
+    t[c][4 * q + 3] = v.w;
   }
-  if (threadIdx.x < kC) {
-    dst[threadIdx.x] = 0.f;
-    dst[(size_t)(Wp - 1) * kC + threadIdx.x] = 0.f;
+  __syncthreads();
+  for (int i = threadIdx.x; i < Wd * (kC / 4); i += blockDim.x) {
+    const int w = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
+    dst4[(size_t)(w + 1) * (kC / 4) + c4 / 4] =
+        make_float4(round_tf32(t[c4][w]), round_tf32(t[c4 + 1][w]), round_tf32(t[c4 + 2][w]), round_tf32(t[c4 + 3][w]));
+  }
+  if (threadIdx.x < kC / 4) {
+    dst4[threadIdx.x] = z;
+    dst4[(size_t)(Wp - 1) * (kC / 4) + threadIdx.x] = z;
   }
 }
 
@@ -237,7 +242,8 @@ static int conv_scratch(size_t bytes, void** out) {
 
 static bool conv_tc_shape(const ConvShape& s) {
   return s.C == kC && s.K == kC && s.KH == 3 && s.KW == 3 && s.SH == 1 && s.SW == 1 && s.PH == 1 && s.PW == 1 &&
-         s.H % 2 == 0 && s.W + 2 <= kPosRow + 2 && s.W >= 8 && s.N >= 1 && (size_t)s.N * (s.H + 2) < (1u << 31);
+         s.H % 2 == 0 && s.W + 2 <= kPosRow && s.W % 4 == 0 && s.W >= 8 && s.N >= 1 &&
+         (size_t)s.N * (s.H + 2) < (1u << 31);
 }
 
 static int conv_run(const float* in, const float* W, float* out, const ConvShape& s, int flip, cudaStream_t st) {
@@ -293,6 +299,183 @@ int conv_dgrad_tc(const float* dY, const float* W, float* dX, const ConvShape& s
   *handled = conv_tc_shape(s);
   if (!*handled) return AMC_OK;
   return conv_run(dY, W, dX, s, 1, st);
+}
+
+// ------------------------------------------------------------------ weight gradient
+// dW[co, ci, kh, kw] = sum_{n, q} dY[n, co, q - (kh-1)*W] * X_kw[n, ci, q]
+// over flattened positions q of the H x W plane, where X_kw is X shifted by
+// kw-1 columns with zeros at the row ends (dY is zero outside the plane; the
+// row shift is a TMA coordinate offset of W elements, zero-filled out of
+// range).  The reference's order is a batch sum of per-image GEMMs
+// dY_n . im2col(X_n)^T; here the position sum is split across CTAs and the
+// CTA partials are added in CTA order by a second kernel.
+// Per K-chunk of 32 positions a stage holds A = dY rows for kh = 0, 1, 2
+// (3 x 64 rows, K-major) and B = X_kw for kw = 0, 1, 2 (3 x 64 rows).  For
+// each kw two M=128 MMAs cover the kh rows (0,1) and (1,2); their 64-column
+// accumulators live in tensor memory for the CTA's whole chunk range.
+namespace {
+constexpr int kWgStage = 6 * 8192;        // 3 A blocks + 3 B blocks of 64 rows x 128 B
+constexpr int kWgStages = 4;
+constexpr int kWgBarOff = kWgStages * kWgStage;
+constexpr int kWgSmem = kWgBarOff + 256 + 1024;
+}  // namespace
+
+__global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant__ CUtensorMap mDY,
+                                                         const __grid_constant__ CUtensorMap mXk,
+                                                         float* __restrict__ partials, int N, int HW,
+                                                         int Wd, int chunks_per_img) {
+  extern __shared__ unsigned char wg_sm_raw[];
+  unsigned char* sm = (unsigned char*)(((uintptr_t)wg_sm_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = (uint64_t*)(sm + kWgBarOff);   // [kWgStages]
+  uint64_t* empty = full + kWgStages;             // [kWgStages]
+  uint64_t* done = full + 2 * kWgStages;
+  uint32_t* tslot = (uint32_t*)(sm + kWgBarOff + 128);
+  volatile int* abort_flag = (volatile int*)(sm + kWgBarOff + 132);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int total = N * chunks_per_img;
+  const int c0 = (int)((long long)total * blockIdx.x / gridDim.x);
+  const int c1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+  if (tid == 0) {
+    for (int i = 0; i < kWgStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(done, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 0) tmem_alloc(tslot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int c = c0, it = 0; c < c1; ++c, ++it) {
+        const int st = it % kWgStages;
+        if (it >= kWgStages && !mbar_wait(&empty[st], (uint32_t)((it / kWgStages) - 1) & 1u)) { *abort_flag = 1; break; }
+        const int n = c / chunks_per_img, q0 = (c % chunks_per_img) * 32;
+        unsigned char* sb = sm + st * kWgStage;
+        mbar_expect_tx(&full[st], kWgStage);
+        for (int kh = 0; kh < 3; ++kh) tma_load_2d(sb + kh * 8192, &mDY, q0 - (kh - 1) * Wd, n * kC, &full[st]);
+        for (int kw = 0; kw < 3; ++kw)
+          tma_load_2d(sb + (3 + kw) * 8192, &mXk, q0, (kw * N + n) * kC, &full[st]);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32(128, kC, false, false);
+      bool ok = true;
+      for (int c = c0, it = 0; c < c1; ++c, ++it) {
+        const int st = it % kWgStages;
+        if (!mbar_wait(&full[st], (uint32_t)(it / kWgStages) & 1u)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sb = smem_addr(sm + st * kWgStage);
+        for (int kw = 0; kw < 3; ++kw)
+          for (int blk = 0; blk < 2; ++blk) {
+            const uint32_t d = tmem + (uint32_t)(kw * 128 + blk * 64);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_tf32(d, sdesc(sb + blk * 8192 + k * 32, 16, 1024), sdesc(sb + (3 + kw) * 8192 + k * 32, 16, 1024),
+                       idesc, it > 0 || k > 0);
+          }
+        mma_commit(&empty[st]);
+      }
+      if (!ok) *abort_flag = 1;
+      mma_commit(done);
+    }
+  } else if (warp >= 4) {
+    const int row = tid - 128;   // TMEM lane
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const bool ok = named_bar_and(1, 128, mbar_wait(done, 0) && !*abort_flag);
+    if (ok && c1 > c0) {
+      tc_fence_after();
+      // lanes 0-63 of block 0 are kh=0, 64-127 kh=1; block 1 lanes 64-127 are kh=2
+      float* part = partials + (size_t)blockIdx.x * (kC * kC * 9);
+      for (int kw = 0; kw < 3; ++kw)
+        for (int blk = 0; blk < 2; ++blk) {
+          if (blk == 1 && row < 64) continue;   // duplicate of kh=1
+          const int kh = blk == 0 ? (row < 64 ? 0 : 1) : 2, co = row & 63;
+          for (int half = 0; half < 2; ++half) {
+            float v[32];
+            tmem_ld32(tmem + (uint32_t)(kw * 128 + blk * 64 + half * 32) + lane_base, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) part[(((size_t)co * kC + half * 32 + i) * 3 + kh) * 3 + kw] = v[i];
+          }
+        }
+    } else if (!ok && row == 0) {
+      atomicExch(&g_conv_error, AMC_ERR_TIMEOUT);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// dW = sum of the CTA partials in CTA order (zero for CTAs without chunks).
+__global__ void k_wgrad_reduce(const float* __restrict__ partials, float* __restrict__ dW, int nparts, const int* counts) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= kC * kC * 9) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p)
+    if (counts[p]) s += partials[(size_t)p * kC * kC * 9 + i];
+  dW[i] = s;
+}
+
+// X (N, 64, H, W) -> X_kw (3, N, 64, H*W), X_kw[.., h, w] = X[.., h, w + kw - 1] (0 outside),
+// and dY -> rounded copy; all rounded to the nearest tf32.
+__global__ void k_wgrad_prep(const float* __restrict__ X, const float* __restrict__ dY, float* __restrict__ Xk,
+                             float* __restrict__ dYr, long long plane_elems, int Wd) {
+  const long long total = plane_elems;   // N * 64 * H * W
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (; i < total; i += stride) {
+    const int w = (int)(i % Wd);
+    const float x = X[i];
+    Xk[total + i] = round_tf32(x);
+    Xk[i] = w > 0 ? round_tf32(X[i - 1]) : 0.f;                // kw = 0: X[w - 1]
+    Xk[2 * total + i] = w < Wd - 1 ? round_tf32(X[i + 1]) : 0.f;  // kw = 2: X[w + 1]
+    dYr[i] = round_tf32(dY[i]);
+  }
+}
+
+int conv_wgrad_tc(const float* X, const float* dY, float* dW, const ConvShape& s, cudaStream_t st, bool* handled) {
+  *handled = s.C == kC && s.K == kC && s.KH == 3 && s.KW == 3 && s.SH == 1 && s.SW == 1 && s.PH == 1 && s.PW == 1 &&
+             s.W % 4 == 0 && (s.H * s.W) % 32 == 0 && s.N >= 1 && (long long)s.N * kC * 3 < (1 << 30);
+  if (!*handled) return AMC_OK;
+  const long long plane = (long long)s.N * kC * s.H * s.W;
+  const int nsm = num_sms();
+  const size_t part_bytes = (size_t)nsm * kC * kC * 9 * sizeof(float);
+  void* scratch = nullptr;
+  int rc = conv_scratch((size_t)plane * 4 * sizeof(float) + part_bytes + 4096, &scratch);
+  if (rc) return rc;
+  float* Xk = (float*)scratch;
+  float* dYr = Xk + 3 * plane;
+  float* parts = dYr + plane;
+  int* counts = (int*)(parts + (size_t)nsm * kC * kC * 9);
+  k_wgrad_prep<<<nsm * 8, 256, 0, st>>>(X, dY, Xk, dYr, plane, s.W);
+  AMC_CUDA(cudaGetLastError());
+  const int HW = s.H * s.W, cpi = HW / 32, total = s.N * cpi;
+  const int grid = total < nsm ? total : nsm;
+  std::vector<int> cnt(grid);
+  for (int b = 0; b < grid; ++b)
+    cnt[b] = (int)((long long)total * (b + 1) / grid) - (int)((long long)total * b / grid);
+  AMC_CUDA(cudaMemcpyAsync(counts, cnt.data(), grid * sizeof(int), cudaMemcpyHostToDevice, st));
+  CUtensorMap mDY, mXk;
+  rc = make_tmap_2d_f32(&mDY, dYr, (uint64_t)s.N * kC, (uint64_t)HW, (uint64_t)HW, 64);
+  if (!rc) rc = make_tmap_2d_f32(&mXk, Xk, (uint64_t)3 * s.N * kC, (uint64_t)HW, (uint64_t)HW, 64);
+  if (rc) return rc;
+  static bool attr = false;
+  if (!attr) {
+    AMC_CUDA(cudaFuncSetAttribute(k_conv_wgrad_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kWgSmem));
+    attr = true;
+  }
+  k_conv_wgrad_tc<<<grid, 256, kWgSmem, st>>>(mDY, mXk, parts, s.N, HW, s.W, cpi);
+  AMC_CUDA(cudaGetLastError());
+  k_wgrad_reduce<<<(kC * kC * 9 + 255) / 256, 256, 0, st>>>(parts, dW, grid, counts);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
 }
 
 int conv_check_error() {

@@ -407,15 +407,20 @@ def bench_other(args, ws, rank, local):
         launches = 1
     elif wl == "conv":
         N = args.batch
-        x = torch.randn(N, 64, 56, 56, device="cuda")
-        wt = torch.randn(64, 64, 3, 3, device="cuda") * math.sqrt(2 / 576)
-        yy = torch.empty_like(x)
-        run = lambda: W.conv2d_fwd(x, wt, yy)
-        work = 2.0 * N * 64 * 64 * 9 * 56 * 56
-        unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward TFLOP/s"
+        x = torch.from_numpy(W.normal(W.seed_of(3, 0), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
+        wt = torch.from_numpy((W.normal(W.seed_of(3, 1), 64 * 64 * 9) * math.sqrt(2 / 576)).astype(np.float32)).cuda().view(64, 64, 3, 3)
+        dy = torch.from_numpy(W.normal(W.seed_of(3, 2), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
+        yy, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(wt)
+
+        def run():
+            W.conv2d_fwd(x, wt, yy)
+            W.conv2d_dgrad(dy, wt, dx)
+            W.conv2d_wgrad(x, dy, dw)
+        work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
+        unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward + data gradient + weight gradient TFLOP/s"
         pre = lambda: None
-        cfg = {"workload": f"config 3: x ({N},64,56,56) f32, w (64,64,3,3), stride 1 pad 1, forward"}
-        launches = 1
+        cfg = {"workload": f"config 3: x ({N},64,56,56) f32, w (64,64,3,3), stride 1 pad 1; Y, dX and dW per step"}
+        launches = 9
     else:
         raise SystemExit(f"unknown workload {wl}")
     for _ in range(args.warmup):

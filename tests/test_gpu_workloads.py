@@ -219,7 +219,7 @@ def test_attention_entry_points(amc, shape):
         assert e <= 2e-3, e
 
 
-@pytest.mark.parametrize("N,Cc,H,Wd,K", [(2, 4, 9, 7, 5), (3, 64, 14, 14, 64), (2, 64, 56, 56, 64), (1, 64, 8, 62, 64)])
+@pytest.mark.parametrize("N,Cc,H,Wd,K", [(2, 4, 9, 7, 5), (3, 64, 14, 14, 64), (2, 64, 56, 56, 64), (1, 64, 8, 60, 64), (1, 64, 6, 64, 64)])
 def test_conv_entry_points(amc, N, Cc, H, Wd, K):
     import torch
     from amcuda import workloads as W
