@@ -33,7 +33,7 @@ PER_FILE = {"amc_window.cu": ["-fmad=false"]}
 
 def _compile(src: Path, force: bool) -> Path:
     obj = BUILD / (src.stem + ".o")
-    deps = [src] + sorted(CSRC.glob("*.h")) + [HERE.parent / "include" / "amc.h"]
+    deps = [src] + sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + [HERE.parent / "include" / "amc.h"]
     if not force and obj.exists() and obj.stat().st_mtime >= max(d.stat().st_mtime for d in deps):
         return obj
     extra = PER_FILE.get(src.name, [])

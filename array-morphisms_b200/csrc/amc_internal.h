@@ -178,6 +178,7 @@ int launch_fir(const FirArgs& a, cudaStream_t s);
 int fir_launches(const FirArgs& a);
 int fir_check_error();   // reads and clears the device-side wait-timeout flag
 int attention_check_error();
+int attention_bwd_check_error();
 int conv_check_error();
 int device_check_errors();  // all kernels' bounded-wait flags
 

@@ -53,6 +53,12 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       ::"r"(smem_addr(dst)), "l"((uint64_t)map), "r"(x), "r"(y), "r"(smem_addr(bar)) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// 1-D bulk copy global -> shared (both 16-byte aligned, bytes a multiple of 16),
+// counted on `bar` (the caller posts the expected bytes).  No multicast.
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
+}
 
 // ------------------------------------------------------------------ tensor memory
 // alloc/dealloc are warp-collective; the base address is written to *dst (shared).

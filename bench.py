@@ -397,14 +397,21 @@ def bench_other(args, ws, rank, local):
         B, H, S, D = args.batch, 16, 2048, 64
         q, k, v = (torch.from_numpy(W.normal(W.seed_of(4, j), B * H * S * D).astype(np.float32)).cuda().view(B, H, S, D)
                    for j in range(3))
+        do = torch.from_numpy(W.normal(W.seed_of(4, 3), B * H * S * D).astype(np.float32)).cuda().view(B, H, S, D)
         o = torch.empty_like(q)
         lse = torch.empty((B, H, S), dtype=torch.float32, device="cuda")
-        run = lambda: W.attention_fwd(q, k, v, o, lse, 1.0 / 8.0)
-        work = 4.0 * B * H * S * S * D
-        unit, bound, metric = "TFLOP/s", "tensor", "attention forward TFLOP/s"
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+        def run():
+            W.attention_fwd(q, k, v, o, lse, 1.0 / 8.0)
+            W.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, 1.0 / 8.0)
+        # algorithmic: forward 2 GEMMs (Q K^T, P V), backward 4 (dV, dP, dQ, dK)
+        work = 12.0 * B * H * S * S * D
+        unit, bound, metric = "TFLOP/s", "tensor", "attention forward + backward TFLOP/s"
         pre = lambda: None
-        cfg = {"workload": f"config 4: Q,K,V ({B},16,2048,64) f32, scale 1/8, forward"}
-        launches = 1
+        cfg = {"workload": f"config 4: Q,K,V,dO ({B},16,2048,64) f32, scale 1/8; O, dQ, dK, dV per step",
+               "flops": "algorithmic 12*B*H*S^2*D (6 GEMMs; the backward recomputes S and dP twice more)"}
+        launches = 6   # forward: V^T, K rounding, kernel; backward: pre-pass, dK/dV, dQ
     elif wl == "conv":
         N = args.batch
         x = torch.from_numpy(W.normal(W.seed_of(3, 0), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
