@@ -19,8 +19,9 @@
 // tf32-rounded copies (Q^T, dO^T, K^T) that a pre-pass writes together with
 // rounded copies of Q, K, V, dO and the per-row (lse * log2 e, D) pairs.
 // Three S/dP tensor-memory buffers let the MMAs of the next two tiles run
-// while the threads work on the current one.  Every wait is bounded; on
-// expiry the kernel records AMC_ERR_TIMEOUT, drains and returns.
+// while the threads work on the current one; two warpgroups share each tile,
+// one taking its first 32 columns, the other the last 32.  Every wait is
+// bounded; on expiry the kernel records AMC_ERR_TIMEOUT, drains and returns.
 #include <cmath>
 #include <mutex>
 #include <unordered_map>
@@ -37,7 +38,8 @@ namespace {
 constexpr int kD = 64;        // head dim
 constexpr int kTile = 128;    // keys (dK/dV) or queries (dQ) per CTA
 constexpr int kStream = 64;   // streamed queries (dK/dV) or keys (dQ) per step
-constexpr int kThreadsB = 224;   // warps 0-3 rows, 4 and 5 producers, 6 MMA issuer
+constexpr int kThreadsB = 352;   // warps 0-7 rows (two warpgroups), 8 and 9 producers, 10 MMA issuer
+constexpr int kRowThreads = 256;
 
 // dK/dV kernel shared memory (bytes from a 1024-aligned base)
 constexpr int kKVK = 0;                          // K tile, 2 x 16 KB (dims 0-31, 32-63)
@@ -60,11 +62,6 @@ static_assert(kKVSmem <= 232448, "dK/dV shared memory");
 static_assert(kQSmem <= 232448, "dQ shared memory");
 
 __device__ int g_attn_bwd_error;
-
-__device__ __forceinline__ uint64_t kdesc(const unsigned char* region_base, int k, int region_bytes) {
-  // K step k (8 tf32) of a K-major operand stored as 32-wide regions
-  return sdesc(smem_addr(region_base + (k / 4) * region_bytes + (k % 4) * 32), 16, 1024);
-}
 
 }  // namespace
 
@@ -155,9 +152,9 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
     mbar_init(kv_full, 1);
     for (int i = 0; i < 3; ++i) {
       mbar_init(&f_full[i], 1);
-      mbar_init(&f_empty[i], 1 + 128);
+      mbar_init(&f_empty[i], 1 + kRowThreads);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], kRowThreads);
       mbar_init(&t_free[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -176,7 +173,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
   const uint32_t tmem = *tslot;
   const uint32_t t_dv = tmem + 384, t_dk = tmem + 448;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       mbar_expect_tx(kv_full, 4 * 16384);
       for (int r = 0; r < 2; ++r) {
@@ -197,7 +194,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         bulk_load_1d(sm + kKVL + s * 512, LD + q0, 512, &f_full[s]);
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       for (int i = 0; i < nt; ++i) {
         const int b = i & 1;
@@ -211,9 +208,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         }
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == 10) {
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
+      const uint64_t dk0 = sdesc(smem_addr(sm + kKVK), 16, 1024), dv0 = sdesc(smem_addr(sm + kKVV), 16, 1024);
+      const uint64_t df0 = sdesc(smem_addr(sm + kKVF), 16, 1024), db0 = sdesc(smem_addr(sm + kKVB), 16, 1024);
       // S^T = K Q_i^T and dP^T = V dO_i^T into buffer i % 3
       auto sdp = [&](int i) -> bool {
         const int s = i % 3;
@@ -221,12 +220,12 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         if (i >= 3 && !mbar_wait(&t_free[s], (uint32_t)((i - 3) / 3) & 1u)) return false;
         tc_fence_after();
         const uint32_t ts = tmem + s * 128;
-        const unsigned char* st = sm + kKVF + s * 32768;
+        const uint64_t st = desc_add(df0, s * 32768);
 #pragma unroll
-        for (int k = 0; k < kD / 8; ++k) mma_tf32(ts, kdesc(sm + kKVK, k, 16384), kdesc(st, k, 8192), id, k > 0);
-#pragma unroll
-        for (int k = 0; k < kD / 8; ++k)
-          mma_tf32(ts + 64, kdesc(sm + kKVV, k, 16384), kdesc(st + 16384, k, 8192), id, k > 0);
+        for (int k = 0; k < kD / 8; ++k) {
+          mma_tf32(ts, desc_add(dk0, kstep_off(k, 16384)), desc_add(st, kstep_off(k, 8192)), id, k > 0);
+          mma_tf32(ts + 64, desc_add(dv0, kstep_off(k, 16384)), desc_add(st, 16384 + kstep_off(k, 8192)), id, k > 0);
+        }
         mma_commit(&s_full[s]);
         mma_commit(&f_empty[s]);
         return true;
@@ -238,11 +237,13 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         if (!mbar_wait(&b_full[b], (uint32_t)(i >> 1) & 1u)) return false;
         tc_fence_after();
         const uint32_t ts = tmem + s * 128;
-        const unsigned char* st = sm + kKVB + b * 32768;
+        const uint64_t st = desc_add(db0, b * 32768);
+        const bool acc0 = i > 0;
 #pragma unroll
-        for (int k = 0; k < kStream / 8; ++k) mma_tf32_ts(t_dv, ts + k * 8, kdesc(st + 16384, k, 8192), id, i > 0 || k > 0);
-#pragma unroll
-        for (int k = 0; k < kStream / 8; ++k) mma_tf32_ts(t_dk, ts + 64 + k * 8, kdesc(st, k, 8192), id, i > 0 || k > 0);
+        for (int k = 0; k < kStream / 8; ++k) {
+          mma_tf32_ts(t_dv, ts + k * 8, desc_add(st, 16384 + kstep_off(k, 8192)), id, acc0 || k > 0);
+          mma_tf32_ts(t_dk, ts + 64 + k * 8, desc_add(st, kstep_off(k, 8192)), id, acc0 || k > 0);
+        }
         mma_commit(&b_empty[b]);
         mma_commit(&t_free[s]);
         return true;
@@ -257,56 +258,53 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
       if (ok) mma_commit(acc_full);
       else *abort_flag = 1;
     }
-  } else if (warp < 4) {
-    // one thread per key row of the tile
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  } else if (warp < 8) {
+    // one thread per key row of the tile; warpgroup g takes columns 32g..32g+31
+    const int g = warp >> 2, t = tid & 127;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     bool ok = true;
     for (int i = 0; i < nt; ++i) {
       const int s = i % 3;
       const uint32_t ph = (uint32_t)(i / 3) & 1u;
-      ok = named_bar_and(1, 128, mbar_wait(&s_full[s], ph) && mbar_wait(&f_full[s], ph) && !*abort_flag);
+      ok = named_bar_and(1, kRowThreads, mbar_wait(&s_full[s], ph) && mbar_wait(&f_full[s], ph) && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const float2* ld = reinterpret_cast<const float2*>(sm + kKVL + s * 512);
-      const uint32_t ts = tmem + s * 128 + lane_base;
+      const float2* ld = reinterpret_cast<const float2*>(sm + kKVL + s * 512) + 32 * g;
+      const uint32_t ts = tmem + s * 128 + lane_base + 32 * g;
+      uint32_t sv[32], pv[32];
+      tmem_ld32_nowait(ts, sv);
+      tmem_ld32_nowait(ts + 64, pv);
+      tmem_ld_wait();
+      float po[32], dso[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], pv[32];
-        tmem_ld32_nowait(ts + 32 * c, sv);
-        tmem_ld32_nowait(ts + 64 + 32 * c, pv);
-        tmem_ld_wait();
-        float po[32], dso[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float2 e = ld[32 * c + j];
-          const float p = ex2_approx(fmaf(__uint_as_float(sv[j]), scale_log2, -e.x));
-          po[j] = round_tf32_int(p);
-          dso[j] = round_tf32_int(p * (__uint_as_float(pv[j]) - e.y));
-        }
-        tmem_st32(ts + 32 * c, po);
-        tmem_st32(ts + 64 + 32 * c, dso);
+      for (int j = 0; j < 32; ++j) {
+        const float2 e = ld[j];
+        const float p = ex2_approx(fmaf(__uint_as_float(sv[j]), scale_log2, -e.x));
+        po[j] = round_tf32_int(p);
+        dso[j] = round_tf32_int(p * (__uint_as_float(pv[j]) - e.y));
       }
+      tmem_st32(ts, po);
+      tmem_st32(ts + 64, dso);
       tmem_st_wait();
       mbar_arrive(&f_empty[s]);
       tc_fence_before();
       mbar_arrive(&p_full[s]);
     }
-    if (ok) ok = named_bar_and(1, 128, mbar_wait(acc_full, 0) && !*abort_flag);
+    if (ok) ok = named_bar_and(1, kRowThreads, mbar_wait(acc_full, 0) && !*abort_flag);
     if (ok) {
+      // warpgroup 0 writes the dV row, warpgroup 1 the dK row
       tc_fence_after();
-      const size_t row = (size_t)key0 + tid;
+      const size_t row = (size_t)key0 + t;
+      const float f = g ? scale : 1.f;
+      float* dst = (g ? dK : dV) + row * kD;
+      const uint32_t src = (g ? t_dk : t_dv) + lane_base;
 #pragma unroll
       for (int c = 0; c < kD; c += 32) {
         float v[32];
-        tmem_ld32(t_dv + lane_base + c, v);
-        float4* dvr = reinterpret_cast<float4*>(dV + row * kD + c);
+        tmem_ld32(src + c, v);
+        float4* o4 = reinterpret_cast<float4*>(dst + c);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) dvr[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-        tmem_ld32(t_dk + lane_base + c, v);
-        float4* dkr = reinterpret_cast<float4*>(dK + row * kD + c);
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          dkr[j] = make_float4(v[4 * j] * scale, v[4 * j + 1] * scale, v[4 * j + 2] * scale, v[4 * j + 3] * scale);
+        for (int j = 0; j < 8; ++j) o4[j] = make_float4(v[4 * j] * f, v[4 * j + 1] * f, v[4 * j + 2] * f, v[4 * j + 3] * f);
       }
     } else if (tid == 0) {
       *abort_flag = 1;
@@ -358,7 +356,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
       mbar_init(&f_full[i], 1);
       mbar_init(&f_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], kRowThreads);
       mbar_init(&t_free[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
@@ -377,7 +375,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
   const uint32_t tmem = *tslot;
   const uint32_t t_dq = tmem + 384;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       mbar_expect_tx(qd_full, 4 * 16384);
       for (int r = 0; r < 2; ++r) {
@@ -397,7 +395,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     if (lane == 0) {
       for (int j = 0; j < nt; ++j) {
         const int b = j & 1;
@@ -408,21 +406,23 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         for (int r = 0; r < 2; ++r) tma_load_2d(st + r * 8192, &mKt, j * kStream + 32 * r, bh * kD, &b_full[b]);
       }
     }
-  } else if (warp == 6) {
+  } else if (warp == 10) {
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
+      const uint64_t dq0 = sdesc(smem_addr(sm + kQQ), 16, 1024), ddo0 = sdesc(smem_addr(sm + kQdO), 16, 1024);
+      const uint64_t df0 = sdesc(smem_addr(sm + kQF), 16, 1024), db0 = sdesc(smem_addr(sm + kQB), 16, 1024);
       auto sdp = [&](int j) -> bool {
         const int s = j % 3;
         if (!mbar_wait(&f_full[s], (uint32_t)(j / 3) & 1u)) return false;
         if (j >= 3 && !mbar_wait(&t_free[s], (uint32_t)((j - 3) / 3) & 1u)) return false;
         tc_fence_after();
         const uint32_t ts = tmem + s * 128;
-        const unsigned char* st = sm + kQF + s * 32768;
+        const uint64_t st = desc_add(df0, s * 32768);
 #pragma unroll
-        for (int k = 0; k < kD / 8; ++k) mma_tf32(ts, kdesc(sm + kQQ, k, 16384), kdesc(st, k, 8192), id, k > 0);
-#pragma unroll
-        for (int k = 0; k < kD / 8; ++k)
-          mma_tf32(ts + 64, kdesc(sm + kQdO, k, 16384), kdesc(st + 16384, k, 8192), id, k > 0);
+        for (int k = 0; k < kD / 8; ++k) {
+          mma_tf32(ts, desc_add(dq0, kstep_off(k, 16384)), desc_add(st, kstep_off(k, 8192)), id, k > 0);
+          mma_tf32(ts + 64, desc_add(ddo0, kstep_off(k, 16384)), desc_add(st, 16384 + kstep_off(k, 8192)), id, k > 0);
+        }
         mma_commit(&s_full[s]);
         mma_commit(&f_empty[s]);
         return true;
@@ -433,9 +433,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         if (!mbar_wait(&b_full[b], (uint32_t)(j >> 1) & 1u)) return false;
         tc_fence_after();
         const uint32_t ts = tmem + s * 128;
-        const unsigned char* st = sm + kQB + b * 16384;
+        const uint64_t st = desc_add(db0, b * 16384);
+        const bool acc0 = j > 0;
 #pragma unroll
-        for (int k = 0; k < kStream / 8; ++k) mma_tf32_ts(t_dq, ts + 64 + k * 8, kdesc(st, k, 8192), id, j > 0 || k > 0);
+        for (int k = 0; k < kStream / 8; ++k) mma_tf32_ts(t_dq, ts + 64 + k * 8, desc_add(st, kstep_off(k, 8192)), id, acc0 || k > 0);
         mma_commit(&b_empty[b]);
         mma_commit(&t_free[s]);
         return true;
@@ -450,48 +451,44 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
       if (ok) mma_commit(acc_full);
       else *abort_flag = 1;
     }
-  } else if (warp < 4) {
-    // one thread per query row of the tile
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    const float2 e = LD[q0 + tid];
+  } else if (warp < 8) {
+    // one thread per query row of the tile; warpgroup g takes columns 32g..32g+31
+    const int g = warp >> 2, t = tid & 127;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const float2 e = LD[q0 + t];
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       const int s = j % 3;
-      ok = named_bar_and(1, 128, mbar_wait(&s_full[s], (uint32_t)(j / 3) & 1u) && !*abort_flag);
+      ok = named_bar_and(1, kRowThreads, mbar_wait(&s_full[s], (uint32_t)(j / 3) & 1u) && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const uint32_t ts = tmem + s * 128 + lane_base;
+      const uint32_t ts = tmem + s * 128 + lane_base + 32 * g;
+      uint32_t sv[32], pv[32];
+      tmem_ld32_nowait(ts, sv);
+      tmem_ld32_nowait(ts + 64, pv);
+      tmem_ld_wait();
+      float dso[32];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], pv[32];
-        tmem_ld32_nowait(ts + 32 * c, sv);
-        tmem_ld32_nowait(ts + 64 + 32 * c, pv);
-        tmem_ld_wait();
-        float dso[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float p = ex2_approx(fmaf(__uint_as_float(sv[i]), scale_log2, -e.x));
-          dso[i] = round_tf32_int(p * (__uint_as_float(pv[i]) - e.y));
-        }
-        tmem_st32(ts + 64 + 32 * c, dso);
+      for (int i = 0; i < 32; ++i) {
+        const float p = ex2_approx(fmaf(__uint_as_float(sv[i]), scale_log2, -e.x));
+        dso[i] = round_tf32_int(p * (__uint_as_float(pv[i]) - e.y));
       }
+      tmem_st32(ts + 64, dso);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[s]);
     }
-    if (ok) ok = named_bar_and(1, 128, mbar_wait(acc_full, 0) && !*abort_flag);
+    if (ok) ok = named_bar_and(1, kRowThreads, mbar_wait(acc_full, 0) && !*abort_flag);
     if (ok) {
+      // warpgroup g writes dQ columns 32g..32g+31
       tc_fence_after();
-      const size_t row = (size_t)q0 + tid;
+      const size_t row = (size_t)q0 + t;
+      float v[32];
+      tmem_ld32(t_dq + lane_base + 32 * g, v);
+      float4* dqr = reinterpret_cast<float4*>(dQ + row * kD + 32 * g);
 #pragma unroll
-      for (int c = 0; c < kD; c += 32) {
-        float v[32];
-        tmem_ld32(t_dq + lane_base + c, v);
-        float4* dqr = reinterpret_cast<float4*>(dQ + row * kD + c);
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          dqr[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale, v[4 * i + 3] * scale);
-      }
+      for (int i = 0; i < 8; ++i)
+        dqr[i] = make_float4(v[4 * i] * scale, v[4 * i + 1] * scale, v[4 * i + 2] * scale, v[4 * i + 3] * scale);
     } else if (tid == 0) {
       *abort_flag = 1;
       atomicExch(&g_attn_bwd_error, AMC_ERR_TIMEOUT);

@@ -104,12 +104,11 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
     if (!ok) break;
     tc_fence_after();
     if (tid == 0) {
+      const uint64_t qd = sdesc(smem_addr(sm + kQOff), 16, 1024);
+      const uint64_t kd = sdesc(smem_addr(sm + kKOff + b * 32768), 16, 1024);
 #pragma unroll
-      for (int k = 0; k < kD / 8; ++k) {
-        const uint64_t ad = sdesc(smem_addr(sm + kQOff + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
-        const uint64_t bd = sdesc(smem_addr(sm + kKOff + b * 32768 + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
-        mma_tf32(t_s, ad, bd, id_s, k > 0);
-      }
+      for (int k = 0; k < kD / 8; ++k)
+        mma_tf32(t_s, desc_add(qd, kstep_off(k, 16384)), desc_add(kd, kstep_off(k, 16384)), id_s, k > 0);
       mma_commit(bar_s);
     }
     ok = __syncthreads_and(mbar_wait(bar_s, (uint32_t)j & 1u));
@@ -151,12 +150,11 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
     __syncthreads();
     tc_fence_after();
     if (tid == 0) {
+      const uint64_t pd = sdesc(smem_addr(sm + kPOff), 16, 1024);
+      const uint64_t vd = sdesc(smem_addr(sm + kVOff + b * 32768), 16, 1024);
 #pragma unroll
-      for (int k = 0; k < kBN / 8; ++k) {
-        const uint64_t ad = sdesc(smem_addr(sm + kPOff + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
-        const uint64_t bd = sdesc(smem_addr(sm + kVOff + b * 32768 + (k / 4) * 8192 + (k % 4) * 32), 16, 1024);
-        mma_tf32(t_o, ad, bd, id_o, k > 0);
-      }
+      for (int k = 0; k < kBN / 8; ++k)
+        mma_tf32(t_o, desc_add(pd, kstep_off(k, 16384)), desc_add(vd, kstep_off(k, 8192)), id_o, k > 0);
       mma_commit(bar_o);
     }
     ok = __syncthreads_and(mbar_wait(bar_o, (uint32_t)j & 1u));
@@ -296,16 +294,14 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
     ok = named_bar_and(1 + g, 128, ok);
     for (int j = 0; j < ntiles && ok; ++j) {
       const int b = j & 1;
-      unsigned char* kb = sm + kKV2Off + b * 65536;
       if (!named_bar_and(1 + g, 128, mbar_wait(&full[b], (uint32_t)(j >> 1) & 1u))) { *abort_flag = 1; ok = false; break; }
       tc_fence_after();
       if (t == 0) {
+        const uint64_t qdesc = sdesc(smem_addr(qg), 16, 1024);
+        const uint64_t kvdesc = sdesc(smem_addr(sm + kKV2Off + b * 65536), 16, 1024);
 #pragma unroll
-        for (int k = 0; k < kD / 8; ++k) {
-          const uint64_t ad = sdesc(smem_addr(qg + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
-          const uint64_t bd = sdesc(smem_addr(kb + (k / 4) * 16384 + (k % 4) * 32), 16, 1024);
-          mma_tf32(t_s, ad, bd, id_s, k > 0);
-        }
+        for (int k = 0; k < kD / 8; ++k)
+          mma_tf32(t_s, desc_add(qdesc, kstep_off(k, 16384)), desc_add(kvdesc, kstep_off(k, 16384)), id_s, k > 0);
         mma_commit(&bar_s[g]);
       }
       if (!named_bar_and(1 + g, 128, mbar_wait(&bar_s[g], (uint32_t)j & 1u))) { *abort_flag = 1; ok = false; break; }
@@ -353,11 +349,11 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
       named_bar(1 + g, 128);
       tc_fence_after();
       if (t == 0) {
+        const bool acc0 = j > 0;
+        const uint64_t vdesc = sdesc(smem_addr(sm + kKV2Off + b * 65536 + 32768), 16, 1024);
 #pragma unroll
-        for (int k = 0; k < kBN / 8; ++k) {
-          const uint64_t bd = sdesc(smem_addr(kb + 32768 + (k / 4) * 8192 + (k % 4) * 32), 16, 1024);
-          mma_tf32_ts(t_o, t_s + k * 8, bd, id_o, j > 0 || k > 0);
-        }
+        for (int k = 0; k < kBN / 8; ++k)
+          mma_tf32_ts(t_o, t_s + k * 8, desc_add(vdesc, kstep_off(k, 8192)), id_o, acc0 || k > 0);
         mma_commit(&bar_o[g]);
         mma_commit(&empty[b]);
       }

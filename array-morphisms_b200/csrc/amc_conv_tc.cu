@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(128, kC, false, false);
+      const uint64_t xdesc = sdesc(smem_addr(sm + kXOff), 16, 1024), wdesc = sdesc(smem_addr(sm + kWOff), 16, 1024);
       bool ok = mbar_wait(w_full, 0);
       int li = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++li) {
@@ -117,14 +118,13 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         for (int c = 0; c < 2; ++c) {
           if (!mbar_wait(&x_full[c], (uint32_t)li & 1u)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t xbase = smem_addr(sm + kXOff + c * kRegion);
+          const uint64_t xd = desc_add(xdesc, c * kRegion), wd = desc_add(wdesc, c * 8192);
+#pragma unroll
           for (int tap = 0; tap < 9; ++tap) {
             const int kh = tap / 3, kw = tap % 3;
-            const uint32_t abase = xbase + (uint32_t)((kh * kPosRow + kw) * 128);
-            const uint32_t bbase = smem_addr(sm + kWOff + (tap * 2 + c) * 8192);
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              mma_tf32(d, sdesc(abase + k * 32, 16, 1024), sdesc(bbase + k * 32, 16, 1024), idesc,
+              mma_tf32(d, desc_add(xd, (kh * kPosRow + kw) * 128 + k * 32), desc_add(wd, tap * 2 * 8192 + k * 32), idesc,
                        (c | tap | k) != 0);
           }
           mma_commit(&x_empty[c]);
@@ -366,20 +366,22 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = idesc_tf32(128, kC, false, false);
+      const uint64_t sdesc0 = sdesc(smem_addr(sm), 16, 1024);
       bool ok = true;
       for (int c = c0, it = 0; c < c1; ++c, ++it) {
         const int st = it % kWgStages;
         if (!mbar_wait(&full[st], (uint32_t)(it / kWgStages) & 1u)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sb = smem_addr(sm + st * kWgStage);
-        for (int kw = 0; kw < 3; ++kw)
-          for (int blk = 0; blk < 2; ++blk) {
-            const uint32_t d = tmem + (uint32_t)(kw * 128 + blk * 64);
+        const uint64_t sd = desc_add(sdesc0, st * kWgStage);
+        const bool acc0 = it > 0;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_tf32(d, sdesc(sb + blk * 8192 + k * 32, 16, 1024), sdesc(sb + (3 + kw) * 8192 + k * 32, 16, 1024),
-                       idesc, it > 0 || k > 0);
-          }
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int kw = 0; kw < 3; ++kw)
+#pragma unroll
+            for (int blk = 0; blk < 2; ++blk)
+              mma_tf32(tmem + (uint32_t)(kw * 128 + blk * 64), desc_add(sd, blk * 8192 + k * 32),
+                       desc_add(sd, (3 + kw) * 8192 + k * 32), idesc, acc0 || k > 0);
         mma_commit(&empty[st]);
       }
       if (!ok) *abort_flag = 1;

@@ -208,6 +208,17 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, ui
   return d;
 }
 
+// Byte offset of K step k (8 tf32 = 32 bytes) in a K-major operand stored as
+// 32-column (128-byte) regions of region_bytes each.
+__host__ __device__ constexpr uint32_t kstep_off(int k, int region_bytes) {
+  return (uint32_t)((k / 4) * region_bytes + (k % 4) * 32);
+}
+// Descriptor of the operand `off` bytes past the one `d` describes: the start
+// address field counts 16-byte units and shared addresses stay below 2^18, so
+// the addition never carries out of the field.  Issuing threads precompute one
+// base descriptor and add constants, which keeps the per-MMA issue cost low.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t off) { return d + (uint64_t)(off >> 4); }
+
 // Instruction descriptor for kind::tf32 with f32 accumulation.
 __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                        // D format f32
