@@ -38,7 +38,7 @@ namespace {
 constexpr int kD = 64;        // head dim
 constexpr int kTile = 128;    // keys (dK/dV) or queries (dQ) per CTA
 constexpr int kStream = 64;   // streamed queries (dK/dV) or keys (dQ) per step
-constexpr int kThreadsB = 352;   // warps 0-7 rows (two warpgroups), 8 and 9 producers, 10 MMA issuer
+constexpr int kThreadsB = 384;   // warps 0-7 rows (two warpgroups), 8 and 9 producers, 10 and 11 MMA issuers
 constexpr int kRowThreads = 256;
 
 // dK/dV kernel shared memory (bytes from a 1024-aligned base)
@@ -208,7 +208,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         }
       }
     }
-  } else if (warp == 10) {
+  } else if (warp >= 10) {
+    // warp 10 issues the S/dP products, warp 11 the accumulating ones
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
       const uint64_t dk0 = sdesc(smem_addr(sm + kKVK), 16, 1024), dv0 = sdesc(smem_addr(sm + kKVV), 16, 1024);
@@ -248,15 +249,15 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         mma_commit(&t_free[s]);
         return true;
       };
-      bool ok = mbar_wait(kv_full, 0);
-      if (ok) ok = sdp(0);
-      if (ok && nt > 1) ok = sdp(1);
-      for (int i = 0; i < nt && ok; ++i) {
-        ok = dvdk(i);
-        if (ok && i + 2 < nt) ok = sdp(i + 2);
+      bool ok = true;
+      if (warp == 10) {
+        ok = mbar_wait(kv_full, 0);
+        for (int i = 0; i < nt && ok && !*abort_flag; ++i) ok = sdp(i);
+      } else {
+        for (int i = 0; i < nt && ok && !*abort_flag; ++i) ok = dvdk(i);
+        if (ok) mma_commit(acc_full);
       }
-      if (ok) mma_commit(acc_full);
-      else *abort_flag = 1;
+      if (!ok) *abort_flag = 1;
     }
   } else if (warp < 8) {
     // one thread per key row of the tile; warpgroup g takes columns 32g..32g+31
@@ -406,7 +407,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         for (int r = 0; r < 2; ++r) tma_load_2d(st + r * 8192, &mKt, j * kStream + 32 * r, bh * kD, &b_full[b]);
       }
     }
-  } else if (warp == 10) {
+  } else if (warp >= 10) {
+    // warp 10 issues the S/dP products, warp 11 the accumulating ones
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
       const uint64_t dq0 = sdesc(smem_addr(sm + kQQ), 16, 1024), ddo0 = sdesc(smem_addr(sm + kQdO), 16, 1024);
@@ -441,15 +443,15 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         mma_commit(&t_free[s]);
         return true;
       };
-      bool ok = mbar_wait(qd_full, 0);
-      if (ok) ok = sdp(0);
-      if (ok && nt > 1) ok = sdp(1);
-      for (int j = 0; j < nt && ok; ++j) {
-        ok = dq(j);
-        if (ok && j + 2 < nt) ok = sdp(j + 2);
+      bool ok = true;
+      if (warp == 10) {
+        ok = mbar_wait(qd_full, 0);
+        for (int j = 0; j < nt && ok && !*abort_flag; ++j) ok = sdp(j);
+      } else {
+        for (int j = 0; j < nt && ok && !*abort_flag; ++j) ok = dq(j);
+        if (ok) mma_commit(acc_full);
       }
-      if (ok) mma_commit(acc_full);
-      else *abort_flag = 1;
+      if (!ok) *abort_flag = 1;
     }
   } else if (warp < 8) {
     // one thread per query row of the tile; warpgroup g takes columns 32g..32g+31

@@ -193,48 +193,63 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
-// ------------------------------------------------------------------ two-warpgroup kernel
-// 256 query rows per CTA in two warpgroups (128 rows each) that share the K
-// and V^T tiles; warp 8 is the TMA producer.  Each warpgroup runs its own
-// S -> softmax -> P V chain, so one group's softmax overlaps the other's
-// tensor-core work.  P is written back over S in tensor memory (rounded to
-// tf32) and is the A operand of the P V product straight from TMEM.
-// A K/V buffer is released to the producer by a tcgen05.commit from each
-// warpgroup once its MMAs on that buffer have completed.
+// ------------------------------------------------------------------ two-group kernel, one MMA warp
+// 256 query rows per CTA in two groups of 128 (warpgroups 0 and 1, one
+// thread per row) that share the K and V^T tiles.  Warp 8 loads Q and K,
+// warp 10 loads V^T, warp 9 alone issues the tensor-core work, in the order
+//   S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) PV1(1) S1(2) | ...
+// so the next S of one group runs while the other group is in its softmax.
+// S_g(j+1) is issued into the columns that hold P_g(j) right after PV_g(j):
+// the MMAs of one thread execute in issue order.  P is written back over S
+// (rounded to tf32) and is the A operand of P V straight from tensor memory;
+// O accumulates in tensor memory.  The running maximum is raised lazily
+// (only when a score exceeds it by more than 2^8), and O is rescaled in place
+// then, after that group's previous P V product has completed.  The decision
+// is taken per warp, so the warp-collective tensor-memory accesses stay
+// convergent.
 namespace {
-constexpr int kQ2Off = 0;                        // 2 groups x 2 x 16 KB
-constexpr int kKV2Off = 2 * 32768;               // 2 bufs x (K 32 KB + V^T 32 KB)
-constexpr int kBar2Off = kKV2Off + 2 * 65536;
-constexpr int kSmem2Bytes = kBar2Off + 256 + 1024;
-constexpr int kThreads2 = 288;
+constexpr int kQ3Off = 0;                        // 2 groups x 2 x 16 KB
+constexpr int kK3Off = 2 * 32768;                // 2 bufs x K 32 KB
+constexpr int kV3Off = kK3Off + 2 * 32768;       // 2 bufs x V^T 32 KB
+constexpr int kBar3Off = kV3Off + 2 * 32768;
+constexpr int kSmem3Bytes = kBar3Off + 256 + 1024;
+constexpr int kThreads3 = 352;
 }  // namespace
 
-__global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_constant__ CUtensorMap mQ,
+__global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_constant__ CUtensorMap mQ,
                                                               const __grid_constant__ CUtensorMap mK,
                                                               const __grid_constant__ CUtensorMap mVt,
                                                               float* __restrict__ O, float* __restrict__ lse, int n,
                                                               float scale_log2) {
-  extern __shared__ unsigned char attn2_sm_raw[];
-  unsigned char* sm = (unsigned char*)(((uintptr_t)attn2_sm_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(sm + kBar2Off);      // [2] K and V^T tile landed
-  uint64_t* empty = full + 2;                       // [2]
-  uint64_t* bar_q = full + 4;
-  uint64_t* bar_s = full + 5;                       // [2] per group
-  uint64_t* bar_o = full + 7;                       // [2] per group
-  uint32_t* tslot = (uint32_t*)(sm + kBar2Off + 128);
-  volatile int* abort_flag = (volatile int*)(sm + kBar2Off + 132);
-  const int tid = threadIdx.x, warp = tid >> 5;
+  extern __shared__ unsigned char attn3_sm_raw[];
+  unsigned char* sm = (unsigned char*)(((uintptr_t)attn3_sm_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* q_full = (uint64_t*)(sm + kBar3Off);
+  uint64_t* q_ready = q_full + 1;     // both groups rounded Q (count 256)
+  uint64_t* k_full = q_full + 2;      // [2]
+  uint64_t* k_empty = q_full + 4;     // [2]
+  uint64_t* v_full = q_full + 6;      // [2]
+  uint64_t* v_empty = q_full + 8;     // [2]
+  uint64_t* s_full = q_full + 10;     // [2] per group: S_g(j) complete
+  uint64_t* p_full = q_full + 12;     // [2] per group: P_g(j) written (count 128)
+  uint64_t* o_done = q_full + 14;     // [2] per group: P V product j complete
+  uint32_t* tslot = (uint32_t*)(sm + kBar3Off + 192);
+  volatile int* abort_flag = (volatile int*)(sm + kBar3Off + 196);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int bh = blockIdx.y;
   const int row0 = bh * n + blockIdx.x * 256;
-  const int ntiles = n / kBN;
+  const int nt = n / kBN;
   if (tid == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_ready, 256);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 2);
-      mbar_init(&bar_s[i], 1);
-      mbar_init(&bar_o[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 128);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(bar_q, 1);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -243,36 +258,93 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;
+  const uint32_t tmem = *tslot;   // S_g at g*128, O_g at 256 + g*64
 
   if (warp == 8) {
-    // ---------------- producer: TMA the (pre-rounded) K and V^T tiles
-    if ((tid & 31) == 0) {
-      mbar_expect_tx(bar_q, 4 * 16384);
+    if (lane == 0) {
+      mbar_expect_tx(q_full, 4 * 16384);
       for (int g = 0; g < 2; ++g)
-        for (int r = 0; r < 2; ++r) tma_load_2d(sm + kQ2Off + g * 32768 + r * 16384, &mQ, 32 * r, row0 + g * 128, bar_q);
-      for (int j = 0; j < ntiles; ++j) {
+        for (int r = 0; r < 2; ++r) tma_load_2d(sm + kQ3Off + g * 32768 + r * 16384, &mQ, 32 * r, row0 + g * 128, q_full);
+      for (int j = 0; j < nt; ++j) {
         const int b = j & 1;
-        if (j >= 2 && !mbar_wait(&empty[b], (uint32_t)((j - 2) >> 1) & 1u)) {
-          *abort_flag = 1;
-          break;
-        }
+        if (j >= 2 && !mbar_wait(&k_empty[b], (uint32_t)((j - 2) >> 1) & 1u)) { *abort_flag = 1; break; }
         if (*abort_flag) break;
-        unsigned char* kb = sm + kKV2Off + b * 65536;
-        mbar_expect_tx(&full[b], 2 * 16384 + 4 * 8192);
-        for (int r = 0; r < 2; ++r) tma_load_2d(kb + r * 16384, &mK, 32 * r, bh * n + j * kBN, &full[b]);
-        for (int r = 0; r < 4; ++r) tma_load_2d(kb + 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &full[b]);
+        mbar_expect_tx(&k_full[b], 32768);
+        for (int r = 0; r < 2; ++r) tma_load_2d(sm + kK3Off + b * 32768 + r * 16384, &mK, 32 * r, bh * n + j * kBN, &k_full[b]);
       }
     }
-  } else {
-    // ---------------- consumer warpgroup g
-    const int g = tid >> 7, t = tid & 127;
+  } else if (warp == 10) {
+    if (lane == 0) {
+      for (int j = 0; j < nt; ++j) {
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(&v_empty[b], (uint32_t)((j - 2) >> 1) & 1u)) { *abort_flag = 1; break; }
+        if (*abort_flag) break;
+        mbar_expect_tx(&v_full[b], 32768);
+        for (int r = 0; r < 4; ++r)
+          tma_load_2d(sm + kV3Off + b * 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &v_full[b]);
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
+      const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
+      const uint64_t qd = sdesc(smem_addr(sm + kQ3Off), 16, 1024);
+      const uint64_t kd = sdesc(smem_addr(sm + kK3Off), 16, 1024);
+      const uint64_t vd = sdesc(smem_addr(sm + kV3Off), 16, 1024);
+      auto issue_s = [&](int g, int j) {
+        const uint64_t kb = desc_add(kd, (j & 1) * 32768), qg = desc_add(qd, g * 32768);
+#pragma unroll
+        for (int k = 0; k < kD / 8; ++k)
+          mma_tf32(tmem + g * 128, desc_add(qg, kstep_off(k, 16384)), desc_add(kb, kstep_off(k, 16384)), id_s, k > 0);
+        mma_commit(&s_full[g]);
+      };
+      auto issue_pv = [&](int g, int j) {
+        const uint64_t vb = desc_add(vd, (j & 1) * 32768);
+        const bool acc0 = j > 0;
+#pragma unroll
+        for (int k = 0; k < kBN / 8; ++k)
+          mma_tf32_ts(tmem + 256 + g * 64, tmem + g * 128 + k * 8, desc_add(vb, kstep_off(k, 8192)), id_o,
+                      acc0 || k > 0);
+        mma_commit(&o_done[g]);
+      };
+      bool ok = mbar_wait(q_ready, 0) && mbar_wait(&k_full[0], 0);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        issue_s(1, 0);
+        mma_commit(&k_empty[0]);
+      }
+      for (int j = 0; j < nt && ok; ++j) {
+        const int b = j & 1;
+        const bool more = j + 1 < nt;
+        if (!mbar_wait(&v_full[b], (uint32_t)(j >> 1) & 1u) || !mbar_wait(&p_full[0], (uint32_t)j & 1u)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(0, j);
+        if (more) {
+          if (!mbar_wait(&k_full[b ^ 1], (uint32_t)((j + 1) >> 1) & 1u)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(0, j + 1);
+        }
+        if (!mbar_wait(&p_full[1], (uint32_t)j & 1u)) { ok = false; break; }
+        tc_fence_after();
+        issue_pv(1, j);
+        mma_commit(&v_empty[b]);
+        if (more) {
+          issue_s(1, j + 1);
+          mma_commit(&k_empty[b ^ 1]);
+        }
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else if (warp < 8) {
+    // ---------------- softmax group g, one thread per query row
+    const int g = warp >> 2, t = tid & 127;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t t_s = tmem + g * 128, t_o = tmem + 256 + g * 64;
-    unsigned char* qg = sm + kQ2Off + g * 32768;
-    bool ok = mbar_wait(bar_q, 0);
+    const uint32_t t_s = tmem + g * 128 + lane_base, t_o = tmem + 256 + g * 64 + lane_base;
+    bool ok = mbar_wait(q_full, 0);
     if (ok) {
       // round this thread's Q row to the nearest tf32 in place (both 128 B halves)
+      unsigned char* qg = sm + kQ3Off + g * 32768;
       for (int r = 0; r < 2; ++r) {
         float4* row = reinterpret_cast<float4*>(qg + r * 16384 + t * 128);
 #pragma unroll
@@ -285,30 +357,17 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
     } else {
       *abort_flag = 1;
     }
-    const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
-    const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
-    // m: the exponent offset in use (log2 units); it is raised only when a
-    // score exceeds it by more than 8, so p = 2^(s*c - m) <= 256 and O, which
-    // accumulates in TMEM across tiles, is rescaled only on those raises.
+    mbar_arrive(q_ready);
+    // m: the exponent offset in use (log2 units), raised only when a score
+    // exceeds it by more than 8, so p = 2^(s*c - m) <= 256
     float m = -INFINITY, l = 0.f;
-    ok = named_bar_and(1 + g, 128, ok);
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int b = j & 1;
-      if (!named_bar_and(1 + g, 128, mbar_wait(&full[b], (uint32_t)(j >> 1) & 1u))) { *abort_flag = 1; ok = false; break; }
-      tc_fence_after();
-      if (t == 0) {
-        const uint64_t qdesc = sdesc(smem_addr(qg), 16, 1024);
-        const uint64_t kvdesc = sdesc(smem_addr(sm + kKV2Off + b * 65536), 16, 1024);
-#pragma unroll
-        for (int k = 0; k < kD / 8; ++k)
-          mma_tf32(t_s, desc_add(qdesc, kstep_off(k, 16384)), desc_add(kvdesc, kstep_off(k, 16384)), id_s, k > 0);
-        mma_commit(&bar_s[g]);
-      }
-      if (!named_bar_and(1 + g, 128, mbar_wait(&bar_s[g], (uint32_t)j & 1u))) { *abort_flag = 1; ok = false; break; }
+    for (int j = 0; j < nt; ++j) {
+      ok = named_bar_and(1 + g, 128, ok && mbar_wait(&s_full[g], (uint32_t)j & 1u) && !*abort_flag);
+      if (!ok) break;
       tc_fence_after();
       uint32_t sr[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + lane_base + 32 * c, sr[c]);
+      for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + 32 * c, sr[c]);
       tmem_ld_wait();
       float mraw = -INFINITY;
 #pragma unroll
@@ -316,20 +375,26 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
 #pragma unroll
         for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(sr[c][i]));
       const float mt = mraw * scale_log2;
-      if (mt > m + 8.f) {
-        const float corr = ex2_approx(m - mt);   // 0 on the first tile
-        l *= corr;
-        if (j > 0) {   // rescale the accumulated O held in TMEM
+      const bool up = mt > m + 8.f;
+      if (__any_sync(0xffffffffu, up)) {
+        const float corr = up ? ex2_approx(m - mt) : 1.f;   // 0 on the first tile
+        if (up) {
+          l *= corr;
+          m = mt;
+        }
+        if (j > 0) {
+          // O of this group may still be written by P V product j-1
+          if (!__all_sync(0xffffffffu, mbar_wait(&o_done[g], (uint32_t)(j - 1) & 1u))) *abort_flag = 1;
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < kD; c += 16) {
             float v[16];
-            tmem_ld16(t_o + lane_base + c, v);
+            tmem_ld16(t_o + c, v);
 #pragma unroll
             for (int i = 0; i < 16; ++i) v[i] *= corr;
-            tmem_st16(t_o + lane_base + c, v);
+            tmem_st16(t_o + c, v);
           }
         }
-        m = mt;
       }
       float sum = 0.f;
 #pragma unroll
@@ -341,51 +406,42 @@ __global__ void __launch_bounds__(kThreads2, 1) k_attn_fwd_tc2(const __grid_cons
           sum += p;
           v[i] = round_tf32_int(p);
         }
-        tmem_st32(t_s + lane_base + 32 * c, v);
+        tmem_st32(t_s + 32 * c, v);
       }
       tmem_st_wait();
       l += sum;
       tc_fence_before();
-      named_bar(1 + g, 128);
-      tc_fence_after();
-      if (t == 0) {
-        const bool acc0 = j > 0;
-        const uint64_t vdesc = sdesc(smem_addr(sm + kKV2Off + b * 65536 + 32768), 16, 1024);
-#pragma unroll
-        for (int k = 0; k < kBN / 8; ++k)
-          mma_tf32_ts(t_o, t_s + k * 8, desc_add(vdesc, kstep_off(k, 8192)), id_o, acc0 || k > 0);
-        mma_commit(&bar_o[g]);
-        mma_commit(&empty[b]);
-      }
-      // P (in the S columns) and O must be settled before the next tile's S
-      // product and any rescale of O
-      if (!named_bar_and(1 + g, 128, mbar_wait(&bar_o[g], (uint32_t)j & 1u))) { *abort_flag = 1; ok = false; break; }
-      tc_fence_after();
+      mbar_arrive(&p_full[g]);
     }
+    if (ok) ok = named_bar_and(1 + g, 128, mbar_wait(&o_done[g], (uint32_t)(nt - 1) & 1u) && !*abort_flag);
     if (ok) {
+      tc_fence_after();
       const float inv = 1.f / l;
       float* orow = O + (size_t)(row0 + g * 128 + t) * kD;
 #pragma unroll
       for (int c = 0; c < kD; c += 32) {
         float v[32];
-        tmem_ld32(t_o + lane_base + c, v);
+        tmem_ld32(t_o + c, v);
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(orow + c + i) = make_float4(v[i] * inv, v[i + 1] * inv, v[i + 2] * inv, v[i + 3] * inv);
       }
       if (lse) lse[row0 + g * 128 + t] = (m + log2f(l)) * 0.69314718055994530942f;
     } else if (t == 0) {
-      fail_timeout();
+      *abort_flag = 1;
     }
   }
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) {
+    if (tid == 0) fail_timeout();
     // bounded drain of anything still in flight before the memory is released
+    mbar_wait(q_full, 0, 1 << 14);
     for (int i = 0; i < 2; ++i) {
-      mbar_wait(&full[i], 0, 1 << 14);
-      mbar_wait(&bar_s[i], 0, 1 << 14);
-      mbar_wait(&bar_o[i], 0, 1 << 14);
+      mbar_wait(&k_full[i], 0, 1 << 14);
+      mbar_wait(&v_full[i], 0, 1 << 14);
+      mbar_wait(&s_full[i], 0, 1 << 14);
+      mbar_wait(&o_done[i], 0, 1 << 14);
     }
   }
   if (warp == 0) tmem_dealloc(tmem, 512);
@@ -464,10 +520,10 @@ int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, f
   static bool attr2 = false, attr1 = false;
   if (n % 256 == 0) {
     if (!attr2) {
-      AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc2, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2Bytes));
+      AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc3, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes));
       attr2 = true;
     }
-    k_attn_fwd_tc2<<<dim3(n / 256, (unsigned)blocks), kThreads2, kSmem2Bytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
+    k_attn_fwd_tc3<<<dim3(n / 256, (unsigned)blocks), kThreads3, kSmem3Bytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
   } else {
     if (!attr1) {
       AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
