@@ -270,7 +270,9 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
       ok = named_bar_and(1, kRowThreads, mbar_wait(&s_full[s], ph) && mbar_wait(&f_full[s], ph) && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      const float2* ld = reinterpret_cast<const float2*>(sm + kKVL + s * 512) + 32 * g;
+      // (lse2, D) of two query columns per 16-byte load: these broadcast loads
+      // share the shared-memory port with the tensor-core operand reads
+      const float4* ld = reinterpret_cast<const float4*>(sm + kKVL + s * 512) + 16 * g;
       const uint32_t ts = tmem + s * 128 + lane_base + 32 * g;
       uint32_t sv[32], pv[32];
       tmem_ld32_nowait(ts, sv);
@@ -278,11 +280,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
       tmem_ld_wait();
       float po[32], dso[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float2 e = ld[j];
-        const float p = ex2_approx(fmaf(__uint_as_float(sv[j]), scale_log2, -e.x));
-        po[j] = round_tf32_int(p);
-        dso[j] = round_tf32_int(p * (__uint_as_float(pv[j]) - e.y));
+      for (int j = 0; j < 32; j += 2) {
+        const float4 e = ld[j >> 1];
+        const float p0 = ex2_approx(fmaf(__uint_as_float(sv[j]), scale_log2, -e.x));
+        const float p1 = ex2_approx(fmaf(__uint_as_float(sv[j + 1]), scale_log2, -e.z));
+        po[j] = round_tf32_int(p0);
+        po[j + 1] = round_tf32_int(p1);
+        dso[j] = round_tf32_int(p0 * (__uint_as_float(pv[j]) - e.y));
+        dso[j + 1] = round_tf32_int(p1 * (__uint_as_float(pv[j + 1]) - e.w));
       }
       tmem_st32(ts, po);
       tmem_st32(ts + 64, dso);
