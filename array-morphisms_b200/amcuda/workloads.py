@@ -279,3 +279,11 @@ def conv2d_wgrad(x, dy, dw, stride: int = 1, pad: int = 1, stream=None):
 def c1_inputs_morph(dtype="f64", n=1 << 20):
     x, y = c1_inputs(dtype, n)
     return morph_from_numpy(x, dtype), morph_from_numpy(y, dtype)
+
+
+def tc_peak_tf32(iters: int = 4000, stream=None) -> float:
+    """Dense TF32 TFLOP/s reached by back-to-back tcgen05 products on this GPU
+    (amc_tc_peak_tf32): the roofline denominator of the tensor-core kernels."""
+    out = C.c_double(0.0)
+    A.call("amc_tc_peak_tf32", iters, C.byref(out), _stream(stream))
+    return out.value

@@ -164,6 +164,10 @@ struct AttnArgs {
   double scale;
 };
 int launch_attention_generic(const AttnArgs& a, cudaStream_t s);
+// Tensor-core attention forward for contiguous f32 (blocks, n, 64) operands,
+// n a multiple of 128; sets *handled = false (and launches nothing) otherwise.
+int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, float* lse, long long blocks, int n,
+                     int dk, int dv, float scale, cudaStream_t s, bool* handled);
 
 // Windowed FIR (the polyphase filter-bank reduction).
 struct FirArgs {

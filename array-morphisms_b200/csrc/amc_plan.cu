@@ -16,8 +16,15 @@
 //     in the reference's order (realization.scm:1309-1388).
 //   - im2col without padding is a strided view when the strides allow it;
 //     otherwise it, pad, col2im, stack and concat are gather kernels.
-//   - matmul / matvec / dot run the double-accumulating GEMM; attention runs
-//     the streaming-softmax kernels.
+//   - matmul / matvec / dot run the double-accumulating GEMM.
+//   - the conv pattern reshape(matmul(W, im2col(X))) on one f32 image
+//     (detect-conv2d-pattern, realization.scm:136-164) runs the convolution
+//     entry, with no column matrix: the implicit-GEMM tensor-core kernel where
+//     its shape conditions hold (TF32 operands, 2e-3 of the output scale),
+//     else the direct kernel with double accumulation.
+//   - attention of contiguous f32 operands with head dim 64 and n a multiple
+//     of 128 runs the tensor-core kernel (TF32, 2e-3); every other attention
+//     runs the streaming kernel that keeps the reference's rounding.
 //   - the polyphase filter bank (a tap reduction of a product of a windowed
 //     view and a broadcast filter) runs the streaming FIR kernel.
 #include <algorithm>
@@ -52,6 +59,14 @@ static void row_major(int32_t rank, const int64_t* shape, int64_t* strides) {
     strides[i] = s;
     s *= shape[i];
   }
+}
+
+static bool is_row_major(const View& v) {
+  int64_t st[AMC_MAX_RANK];
+  row_major(v.rank, v.shape, st);
+  for (int i = 0; i < v.rank; ++i)
+    if (v.shape[i] != 1 && v.strides[i] != st[i]) return false;
+  return true;
 }
 
 static bool same_view(const View& a, const View& b) {
@@ -471,8 +486,54 @@ struct Builder {
     return AMC_OK;
   }
 
+  // reshape(matmul(W, im2col(X))) with X one (C, H, W) f32 image: the
+  // convolution entry computes it without the column matrix.  `done` stays
+  // false (and nothing is planned) for any other tree.
+  int try_conv(const amc_node& nd, Val& out, bool& done) {
+    done = false;
+    const amc_node& mm = nodes[nd.in[0]];
+    if (mm.kind != AMC_N_MATMUL || mm.n_in != 2 || mm.in[1] < 0 || mm.in[1] >= nd.in[0]) return AMC_OK;
+    const amc_node& ic = nodes[mm.in[1]];
+    if (ic.kind != AMC_N_IM2COL || ic.n_in != 1 || nd.dtype != AMC_F32 || mm.dtype != AMC_F32 || ic.dtype != AMC_F32)
+      return AMC_OK;
+    const int32_t KH = ic.iparam[0], KW = ic.iparam[1], SH = ic.iparam[2], SW = ic.iparam[3], PH = ic.iparam[4],
+                  PW = ic.iparam[5];
+    if (KH <= 0 || KW <= 0 || SH <= 0 || SW <= 0 || PH < 0 || PW < 0) return AMC_OK;
+    View X, Wt;
+    int rc = concrete(ic.in[0], X);
+    if (!rc) rc = concrete(mm.in[0], Wt);
+    if (rc) return rc;
+    if (X.rank != 3 || Wt.rank != 2 || X.dtype != AMC_F32 || Wt.dtype != AMC_F32 || !is_row_major(X) ||
+        !is_row_major(Wt))
+      return AMC_OK;
+    const int64_t C = X.shape[0], H = X.shape[1], Wd = X.shape[2], K = Wt.shape[0];
+    if (Wt.shape[1] != C * KH * KW || C > INT32_MAX || H > INT32_MAX || Wd > INT32_MAX || K > INT32_MAX) return AMC_OK;
+    const int64_t OH = 1 + (H + 2 * PH - KH) / SH, OW = 1 + (Wd + 2 * PW - KW) / SW;
+    if (H + 2 * PH < KH || Wd + 2 * PW < KW || nd.rank != 3 || nd.shape[0] != K || nd.shape[1] != OH ||
+        nd.shape[2] != OW)
+      return AMC_OK;
+    View o;
+    rc = new_slot(AMC_F32, 3, nd.shape, {X.buf, Wt.buf}, o);
+    if (rc) return rc;
+    const float* xp = reinterpret_cast<const float*>((const char*)ptr_of(X.buf) + X.offset * 4);
+    const float* wp = reinterpret_cast<const float*>((const char*)ptr_of(Wt.buf) + Wt.offset * 4);
+    float* yp = reinterpret_cast<float*>(ptr_of(o.buf));
+    const int32_t c = (int32_t)C, h = (int32_t)H, w = (int32_t)Wd, k = (int32_t)K;
+    plan->steps.push_back([=](cudaStream_t s) {
+      return amc_conv2d_fwd_f32(xp, wp, yp, 1, c, h, w, k, KH, KW, SH, SW, PH, PW, s);
+    });
+    plan->launches += 3;   // tensor-core path: weights, padded input, kernel
+    out = Val();
+    out.view = o;
+    done = true;
+    return AMC_OK;
+  }
+
   int node_reshape(const amc_node& nd, Val& out) {
     if (nd.n_in != 1) return err(AMC_ERR_INVALID, "reshape needs one operand");
+    bool conv = false;
+    int rc0 = try_conv(nd, out, conv);
+    if (rc0 || conv) return rc0;
     Val x;
     int rc = get(nd.in[0], x);
     if (rc) return rc;
@@ -909,8 +970,20 @@ struct Builder {
     rc = new_slot(nd.dtype, nd.rank, nd.shape, {Q.buf, K.buf, V.buf}, o);
     if (rc) return rc;
     a.O = ptr_of(o.buf);
-    plan->steps.push_back([a](cudaStream_t s) { return launch_attention_generic(a, s); });
-    plan->launches += 1;
+    if (a.dtype == AMC_F32 && a.dk == 64 && a.dv == 64 && a.n >= 128 && a.n % 128 == 0 && is_row_major(Q) &&
+        is_row_major(K) && is_row_major(V)) {
+      plan->steps.push_back([a](cudaStream_t s) {
+        bool handled = false;
+        int rc = attention_fwd_tc((const float*)a.Q, (const float*)a.K, (const float*)a.V, (float*)a.O, nullptr,
+                                  a.blocks, a.n, a.dk, a.dv, (float)a.scale, s, &handled);
+        if (rc || handled) return rc;
+        return launch_attention_generic(a, s);
+      });
+      plan->launches += 3;   // V^T, K rounding, kernel
+    } else {
+      plan->steps.push_back([a](cudaStream_t s) { return launch_attention_generic(a, s); });
+      plan->launches += 1;
+    }
     out = Val();
     out.view = o;
     return AMC_OK;

@@ -449,7 +449,13 @@ def bench_other(args, ws, rank, local):
     t = max_over_ranks(ws, sum(ms))
     per = work / (sum(ms) / len(ms) / 1e3)
     scale = 1e9 if unit == "GB/s" else 1e12
-    peak = hbm if bound == "hbm" else (bf16 / 2.0)
+    if bound == "hbm":
+        peak, peak_source = hbm, kind + " hbm_gbs"
+    else:
+        # TF32 denominator measured now, on this GPU, by the library's tcgen05 probe
+        peak = W.tc_peak_tf32(4000)
+        peak_source = (f"tcgen05 kind::tf32 M=128 N=256 issue loop on this GPU (amc_tc_peak_tf32); "
+                       f"{kind} bf16/2 = {bf16 / 2.0:.1f} for context")
     if rank == 0:
         print(json.dumps({
             "metric": metric, "value": ws * work * args.steps / (t / 1e3) / scale, "unit": unit, "n_gpus": ws,
@@ -458,7 +464,7 @@ def bench_other(args, ws, rank, local):
             "data": "synthetic", "config": cfg,
             "roofline": {"bound": bound, "achieved": per / scale, "peak": peak, "unit": unit, "frac": per / scale / peak,
                          "traffic": None,
-                         "peak_source": kind + (" hbm_gbs" if bound == "hbm" else " bf16/2 as the TF32 denominator")},
+                         "peak_source": peak_source},
             "gpu_launches": launches * args.steps, "clocks": clocks}))
 
 

@@ -148,8 +148,10 @@ typedef struct amc_insn {
  *   MATVEC     2 operands (M,N)x(N)
  *   DOT        2 operands (N)x(N) -> ()
  *   ATTENTION  3 operands Q K V, fparam[0] = scale   (blas-exec.scm:334-398)
- * The planner recognises reshape(matmul(W, im2col(X))) as a convolution
- * (realization.scm:136-164). */
+ * The planner recognises reshape(matmul(W, im2col(X))) on one f32 (C, H, W)
+ * image as a convolution (detect-conv2d-pattern, realization.scm:136-164) and
+ * runs amc_conv2d_fwd_f32 on it; an ATTENTION node of contiguous f32 operands
+ * with head dim 64 and n a multiple of 128 runs the tensor-core kernel. */
 #define AMC_N_LEAF      1
 #define AMC_N_RESHAPE   2
 #define AMC_N_TRANSPOSE 3
@@ -326,6 +328,13 @@ int amc_conv2d_dgrad_f32(const float* dY, const float* W, float* dX, int32_t N, 
                          int32_t K, int32_t KH, int32_t KW, int32_t SH, int32_t SW, int32_t PH, int32_t PW, void* stream);
 int amc_conv2d_wgrad_f32(const float* X, const float* dY, float* dW, int32_t N, int32_t C, int32_t H, int32_t Wd,
                          int32_t K, int32_t KH, int32_t KW, int32_t SH, int32_t SW, int32_t PH, int32_t PW, void* stream);
+
+/* Tensor-core throughput probe (diagnostic; no reference counterpart): one
+ * CTA per SM issues `iters` x 4 back-to-back tcgen05.mma kind::tf32 products
+ * of M=128, N=256, K=8 from shared memory; *tflops receives the dense TF32
+ * rate they reached, the roofline denominator of the tensor-core kernels.
+ * Synchronizes the stream. */
+int amc_tc_peak_tf32(int32_t iters, double* tflops, void* stream);
 
 #ifdef __cplusplus
 }

@@ -181,6 +181,39 @@ def test_attention_node_matches_oracle(amc):
         assert np.max(np.abs(got.astype(np.float64) - ref)) <= tol * np.max(np.abs(ref))
 
 
+def test_attention_node_tensor_core_shape(amc):
+    """A contiguous f32 attention with head dim 64 and n % 128 == 0 plans the
+    tcgen05 kernel (TF32 operands): within 2e-3 of the output scale."""
+    rng = np.random.default_rng(18)
+    q, k, v = (rng.standard_normal((1, 2, 256, 64)).astype(np.float32) for _ in range(3))
+    e = amc.attention_morphism(amc.morph_from_numpy(q), amc.morph_from_numpy(k), amc.morph_from_numpy(v))
+    plan = amc.Plan(e)
+    assert plan.stats()["launches"] == 3
+    plan.execute()
+    got, ref = plan.result().values(), oracle.realize(e).values()
+    assert np.max(np.abs(got.astype(np.float64) - ref)) <= 2e-3 * np.max(np.abs(ref))
+
+
+@pytest.mark.parametrize("C,H,W,K,ksz,stride,pad,tol", [
+    (64, 16, 16, 64, 3, 1, 1, 2e-3),     # implicit-GEMM tensor-core kernel (TF32)
+    (3, 9, 7, 5, 3, 2, 1, 1e-6),         # direct kernel, double accumulation
+    (2, 6, 6, 4, 2, 1, 0, 1e-6),
+])
+def test_conv_pattern_lowering(amc, C, H, W, K, ksz, stride, pad, tol):
+    """reshape(matmul(W, im2col(X))) on one image is planned as a convolution
+    (detect-conv2d-pattern, realization.scm:136-164), no column matrix."""
+    rng = np.random.default_rng(19)
+    x = rng.standard_normal((C, H, W)).astype(np.float32)
+    w = (rng.standard_normal((K, C * ksz * ksz)) * np.sqrt(2.0 / (C * ksz * ksz))).astype(np.float32)
+    oh, ow = 1 + (H + 2 * pad - ksz) // stride, 1 + (W + 2 * pad - ksz) // stride
+    e = amc.morph_reshape(amc.morph_matmul(amc.morph_from_numpy(w),
+                                           amc.im2col_morph(amc.morph_from_numpy(x), ksz, stride, pad)), (K, oh, ow))
+    got = np.asarray(amc.realize(e).values(), np.float64)
+    ref = np.asarray(oracle.realize(e).values(), np.float64)
+    assert got.shape == (K, oh, ow)
+    assert np.max(np.abs(got - ref)) <= tol * np.max(np.abs(ref))
+
+
 def test_plan_rejects_bad_trees(amc):
     a = amc.morph_from_numpy(np.zeros((4, 4)))
     with pytest.raises(ValueError):

@@ -249,3 +249,11 @@ def test_conv_entry_points(amc, N, Cc, H, Wd, K):
     rdw = oracle.conv2d_wgrad(x, dy, w.shape)
     e = np.max(np.abs(dw.cpu().numpy() - rdw)) / np.max(np.abs(rdw))
     assert e <= 2e-3, e
+
+
+def test_tc_peak_probe(amc):
+    """The tcgen05 TF32 throughput probe returns a plausible dense rate (the
+    nominal dense TF32 figure of a B200 is about 1.1 PFLOP/s)."""
+    from amcuda import workloads as W
+    v = W.tc_peak_tf32(2000)
+    assert 300.0 < v < 3000.0, v
