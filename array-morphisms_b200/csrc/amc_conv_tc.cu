@@ -17,10 +17,13 @@
 //   - B is the tap's (64 out x 64 in) weight block, K-major, resident in
 //     shared memory for the whole kernel;
 //   - 72 MMAs (9 taps x 64 channels / 8) accumulate one 128 x 64 f32 tile in
-//     tensor memory; two accumulators alternate so the epilogue of one tile
-//     overlaps the MMAs of the next.
+//     tensor memory, issued by two warps (one per 32-channel chunk, 36 each,
+//     into separate accumulators the epilogue adds): one issuing thread
+//     cannot keep the tensor pipe fed with N=64 products.  Two accumulator
+//     pairs alternate so the epilogue of one tile overlaps the MMAs of the
+//     next.
 // Output columns 56..63 of a tile are computed on zero padding and dropped.
-// Warp roles: warp 0 producer, warp 1 MMA issuer, warps 4-7 epilogue.
+// Warp roles: warp 0 producer, warps 1-2 MMA issuers, warps 4-7 epilogue.
 #include <cudaTypedefs.h>
 
 #include "amc_internal.h"
@@ -70,14 +73,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
     for (int i = 0; i < 2; ++i) {
       mbar_init(&x_full[i], 1);
       mbar_init(&x_empty[i], 1);
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], 2);   // one commit from each chunk's MMA warp
       mbar_init(&acc_empty[i], 1);
     }
     *abort_flag = 0;
     mbar_fence_init();
   }
   __syncthreads();
-  if (warp == 0) tmem_alloc(tslot, 128);
+  if (warp == 0) tmem_alloc(tslot, 256);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -104,33 +107,33 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
         if (*abort_flag) break;
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == 2) {
+    // warp 1 + c issues the products of input-channel chunk c into its own
+    // accumulator (tensor memory a * 128 + c * 64); the epilogue adds the two
     if (lane == 0) {
+      const int c = warp - 1;
       const uint32_t idesc = idesc_tf32(128, kC, false, false);
-      const uint64_t xdesc = sdesc(smem_addr(sm + kXOff), 16, 1024), wdesc = sdesc(smem_addr(sm + kWOff), 16, 1024);
+      const uint64_t xd = sdesc(smem_addr(sm + kXOff + c * kRegion), 16, 1024);
+      const uint64_t wd = sdesc(smem_addr(sm + kWOff + c * 8192), 16, 1024);
       bool ok = mbar_wait(w_full, 0);
       int li = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++li) {
         const int a = li & 1;
         if (li >= 2 && !mbar_wait(&acc_empty[a], (uint32_t)((li - 2) >> 1) & 1u)) { ok = false; break; }
+        if (!mbar_wait(&x_full[c], (uint32_t)li & 1u)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t d = tmem + a * kC;
-        for (int c = 0; c < 2; ++c) {
-          if (!mbar_wait(&x_full[c], (uint32_t)li & 1u)) { ok = false; break; }
-          tc_fence_after();
-          const uint64_t xd = desc_add(xdesc, c * kRegion), wd = desc_add(wdesc, c * 8192);
+        const uint32_t d = tmem + a * 2 * kC + c * kC;
 #pragma unroll
-          for (int tap = 0; tap < 9; ++tap) {
-            const int kh = tap / 3, kw = tap % 3;
+        for (int tap = 0; tap < 9; ++tap) {
+          const int kh = tap / 3, kw = tap % 3;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma_tf32(d, desc_add(xd, (kh * kPosRow + kw) * 128 + k * 32), desc_add(wd, tap * 2 * 8192 + k * 32), idesc,
-                       (c | tap | k) != 0);
-          }
-          mma_commit(&x_empty[c]);
+          for (int k = 0; k < 4; ++k)
+            mma_tf32(d, desc_add(xd, (kh * kPosRow + kw) * 128 + k * 32), desc_add(wd, tap * 2 * 8192 + k * 32), idesc,
+                     (tap | k) != 0);
         }
-        if (!ok) break;
+        mma_commit(&x_empty[c]);
         mma_commit(&acc_full[a]);
+        if (*abort_flag) break;
       }
       if (!ok) *abort_flag = 1;
     }
@@ -147,8 +150,14 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
       if (!ok) break;
       tc_fence_after();
       float v[2][32];
-      tmem_ld32(tmem + a * kC + lane_base, v[0]);
-      tmem_ld32(tmem + a * kC + lane_base + 32, v[1]);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float u[32];
+        tmem_ld32(tmem + a * 2 * kC + lane_base + 32 * h, v[h]);
+        tmem_ld32(tmem + a * 2 * kC + kC + lane_base + 32 * h, u);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[h][i] += u[i];
+      }
       tc_fence_before();
       named_bar(1, 128);
       if (q == 0) mbar_arrive(&acc_empty[a]);
@@ -169,7 +178,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
       mbar_wait(&acc_full[i], 0, 1 << 14);
     }
   }
-  if (warp == 0) tmem_dealloc(tmem, 128);
+  if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // NCHW (N, 64, H, W) -> zero-bordered NHWC (N, H+2, W+2, 64), rounded to tf32.
@@ -308,11 +317,12 @@ int conv_dgrad_tc(const float* dY, const float* W, float* dX, const ConvShape& s
 // row shift is a TMA coordinate offset of W elements, zero-filled out of
 // range).  The reference's order is a batch sum of per-image GEMMs
 // dY_n . im2col(X_n)^T; here the position sum is split across CTAs and the
-// CTA partials are added in CTA order by a second kernel.
+// CTA partials are added in a fixed order by a second kernel.
 // Per K-chunk of 32 positions a stage holds A = dY rows for kh = 0, 1, 2
 // (3 x 64 rows, K-major) and B = X_kw for kw = 0, 1, 2 (3 x 64 rows).  For
 // each kw two M=128 MMAs cover the kh rows (0,1) and (1,2); their 64-column
-// accumulators live in tensor memory for the CTA's whole chunk range.
+// accumulators live in tensor memory for the CTA's whole chunk range.  Warp
+// 1 + kw issues the products of column tap kw.
 namespace {
 constexpr int kWgStage = 6 * 8192;        // 3 A blocks + 3 B blocks of 64 rows x 128 B
 constexpr int kWgStages = 4;
@@ -338,9 +348,9 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   if (tid == 0) {
     for (int i = 0; i < kWgStages; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], 3);   // one commit from each column tap's MMA warp
     }
-    mbar_init(done, 1);
+    mbar_init(done, 3);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -363,8 +373,10 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
           tma_load_2d(sb + (3 + kw) * 8192, &mXk, q0, (kw * N + n) * kC, &full[st]);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp >= 1 && warp <= 3) {
+    // warp 1 + kw issues the two products of column tap kw (its own accumulators)
     if (lane == 0) {
+      const int kw = warp - 1;
       const uint32_t idesc = idesc_tf32(128, kC, false, false);
       const uint64_t sdesc0 = sdesc(smem_addr(sm), 16, 1024);
       bool ok = true;
@@ -377,12 +389,11 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
 #pragma unroll
         for (int k = 0; k < 4; ++k)
 #pragma unroll
-          for (int kw = 0; kw < 3; ++kw)
-#pragma unroll
-            for (int blk = 0; blk < 2; ++blk)
-              mma_tf32(tmem + (uint32_t)(kw * 128 + blk * 64), desc_add(sd, blk * 8192 + k * 32),
-                       desc_add(sd, (3 + kw) * 8192 + k * 32), idesc, acc0 || k > 0);
+          for (int blk = 0; blk < 2; ++blk)
+            mma_tf32(tmem + (uint32_t)(kw * 128 + blk * 64), desc_add(sd, blk * 8192 + k * 32),
+                     desc_add(sd, (3 + kw) * 8192 + k * 32), idesc, acc0 || k > 0);
         mma_commit(&empty[st]);
+        if (*abort_flag) break;
       }
       if (!ok) *abort_flag = 1;
       mma_commit(done);
@@ -415,30 +426,50 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// dW = sum of the CTA partials in CTA order (zero for CTAs without chunks).
+// dW = sum of the CTA partials in a fixed order (CTAs without chunks add
+// nothing): eight interleaved running sums (partial p goes to sum p % 8), then
+// the eight in index order, so the loads are independent and the result does
+// not depend on timing.
 __global__ void k_wgrad_reduce(const float* __restrict__ partials, float* __restrict__ dW, int nparts, const int* counts) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= kC * kC * 9) return;
-  float s = 0.f;
-  for (int p = 0; p < nparts; ++p)
-    if (counts[p]) s += partials[(size_t)p * kC * kC * 9 + i];
-  dW[i] = s;
+  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int p = 0;
+  for (; p + 8 <= nparts; p += 8) {
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (counts[p + u]) s[u] += __ldg(partials + (size_t)(p + u) * kC * kC * 9 + i);
+  }
+  for (int u = 0; p < nparts; ++p, ++u)
+    if (counts[p]) s[u] += __ldg(partials + (size_t)p * kC * kC * 9 + i);
+  dW[i] = ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
 }
 
 // X (N, 64, H, W) -> X_kw (3, N, 64, H*W), X_kw[.., h, w] = X[.., h, w + kw - 1] (0 outside),
-// and dY -> rounded copy; all rounded to the nearest tf32.
+// and dY -> rounded copy; all rounded to the nearest tf32.  One thread per 4
+// consecutive columns of one row (W % 4 == 0): 16-byte loads and stores, the
+// neighbouring columns from the adjacent vectors of the same row.
 __global__ void k_wgrad_prep(const float* __restrict__ X, const float* __restrict__ dY, float* __restrict__ Xk,
                              float* __restrict__ dYr, long long plane_elems, int Wd) {
-  const long long total = plane_elems;   // N * 64 * H * W
+  const long long total4 = plane_elems / 4;
+  const int w4 = Wd / 4;
+  const float4* X4 = reinterpret_cast<const float4*>(X);
+  float4* K0 = reinterpret_cast<float4*>(Xk);
+  float4* K1 = K0 + total4;
+  float4* K2 = K1 + total4;
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (; i < total; i += stride) {
-    const int w = (int)(i % Wd);
-    const float x = X[i];
-    Xk[total + i] = round_tf32(x);
-    Xk[i] = w > 0 ? round_tf32(X[i - 1]) : 0.f;                // kw = 0: X[w - 1]
-    Xk[2 * total + i] = w < Wd - 1 ? round_tf32(X[i + 1]) : 0.f;  // kw = 2: X[w + 1]
-    dYr[i] = round_tf32(dY[i]);
+  for (; i < total4; i += stride) {
+    const int q = (int)(i % w4);   // vector index within the row
+    const float4 c = X4[i];
+    const float left = q > 0 ? X[4 * i - 1] : 0.f;
+    const float right = q < w4 - 1 ? X[4 * i + 4] : 0.f;
+    const float4 r = make_float4(round_tf32(c.x), round_tf32(c.y), round_tf32(c.z), round_tf32(c.w));
+    K1[i] = r;
+    K0[i] = make_float4(round_tf32(left), r.x, r.y, r.z);       // kw = 0: X[w - 1]
+    K2[i] = make_float4(r.y, r.z, r.w, round_tf32(right));      // kw = 2: X[w + 1]
+    const float4 g = reinterpret_cast<const float4*>(dY)[i];
+    reinterpret_cast<float4*>(dYr)[i] = make_float4(round_tf32(g.x), round_tf32(g.y), round_tf32(g.z), round_tf32(g.w));
   }
 }
 
