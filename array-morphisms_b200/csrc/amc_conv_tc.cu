@@ -57,19 +57,19 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
                                                                float* __restrict__ Y, int N, int H, int Wd) {
   extern __shared__ unsigned char conv_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)conv_sm_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* w_full = (uint64_t*)(sm + kBarOffC);
-  uint64_t* x_full = w_full + 1;      // [2] per channel chunk
-  uint64_t* x_empty = w_full + 3;     // [2]
-  uint64_t* acc_full = w_full + 5;    // [2] per accumulator
-  uint64_t* acc_empty = w_full + 7;   // [2]
-  uint32_t* tslot = (uint32_t*)(sm + kBarOffC + 128);
-  volatile int* abort_flag = (volatile int*)(sm + kBarOffC + 132);
+  uint64_t* x_full = (uint64_t*)(sm + kBarOffC);   // [2] per channel chunk
+  uint64_t* x_empty = x_full + 2;     // [2]
+  uint64_t* acc_full = x_full + 4;    // [2] per accumulator
+  uint64_t* acc_empty = x_full + 6;   // [2]
+  uint64_t* w_full = x_full + 8;      // [9] per tap: both channel chunks of its weights
+  uint32_t* tslot = (uint32_t*)(sm + kBarOffC + 192);
+  volatile int* abort_flag = (volatile int*)(sm + kBarOffC + 196);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pairs = H / 2;
   const int ntiles = N * pairs;
   const int Hp = H + 2;
   if (tid == 0) {
-    mbar_init(w_full, 1);
+    for (int t = 0; t < 9; ++t) mbar_init(&w_full[t], 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&x_full[i], 1);
       mbar_init(&x_empty[i], 1);
@@ -88,9 +88,6 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
 
   if (warp == 0) {
     if (lane == 0) {
-      // weights once: 18 boxes of (32 in-channels x 64 out-channels)
-      mbar_expect_tx(w_full, 18 * 8192);
-      for (int i = 0; i < 18; ++i) tma_load_2d(sm + kWOff + i * 8192, &mW, 0, i * 64, w_full);
       int li = 0;
       for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++li) {
         const int n = tile / pairs, oh0 = (tile % pairs) * 2;
@@ -104,6 +101,15 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
               ::"r"(smem_addr(sm + kXOff + c * kRegion)), "l"((uint64_t)&mX), "r"(32 * c), "r"(0), "r"(row),
                 "r"(smem_addr(&x_full[c])) : "memory");
         }
+        if (li == 0) {
+          // the weights once, after the first input tile and tap by tap (boxes
+          // of 32 in-channels x 64 out-channels), so the first products start
+          // as soon as their tap has landed
+          for (int t = 0; t < 9; ++t) {
+            mbar_expect_tx(&w_full[t], 2 * 8192);
+            for (int c = 0; c < 2; ++c) tma_load_2d(sm + kWOff + (2 * t + c) * 8192, &mW, 0, (2 * t + c) * 64, &w_full[t]);
+          }
+        }
         if (*abort_flag) break;
       }
     }
@@ -115,7 +121,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
       const uint32_t idesc = idesc_tf32(128, kC, false, false);
       const uint64_t xd = sdesc(smem_addr(sm + kXOff + c * kRegion), 16, 1024);
       const uint64_t wd = sdesc(smem_addr(sm + kWOff + c * 8192), 16, 1024);
-      bool ok = mbar_wait(w_full, 0);
+      bool ok = true;
       int li = 0;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++li) {
         const int a = li & 1;
@@ -126,6 +132,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
 #pragma unroll
         for (int tap = 0; tap < 9; ++tap) {
           const int kh = tap / 3, kw = tap % 3;
+          if (li == 0) {
+            if (!mbar_wait(&w_full[tap], 0)) ok = false;
+            tc_fence_after();
+          }
 #pragma unroll
           for (int k = 0; k < 4; ++k)
             mma_tf32(d, desc_add(xd, (kh * kPosRow + kw) * 128 + k * 32), desc_add(wd, tap * 2 * 8192 + k * 32), idesc,
@@ -177,6 +187,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
       mbar_wait(&x_full[i], 0, 1 << 14);
       mbar_wait(&acc_full[i], 0, 1 << 14);
     }
+    for (int t = 0; t < 9; ++t) mbar_wait(&w_full[t], 0, 1 << 14);
   }
   if (warp == 0) tmem_dealloc(tmem, 256);
 }
@@ -328,6 +339,7 @@ constexpr int kWgStage = 6 * 8192;        // 3 A blocks + 3 B blocks of 64 rows 
 constexpr int kWgStages = 4;
 constexpr int kWgBarOff = kWgStages * kWgStage;
 constexpr int kWgSmem = kWgBarOff + 256 + 1024;
+constexpr int kWgPart = 3 * 2 * 128 * kC;   // floats of one CTA's partial: [kw][block][lane][64]
 }  // namespace
 
 __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant__ CUtensorMap mDY,
@@ -404,17 +416,19 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
     const bool ok = named_bar_and(1, 128, mbar_wait(done, 0) && !*abort_flag);
     if (ok && c1 > c0) {
       tc_fence_after();
-      // lanes 0-63 of block 0 are kh=0, 64-127 kh=1; block 1 lanes 64-127 are kh=2
-      float* part = partials + (size_t)blockIdx.x * (kC * kC * 9);
+      // lanes 0-63 of block 0 are kh=0, 64-127 kh=1; block 1 lanes 64-127 are
+      // kh=2.  Partials keep the tensor-memory layout [kw][block][lane][64],
+      // so each thread writes its row's 64 values contiguously.
+      float* part = partials + (size_t)blockIdx.x * kWgPart;
       for (int kw = 0; kw < 3; ++kw)
         for (int blk = 0; blk < 2; ++blk) {
-          if (blk == 1 && row < 64) continue;   // duplicate of kh=1
-          const int kh = blk == 0 ? (row < 64 ? 0 : 1) : 2, co = row & 63;
+          if (blk == 1 && row < 64) continue;   // duplicate of kh=1 (whole warps 4 and 5)
+          float4* dst = reinterpret_cast<float4*>(part + ((size_t)(kw * 2 + blk) * 128 + row) * kC);
           for (int half = 0; half < 2; ++half) {
             float v[32];
             tmem_ld32(tmem + (uint32_t)(kw * 128 + blk * 64 + half * 32) + lane_base, v);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) part[(((size_t)co * kC + half * 32 + i) * 3 + kh) * 3 + kw] = v[i];
+            for (int i = 0; i < 8; ++i) dst[half * 8 + i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           }
         }
     } else if (!ok && row == 0) {
@@ -427,22 +441,26 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
 }
 
 // dW = sum of the CTA partials in a fixed order (CTAs without chunks add
-// nothing): eight interleaved running sums (partial p goes to sum p % 8), then
-// the eight in index order, so the loads are independent and the result does
-// not depend on timing.
-__global__ void k_wgrad_reduce(const float* __restrict__ partials, float* __restrict__ dW, int nparts, const int* counts) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= kC * kC * 9) return;
-  float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  int p = 0;
-  for (; p + 8 <= nparts; p += 8) {
-#pragma unroll
-    for (int u = 0; u < 8; ++u)
-      if (counts[p + u]) s[u] += __ldg(partials + (size_t)(p + u) * kC * kC * 9 + i);
-  }
-  for (int u = 0; p < nparts; ++p, ++u)
-    if (counts[p]) s[u] += __ldg(partials + (size_t)p * kC * kC * 9 + i);
-  dW[i] = ((s[0] + s[1]) + (s[2] + s[3])) + ((s[4] + s[5]) + (s[6] + s[7]));
+// nothing).  A block takes 32 outputs (consecutive in-channels of one
+// (kw, kh, out-channel)) and 8 groups of partials: group g adds partials
+// g, g+8, ... in ascending order, then the 8 group sums are added in index
+// order, so the result does not depend on timing.
+__global__ void __launch_bounds__(256) k_wgrad_reduce(const float* __restrict__ partials, float* __restrict__ dW,
+                                                      int nparts, const int* counts) {
+  __shared__ float red[8][33];
+  const int l = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int o = blockIdx.x * 32 + l;   // (kw, kh, co, ci), ci fastest
+  const int ci = o & 63, co = (o >> 6) & 63, kh = (o >> 12) % 3, kw = (o >> 12) / 3;
+  const int blk = kh == 2 ? 1 : 0, lane = kh == 2 ? 64 + co : kh * 64 + co;
+  const size_t off = ((size_t)(kw * 2 + blk) * 128 + lane) * kC + ci;
+  float s = 0.f;
+  for (int p = g; p < nparts; p += 8)
+    if (counts[p]) s += __ldg(partials + (size_t)p * kWgPart + off);
+  red[g][l] = s;
+  __syncthreads();
+  if (g == 0)
+    dW[((co * kC + ci) * 3 + kh) * 3 + kw] =
+        ((red[0][l] + red[1][l]) + (red[2][l] + red[3][l])) + ((red[4][l] + red[5][l]) + (red[6][l] + red[7][l]));
 }
 
 // X (N, 64, H, W) -> X_kw (3, N, 64, H*W), X_kw[.., h, w] = X[.., h, w + kw - 1] (0 outside),
@@ -479,14 +497,14 @@ int conv_wgrad_tc(const float* X, const float* dY, float* dW, const ConvShape& s
   if (!*handled) return AMC_OK;
   const long long plane = (long long)s.N * kC * s.H * s.W;
   const int nsm = num_sms();
-  const size_t part_bytes = (size_t)nsm * kC * kC * 9 * sizeof(float);
+  const size_t part_bytes = (size_t)nsm * kWgPart * sizeof(float);
   void* scratch = nullptr;
   int rc = conv_scratch((size_t)plane * 4 * sizeof(float) + part_bytes + 4096, &scratch);
   if (rc) return rc;
   float* Xk = (float*)scratch;
   float* dYr = Xk + 3 * plane;
   float* parts = dYr + plane;
-  int* counts = (int*)(parts + (size_t)nsm * kC * kC * 9);
+  int* counts = (int*)(parts + (size_t)nsm * kWgPart);
   k_wgrad_prep<<<nsm * 8, 256, 0, st>>>(X, dY, Xk, dYr, plane, s.W);
   AMC_CUDA(cudaGetLastError());
   const int HW = s.H * s.W, cpi = HW / 32, total = s.N * cpi;
@@ -506,7 +524,7 @@ int conv_wgrad_tc(const float* X, const float* dY, float* dW, const ConvShape& s
   }
   k_conv_wgrad_tc<<<grid, 256, kWgSmem, st>>>(mDY, mXk, parts, s.N, HW, s.W, cpi);
   AMC_CUDA(cudaGetLastError());
-  k_wgrad_reduce<<<(kC * kC * 9 + 255) / 256, 256, 0, st>>>(parts, dW, grid, counts);
+  k_wgrad_reduce<<<kC * kC * 9 / 32, 256, 0, st>>>(parts, dW, grid, counts);
   AMC_CUDA(cudaGetLastError());
   return AMC_OK;
 }
