@@ -1,11 +1,12 @@
 // Tensor-core throughput probe: the TF32 roofline denominator measured on
-// the running GPU.  One CTA per SM issues back-to-back tcgen05.mma
-// kind::tf32 of M=128, N=256, K=8 (operands resident in shared memory, the
-// accumulator in tensor memory) from one thread; the products' FLOPs over
-// the event-timed duration give the reachable dense TF32 rate.  N=256 is the
-// shape whose issue cost is below its tensor-pipe time, so the figure is the
-// pipe's, not the issuing thread's.  Diagnostic only: no reference
-// counterpart.
+// the running GPU, and the issue-rate table behind the kernels' tile shapes.
+// One CTA per SM; `warps` threads (lane 0 of warps 0..warps-1) each issue
+// back-to-back tcgen05.mma kind::tf32 of M=128, N=n, K=8 (operands resident
+// in shared memory) into their own tensor-memory accumulator.  The products'
+// FLOPs over the event-timed duration give the rate.  With n=256 one issuing
+// thread is faster than the pipe, so that figure is the dense TF32 peak;
+// smaller n show the per-instruction issue floor.  Diagnostic only: no
+// reference counterpart.
 #include "amc_internal.h"
 #include "amc_tc.cuh"
 
@@ -14,71 +15,86 @@ namespace amc {
 using namespace tc;
 
 namespace {
-constexpr int kPeakN = 256;
-constexpr int kPeakSmem = 16384 + 32768 + 1024 + 1024;   // A 128 rows, B 256 rows (128 B each), barrier, alignment
+// A 128 rows and B 256 rows of 128 B, barriers, alignment; sized above half
+// the SM's shared memory so exactly one CTA runs per SM
+constexpr int kPeakSmem = 120 * 1024;
 __device__ int g_peak_error;
 }  // namespace
 
-__global__ void __launch_bounds__(128, 1) k_tc_peak(int iters) {
+template <int N>
+__global__ void __launch_bounds__(128, 1) k_tc_peak(int iters, int warps) {
   extern __shared__ unsigned char peak_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)peak_sm_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bar = (uint64_t*)(sm + 49152);
+  uint64_t* bar = (uint64_t*)(sm + 49152);   // [4]
   uint32_t* slot = (uint32_t*)(sm + 49152 + 64);
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5;
   for (int i = tid; i < 49152 / 4; i += 128) reinterpret_cast<float*>(sm)[i] = 0.0078125f * (float)(i & 7);
   if (tid == 0) {
-    mbar_init(bar, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
     mbar_fence_init();
   }
   fence_proxy_async();
   __syncthreads();
-  if (tid < 32) tmem_alloc(slot, kPeakN);
+  if (warp == 0) tmem_alloc(slot, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *slot;
-  if (tid == 0) {
-    const uint32_t id = idesc_tf32(128, kPeakN, false, false);
+  if ((tid & 31) == 0 && warp < warps) {
+    const uint32_t id = idesc_tf32(128, N, false, false);
     const uint64_t a0 = sdesc(smem_addr(sm), 16, 1024), b0 = sdesc(smem_addr(sm + 16384), 16, 1024);
-    mma_tf32(tmem, a0, b0, id, false);
+    const uint32_t d = tmem + (uint32_t)(warp * N);
+    mma_tf32(d, a0, b0, id, false);
     for (int it = 0; it < iters; ++it) {
 #pragma unroll
-      for (int k = 0; k < 4; ++k) mma_tf32(tmem, desc_add(a0, k * 32), desc_add(b0, k * 32), id, true);
+      for (int k = 0; k < 4; ++k) mma_tf32(d, desc_add(a0, k * 32), desc_add(b0, k * 32), id, true);
     }
-    mma_commit(bar);
-    if (!mbar_wait(bar, 0, 1 << 26)) atomicExch(&g_peak_error, AMC_ERR_TIMEOUT);
+    mma_commit(&bar[warp]);
+    if (!mbar_wait(&bar[warp], 0, 1 << 26)) atomicExch(&g_peak_error, AMC_ERR_TIMEOUT);
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) tmem_dealloc(tmem, kPeakN);
+  if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-}  // namespace amc
-
-using namespace amc;
-
-extern "C" int amc_tc_peak_tf32(int32_t iters, double* tflops, void* stream) {
-  if (!tflops || iters <= 0 || iters > (1 << 20)) return fail(AMC_ERR_INVALID, "amc_tc_peak_tf32: bad arguments");
-  cudaStream_t s = pick_stream(stream);
+template <int N>
+static int run_peak(int iters, int warps, cudaStream_t s, float* ms) {
   static bool attr = false;
   if (!attr) {
-    AMC_CUDA(cudaFuncSetAttribute(k_tc_peak, cudaFuncAttributeMaxDynamicSharedMemorySize, kPeakSmem));
+    AMC_CUDA(cudaFuncSetAttribute(k_tc_peak<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPeakSmem));
     attr = true;
   }
   const int sms = num_sms();
   cudaEvent_t a, b;
   AMC_CUDA(cudaEventCreate(&a));
   AMC_CUDA(cudaEventCreate(&b));
-  k_tc_peak<<<sms, 128, kPeakSmem, s>>>(iters / 4 + 1);   // warm-up
+  k_tc_peak<N><<<sms, 128, kPeakSmem, s>>>(iters / 4 + 1, warps);   // warm-up
   AMC_CUDA(cudaEventRecord(a, s));
-  k_tc_peak<<<sms, 128, kPeakSmem, s>>>(iters);
+  k_tc_peak<N><<<sms, 128, kPeakSmem, s>>>(iters, warps);
   AMC_CUDA(cudaEventRecord(b, s));
   cudaError_t e = cudaEventSynchronize(b);
-  float ms = 0.f;
-  if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, a, b);
+  if (e == cudaSuccess) e = cudaEventElapsedTime(ms, a, b);
   cudaEventDestroy(a);
   cudaEventDestroy(b);
   if (e != cudaSuccess) return cuda_fail(e, "k_tc_peak");
+  return AMC_OK;
+}
+
+}  // namespace amc
+
+using namespace amc;
+
+extern "C" int amc_tc_peak_tf32(int32_t n, int32_t warps, int32_t iters, double* tflops, void* stream) {
+  if (!tflops || iters <= 0 || iters > (1 << 20) || warps < 1 || warps > 4 ||
+      (n != 32 && n != 64 && n != 128 && n != 256) || n * warps > 512)
+    return fail(AMC_ERR_INVALID, "amc_tc_peak_tf32: n in {32,64,128,256}, warps 1..4, n*warps <= 512");
+  cudaStream_t s = pick_stream(stream);
+  float ms = 0.f;
+  int rc = n == 32 ? run_peak<32>(iters, warps, s, &ms)
+           : n == 64 ? run_peak<64>(iters, warps, s, &ms)
+           : n == 128 ? run_peak<128>(iters, warps, s, &ms)
+                      : run_peak<256>(iters, warps, s, &ms);
+  if (rc) return rc;
   int err = 0;
   AMC_CUDA(cudaMemcpyFromSymbol(&err, g_peak_error, sizeof(int)));
   if (err) {
@@ -86,7 +102,7 @@ extern "C" int amc_tc_peak_tf32(int32_t iters, double* tflops, void* stream) {
     AMC_CUDA(cudaMemcpyToSymbol(g_peak_error, &z, sizeof(int)));
     return fail(err, "amc_tc_peak_tf32: the completion wait gave up");
   }
-  const double flops = 2.0 * 128.0 * kPeakN * 8.0 * (4.0 * iters + 1.0) * sms;
+  const double flops = 2.0 * 128.0 * n * 8.0 * (4.0 * iters + 1.0) * warps * num_sms();
   *tflops = ms > 0.f ? flops / (ms * 1e-3) / 1e12 : 0.0;
   return AMC_OK;
 }

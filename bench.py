@@ -205,6 +205,7 @@ def bench_filterbank(args, ws, rank, local):
     import torch
     import amcuda as am
     from amcuda import workloads as W
+    from amcuda.dist import allreduce_fixed_order
     am.init(local)
     torch.cuda.set_device(local)
     B, L = args.signals, args.samples
@@ -351,6 +352,7 @@ def bench_other(args, ws, rank, local):
     import torch
     import amcuda as am
     from amcuda import workloads as W
+    from amcuda.dist import allreduce_fixed_order
     am.init(local)
     torch.cuda.set_device(local)
     stream = torch.cuda.Stream()
@@ -384,8 +386,8 @@ def bench_other(args, ws, rank, local):
             W.linreg_partials(X, y, w, part, N_total)
             W.linreg_reduce(part, npart, d, gl)
             if ws > 1:
-                import torch.distributed as dist
-                dist.all_reduce(gl)
+                # the grad+loss row crosses the row shards: rank-ordered all-reduce
+                allreduce_fixed_order(gl)
             W.linreg_update(w, gl, N_total, 0.1, loss)
         work = n * d * 8 + n * 8
         unit, bound, metric = "GB/s", "hbm", "linear-regression step (fused pass over X) GB/s"
@@ -394,7 +396,7 @@ def bench_other(args, ws, rank, local):
                "l2": "X larger than L2"}
         launches = 3
     elif wl == "attention":
-        B, H, S, D = args.batch, 16, 2048, 64
+        B, H, S, D = args.batch or 16, 16, 2048, 64
         q, k, v = (torch.from_numpy(W.normal(W.seed_of(4, j), B * H * S * D).astype(np.float32)).cuda().view(B, H, S, D)
                    for j in range(3))
         do = torch.from_numpy(W.normal(W.seed_of(4, 3), B * H * S * D).astype(np.float32)).cuda().view(B, H, S, D)
@@ -413,7 +415,7 @@ def bench_other(args, ws, rank, local):
                "flops": "algorithmic 12*B*H*S^2*D (6 GEMMs; the backward recomputes S and dP twice more)"}
         launches = 6   # forward: V^T, K rounding, kernel; backward: pre-pass, dK/dV, dQ
     elif wl == "conv":
-        N = args.batch
+        N = args.batch or 64
         x = torch.from_numpy(W.normal(W.seed_of(3, 0), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
         wt = torch.from_numpy((W.normal(W.seed_of(3, 1), 64 * 64 * 9) * math.sqrt(2 / 576)).astype(np.float32)).cuda().view(64, 64, 3, 3)
         dy = torch.from_numpy(W.normal(W.seed_of(3, 2), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
@@ -423,6 +425,9 @@ def bench_other(args, ws, rank, local):
             W.conv2d_fwd(x, wt, yy)
             W.conv2d_dgrad(dy, wt, dx)
             W.conv2d_wgrad(x, dy, dw)
+            if ws > 1:
+                # dW sums over the batch shards: rank-ordered all-reduce
+                allreduce_fixed_order(dw)
         work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
         unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward + data gradient + weight gradient TFLOP/s"
         pre = lambda: None
@@ -478,7 +483,8 @@ def main():
     ap.add_argument("--signals", type=int, default=64)
     ap.add_argument("--samples", type=int, default=1 << 24)
     ap.add_argument("--rows", type=int, default=1 << 22)
-    ap.add_argument("--batch", type=int, default=16)
+    ap.add_argument("--batch", type=int, default=None,
+                    help="per-GPU batch: default 16 (attention, config 4) or 64 (conv, config 3)")
     ap.add_argument("--dtype", default="f64")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
