@@ -323,34 +323,49 @@ int conv_dgrad_tc(const float* dY, const float* W, float* dX, const ConvShape& s
 
 // ------------------------------------------------------------------ weight gradient
 // dW[co, ci, kh, kw] = sum_{n, q} dY[n, co, q - (kh-1)*W] * X_kw[n, ci, q]
-// over flattened positions q of the H x W plane, where X_kw is X shifted by
-// kw-1 columns with zeros at the row ends (dY is zero outside the plane; the
-// row shift is a TMA coordinate offset of W elements, zero-filled out of
-// range).  The reference's order is a batch sum of per-image GEMMs
-// dY_n . im2col(X_n)^T; here the position sum is split across CTAs and the
-// CTA partials are added in a fixed order by a second kernel.
-// Per K-chunk of 32 positions a stage holds A = dY rows for kh = 0, 1, 2
-// (3 x 64 rows, K-major) and B = X_kw for kw = 0, 1, 2 (3 x 64 rows).  For
-// each kw two M=128 MMAs cover the kh rows (0,1) and (1,2); their 64-column
-// accumulators live in tensor memory for the CTA's whole chunk range.  Warp
-// 1 + kw issues the products of column tap kw.
+// over flattened positions q of the H x W plane, where X_kw[q] = X[q + kw - 1]
+// with zeros where column w + kw - 1 leaves the row.  The reference's order is
+// a batch sum of per-image GEMMs dY_n . im2col(X_n)^T; here the position sum
+// is split across CTAs and the CTA partials are added in a fixed order by a
+// second kernel.
+// Positions are the K dimension, so the NCHW planes are already K-major and
+// the kernel reads dY and X as they are:
+//   - per K-chunk of 32 positions the TMA warp loads A = dY rows for kh = 0,
+//     1, 2 (row shifts of W positions are TMA coordinate offsets, zero-filled
+//     outside the plane), B1 = X (kw = 1) and two 4-column halo boxes of X;
+//   - warps 4-7 round A and B1 to the nearest tf32 in place and write the
+//     column-shifted B0 and B2 (a 4-byte shift cannot start a descriptor);
+//   - warp 1 + kw issues the two M=128 products of column tap kw: kh rows
+//     (0,1) and (1,2); their 64-column accumulators stay in tensor memory
+//     for the CTA's whole chunk range.
 namespace {
-constexpr int kWgStage = 6 * 8192;        // 3 A blocks + 3 B blocks of 64 rows x 128 B
+constexpr int kWgBlk = 8192;                       // 64 rows x 128 B, K-major, 128-byte swizzle
+constexpr int kWgHalo = 64 * 16;                   // 64 rows x 4 floats, row-major
+constexpr int kWgHaloOff = 6 * kWgBlk;             // left halo, then right halo
+constexpr int kWgStage = 6 * kWgBlk + 2 * kWgHalo; // A0-2, B0-2, halos: 50 KB
 constexpr int kWgStages = 4;
 constexpr int kWgBarOff = kWgStages * kWgStage;
 constexpr int kWgSmem = kWgBarOff + 256 + 1024;
-constexpr int kWgPart = 3 * 2 * 128 * kC;   // floats of one CTA's partial: [kw][block][lane][64]
+constexpr int kWgPart = 3 * 2 * 128 * kC;          // floats of one CTA's partial: [kw][block][lane][64]
+static_assert(kWgStage % 1024 == 0, "stages stay 1024-byte aligned");
+static_assert(kWgSmem <= 232448, "weight-gradient shared memory");
+
+__device__ __forceinline__ float4 round4(float4 v) {
+  return make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+}
 }  // namespace
 
 __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant__ CUtensorMap mDY,
-                                                         const __grid_constant__ CUtensorMap mXk,
+                                                         const __grid_constant__ CUtensorMap mX,
+                                                         const __grid_constant__ CUtensorMap mXh,
                                                          float* __restrict__ partials, int N, int HW,
                                                          int Wd, int chunks_per_img) {
   extern __shared__ unsigned char wg_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)wg_sm_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = (uint64_t*)(sm + kWgBarOff);   // [kWgStages]
-  uint64_t* empty = full + kWgStages;             // [kWgStages]
-  uint64_t* done = full + 2 * kWgStages;
+  uint64_t* full = (uint64_t*)(sm + kWgBarOff);   // [kWgStages] TMA landed
+  uint64_t* ready = full + kWgStages;             // [kWgStages] rounded and shifted
+  uint64_t* empty = full + 2 * kWgStages;         // [kWgStages] products done
+  uint64_t* done = full + 3 * kWgStages;
   uint32_t* tslot = (uint32_t*)(sm + kWgBarOff + 128);
   volatile int* abort_flag = (volatile int*)(sm + kWgBarOff + 132);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -360,6 +375,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   if (tid == 0) {
     for (int i = 0; i < kWgStages; ++i) {
       mbar_init(&full[i], 1);
+      mbar_init(&ready[i], 128);
       mbar_init(&empty[i], 3);   // one commit from each column tap's MMA warp
     }
     mbar_init(done, 3);
@@ -377,12 +393,14 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
       for (int c = c0, it = 0; c < c1; ++c, ++it) {
         const int st = it % kWgStages;
         if (it >= kWgStages && !mbar_wait(&empty[st], (uint32_t)((it / kWgStages) - 1) & 1u)) { *abort_flag = 1; break; }
+        if (*abort_flag) break;
         const int n = c / chunks_per_img, q0 = (c % chunks_per_img) * 32;
         unsigned char* sb = sm + st * kWgStage;
-        mbar_expect_tx(&full[st], kWgStage);
-        for (int kh = 0; kh < 3; ++kh) tma_load_2d(sb + kh * 8192, &mDY, q0 - (kh - 1) * Wd, n * kC, &full[st]);
-        for (int kw = 0; kw < 3; ++kw)
-          tma_load_2d(sb + (3 + kw) * 8192, &mXk, q0, (kw * N + n) * kC, &full[st]);
+        mbar_expect_tx(&full[st], 4 * kWgBlk + 2 * kWgHalo);
+        for (int kh = 0; kh < 3; ++kh) tma_load_2d(sb + kh * kWgBlk, &mDY, q0 - (kh - 1) * Wd, n * kC, &full[st]);
+        tma_load_2d(sb + 4 * kWgBlk, &mX, q0, n * kC, &full[st]);
+        tma_load_2d(sb + kWgHaloOff, &mXh, q0 - 4, n * kC, &full[st]);
+        tma_load_2d(sb + kWgHaloOff + kWgHalo, &mXh, q0 + 32, n * kC, &full[st]);
       }
     }
   } else if (warp >= 1 && warp <= 3) {
@@ -394,7 +412,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
       bool ok = true;
       for (int c = c0, it = 0; c < c1; ++c, ++it) {
         const int st = it % kWgStages;
-        if (!mbar_wait(&full[st], (uint32_t)(it / kWgStages) & 1u)) { ok = false; break; }
+        if (!mbar_wait(&ready[st], (uint32_t)(it / kWgStages) & 1u)) { ok = false; break; }
         tc_fence_after();
         const uint64_t sd = desc_add(sdesc0, st * kWgStage);
         const bool acc0 = it > 0;
@@ -402,8 +420,8 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
         for (int k = 0; k < 4; ++k)
 #pragma unroll
           for (int blk = 0; blk < 2; ++blk)
-            mma_tf32(tmem + (uint32_t)(kw * 128 + blk * 64), desc_add(sd, blk * 8192 + k * 32),
-                     desc_add(sd, (3 + kw) * 8192 + k * 32), idesc, acc0 || k > 0);
+            mma_tf32(tmem + (uint32_t)(kw * 128 + blk * 64), desc_add(sd, blk * kWgBlk + k * 32),
+                     desc_add(sd, (3 + kw) * kWgBlk + k * 32), idesc, acc0 || k > 0);
         mma_commit(&empty[st]);
         if (*abort_flag) break;
       }
@@ -411,7 +429,64 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
       mma_commit(done);
     }
   } else if (warp >= 4) {
-    const int row = tid - 128;   // TMEM lane
+    // ---- operand preparation: thread t owns row r (a channel) and positions
+    // 16h..16h+15 of every block; logical 16-byte chunk j of row r sits at
+    // chunk j ^ (r & 7) (the 128-byte swizzle)
+    const int t = tid - 128, r = t >> 1, h = t & 1;
+    bool okp = true;
+    for (int c = c0, it = 0; c < c1 && okp; ++c, ++it) {
+      const int st = it % kWgStages;
+      if (!mbar_wait(&full[st], (uint32_t)(it / kWgStages) & 1u) || *abort_flag) {
+        *abort_flag = 1;
+        okp = false;
+        break;
+      }
+      unsigned char* sb = sm + st * kWgStage;
+      unsigned char* row = sb + r * 128;
+      const int sw = r & 7;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float4* p = reinterpret_cast<float4*>(row + kh * kWgBlk + (((4 * h + i) ^ sw) << 4));
+          *p = round4(*p);
+        }
+      float x[16];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(row + 4 * kWgBlk + (((4 * h + i) ^ sw) << 4));
+        x[4 * i] = v.x; x[4 * i + 1] = v.y; x[4 * i + 2] = v.z; x[4 * i + 3] = v.w;
+      }
+      // neighbours: position 16h - 1 and 16h + 16 of this row (a halo column
+      // at the chunk ends; re-reading a neighbour already rounded is harmless)
+      const float* halo = reinterpret_cast<const float*>(sb + kWgHaloOff);
+      const float left = h ? *reinterpret_cast<const float*>(row + 4 * kWgBlk + ((3 ^ sw) << 4) + 12)
+                           : halo[r * 4 + 3];
+      const float right = h ? halo[kWgHalo / 4 + r * 4]
+                            : *reinterpret_cast<const float*>(row + 4 * kWgBlk + ((4 ^ sw) << 4));
+      const int q = (c % chunks_per_img) * 32 + 16 * h;
+      int w = q % Wd;
+      float b0[16], b2[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float xm = j == 0 ? left : x[j - 1];
+        const float xp = j == 15 ? right : x[j + 1];
+        b0[j] = w == 0 ? 0.f : round_tf32(xm);
+        b2[j] = w == Wd - 1 ? 0.f : round_tf32(xp);
+        w = w + 1 == Wd ? 0 : w + 1;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int off = ((4 * h + i) ^ sw) << 4;
+        *reinterpret_cast<float4*>(row + 3 * kWgBlk + off) = make_float4(b0[4 * i], b0[4 * i + 1], b0[4 * i + 2], b0[4 * i + 3]);
+        *reinterpret_cast<float4*>(row + 4 * kWgBlk + off) =
+            round4(make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
+        *reinterpret_cast<float4*>(row + 5 * kWgBlk + off) = make_float4(b2[4 * i], b2[4 * i + 1], b2[4 * i + 2], b2[4 * i + 3]);
+      }
+      fence_proxy_async();
+      mbar_arrive(&ready[st]);
+    }
+    // ---- epilogue: TMEM lane = row
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const bool ok = named_bar_and(1, 128, mbar_wait(done, 0) && !*abort_flag);
     if (ok && c1 > c0) {
@@ -419,11 +494,12 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
       // lanes 0-63 of block 0 are kh=0, 64-127 kh=1; block 1 lanes 64-127 are
       // kh=2.  Partials keep the tensor-memory layout [kw][block][lane][64],
       // so each thread writes its row's 64 values contiguously.
+      const int lr = tid - 128;
       float* part = partials + (size_t)blockIdx.x * kWgPart;
       for (int kw = 0; kw < 3; ++kw)
         for (int blk = 0; blk < 2; ++blk) {
-          if (blk == 1 && row < 64) continue;   // duplicate of kh=1 (whole warps 4 and 5)
-          float4* dst = reinterpret_cast<float4*>(part + ((size_t)(kw * 2 + blk) * 128 + row) * kC);
+          if (blk == 1 && lr < 64) continue;   // duplicate of kh=1 (whole warps 4 and 5)
+          float4* dst = reinterpret_cast<float4*>(part + ((size_t)(kw * 2 + blk) * 128 + lr) * kC);
           for (int half = 0; half < 2; ++half) {
             float v[32];
             tmem_ld32(tmem + (uint32_t)(kw * 128 + blk * 64 + half * 32) + lane_base, v);
@@ -431,12 +507,16 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
             for (int i = 0; i < 8; ++i) dst[half * 8 + i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
           }
         }
-    } else if (!ok && row == 0) {
+    } else if (!ok && tid == 128) {
       atomicExch(&g_conv_error, AMC_ERR_TIMEOUT);
     }
   }
   tc_fence_before();
   __syncthreads();
+  if (*abort_flag) {
+    for (int i = 0; i < kWgStages; ++i) mbar_wait(&full[i], 0, 1 << 14);
+    mbar_wait(done, 0, 1 << 14);
+  }
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
@@ -463,66 +543,36 @@ __global__ void __launch_bounds__(256) k_wgrad_reduce(const float* __restrict__ 
         ((red[0][l] + red[1][l]) + (red[2][l] + red[3][l])) + ((red[4][l] + red[5][l]) + (red[6][l] + red[7][l]));
 }
 
-// X (N, 64, H, W) -> X_kw (3, N, 64, H*W), X_kw[.., h, w] = X[.., h, w + kw - 1] (0 outside),
-// and dY -> rounded copy; all rounded to the nearest tf32.  One thread per 4
-// consecutive columns of one row (W % 4 == 0): 16-byte loads and stores, the
-// neighbouring columns from the adjacent vectors of the same row.
-__global__ void k_wgrad_prep(const float* __restrict__ X, const float* __restrict__ dY, float* __restrict__ Xk,
-                             float* __restrict__ dYr, long long plane_elems, int Wd) {
-  const long long total4 = plane_elems / 4;
-  const int w4 = Wd / 4;
-  const float4* X4 = reinterpret_cast<const float4*>(X);
-  float4* K0 = reinterpret_cast<float4*>(Xk);
-  float4* K1 = K0 + total4;
-  float4* K2 = K1 + total4;
-  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long stride = (long long)gridDim.x * blockDim.x;
-  for (; i < total4; i += stride) {
-    const int q = (int)(i % w4);   // vector index within the row
-    const float4 c = X4[i];
-    const float left = q > 0 ? X[4 * i - 1] : 0.f;
-    const float right = q < w4 - 1 ? X[4 * i + 4] : 0.f;
-    const float4 r = make_float4(round_tf32(c.x), round_tf32(c.y), round_tf32(c.z), round_tf32(c.w));
-    K1[i] = r;
-    K0[i] = make_float4(round_tf32(left), r.x, r.y, r.z);       // kw = 0: X[w - 1]
-    K2[i] = make_float4(r.y, r.z, r.w, round_tf32(right));      // kw = 2: X[w + 1]
-    const float4 g = reinterpret_cast<const float4*>(dY)[i];
-    reinterpret_cast<float4*>(dYr)[i] = make_float4(round_tf32(g.x), round_tf32(g.y), round_tf32(g.z), round_tf32(g.w));
-  }
-}
-
 int conv_wgrad_tc(const float* X, const float* dY, float* dW, const ConvShape& s, cudaStream_t st, bool* handled) {
   *handled = s.C == kC && s.K == kC && s.KH == 3 && s.KW == 3 && s.SH == 1 && s.SW == 1 && s.PH == 1 && s.PW == 1 &&
-             s.W % 4 == 0 && (s.H * s.W) % 32 == 0 && s.N >= 1 && (long long)s.N * kC * 3 < (1 << 30);
+             s.W % 4 == 0 && (s.H * s.W) % 32 == 0 && s.N >= 1 && (long long)s.N * kC < (1 << 30) &&
+             !(((uintptr_t)X | (uintptr_t)dY) & 15);
   if (!*handled) return AMC_OK;
-  const long long plane = (long long)s.N * kC * s.H * s.W;
   const int nsm = num_sms();
   const size_t part_bytes = (size_t)nsm * kWgPart * sizeof(float);
   void* scratch = nullptr;
-  int rc = conv_scratch((size_t)plane * 4 * sizeof(float) + part_bytes + 4096, &scratch);
+  int rc = conv_scratch(part_bytes + 4096, &scratch);
   if (rc) return rc;
-  float* Xk = (float*)scratch;
-  float* dYr = Xk + 3 * plane;
-  float* parts = dYr + plane;
+  float* parts = (float*)scratch;
   int* counts = (int*)(parts + (size_t)nsm * kWgPart);
-  k_wgrad_prep<<<nsm * 8, 256, 0, st>>>(X, dY, Xk, dYr, plane, s.W);
-  AMC_CUDA(cudaGetLastError());
   const int HW = s.H * s.W, cpi = HW / 32, total = s.N * cpi;
   const int grid = total < nsm ? total : nsm;
   std::vector<int> cnt(grid);
   for (int b = 0; b < grid; ++b)
     cnt[b] = (int)((long long)total * (b + 1) / grid) - (int)((long long)total * b / grid);
   AMC_CUDA(cudaMemcpyAsync(counts, cnt.data(), grid * sizeof(int), cudaMemcpyHostToDevice, st));
-  CUtensorMap mDY, mXk;
-  rc = make_tmap_2d_f32(&mDY, dYr, (uint64_t)s.N * kC, (uint64_t)HW, (uint64_t)HW, 64);
-  if (!rc) rc = make_tmap_2d_f32(&mXk, Xk, (uint64_t)3 * s.N * kC, (uint64_t)HW, (uint64_t)HW, 64);
+  CUtensorMap mDY, mX, mXh;
+  const uint64_t rows = (uint64_t)s.N * kC;
+  rc = make_tmap_2d_f32(&mDY, dY, rows, (uint64_t)HW, (uint64_t)HW, 64);
+  if (!rc) rc = make_tmap_2d_f32(&mX, X, rows, (uint64_t)HW, (uint64_t)HW, 64);
+  if (!rc) rc = make_tmap_2d_f32_box(&mXh, X, rows, (uint64_t)HW, (uint64_t)HW, 4, 64, false);
   if (rc) return rc;
   static bool attr = false;
   if (!attr) {
     AMC_CUDA(cudaFuncSetAttribute(k_conv_wgrad_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kWgSmem));
     attr = true;
   }
-  k_conv_wgrad_tc<<<grid, 256, kWgSmem, st>>>(mDY, mXk, parts, s.N, HW, s.W, cpi);
+  k_conv_wgrad_tc<<<grid, 256, kWgSmem, st>>>(mDY, mX, mXh, parts, s.N, HW, s.W, cpi);
   AMC_CUDA(cudaGetLastError());
   k_wgrad_reduce<<<kC * kC * 9 / 32, 256, 0, st>>>(parts, dW, grid, counts);
   AMC_CUDA(cudaGetLastError());

@@ -236,5 +236,9 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool a_mn_major,
 // a (32 x box_rows) box and 128-byte swizzle, through the driver entry point.
 int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                      uint32_t box_rows);
+// The same with any box width (a multiple of 4 floats) and, without the
+// 128-byte swizzle, plain row-major boxes.
+int make_tmap_2d_f32_box(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                         uint32_t box_cols, uint32_t box_rows, bool swizzle128);
 
 }  // namespace amc
