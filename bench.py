@@ -159,6 +159,65 @@ def cpu_filterbank(n_procs: int, length: int, signals: int):
     return by / wall / 1e9, wall
 
 
+def _timed(fn, min_s: float = 1.0):
+    """Mean seconds of fn() over repeats totalling at least min_s (at least one)."""
+    fn()   # first call builds / warms the oracle
+    n, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= min_s:
+            return dt / n
+
+
+def cpu_other(wl: str, dtype: str):
+    """The oracle port of the reference's CPU path, timed on a bounded sample
+    of the workload on one host thread: (value, unit, sample)."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle
+    from amcuda import morph as M
+    from amcuda import workloads as W
+    if wl == "fused":
+        xm, ym = W.c1_inputs_morph(dtype)
+        tree = W.c1_tree(xm, ym)
+        esz = 8 if dtype == "f64" else 4
+        t = _timed(lambda: oracle.realize(tree))
+        return ((2 * (1 << 19) + 1024) * esz / t / 1e9, "GB/s",
+                f"the whole config-1 tree ({dtype}), per-node realize with materialised map and add nodes, 1 thread")
+    if wl == "linreg":
+        rows, d = 1 << 15, 256
+        X, y, _ = W.c5_inputs(rows, d)
+        t = _timed(lambda: oracle.linreg(X, y, np.zeros(d), 1, 0.1))
+        return (rows * (d + 1) * 8 / t / 1e9, "GB/s",
+                f"{rows} of the 2^22 rows, one step of the SSA replay (GEMV, residual, strided GEMM), 1 thread")
+    if wl == "attention":
+        n, dh = 2048, 64
+        q, k, v, do = (W.normal(W.seed_of(4, j), n * dh).astype(np.float32).reshape(1, n, dh) for j in range(4))
+        tree = M.attention_morphism(M.morph_from_numpy(q), M.morph_from_numpy(k), M.morph_from_numpy(v), 0.125)
+
+        def run():
+            oracle.realize(tree)
+            oracle.attention_bwd(q, k, v, do, 0.125)
+        t = _timed(run)
+        return (12.0 * n * n * dh / t / 1e12, "TFLOP/s",
+                "1 of the 256 (batch, head) blocks: the %attn-2d! restatement forward and a double-precision VJP, 1 thread")
+    if wl == "conv":
+        x = W.normal(W.seed_of(3, 0), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
+        w = (W.normal(W.seed_of(3, 1), 64 * 64 * 9) * np.sqrt(2 / 576)).astype(np.float32).reshape(64, 64, 3, 3)
+        dy = W.normal(W.seed_of(3, 2), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
+
+        def run():
+            oracle.conv2d_fwd(x, w)
+            oracle.conv2d_dgrad(dy, w, x.shape)
+            oracle.conv2d_wgrad(x, dy, w.shape)
+        t = _timed(run)
+        return (3 * 2.0 * 64 * 64 * 9 * 56 * 56 / t / 1e12, "TFLOP/s",
+                "1 of the 64 images: im2col + double-accumulating GEMM forward, col2im data gradient, weight gradient, 1 thread")
+    return None
+
+
 def reference_arm(args, ws, rank):
     if rank != 0:
         return
@@ -453,6 +512,11 @@ def bench_other(args, ws, rank, local):
     clocks = clk.stop()
     t = max_over_ranks(ws, sum(ms))
     per = work / (sum(ms) / len(ms) / 1e3)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        r = cpu_other(wl, args.dtype)
+        if r:
+            cpu = {"value": r[0], "unit": r[1], "cores": 1, "kind": "port", "sample": r[2]}
     scale = 1e9 if unit == "GB/s" else 1e12
     if bound == "hbm":
         peak, peak_source = hbm, kind + " hbm_gbs"
@@ -470,7 +534,7 @@ def bench_other(args, ws, rank, local):
             "roofline": {"bound": bound, "achieved": per / scale, "peak": peak, "unit": unit, "frac": per / scale / peak,
                          "traffic": None,
                          "peak_source": peak_source},
-            "gpu_launches": launches * args.steps, "clocks": clocks}))
+            "cpu_baseline": cpu, "gpu_launches": launches * args.steps, "clocks": clocks}))
 
 
 def main():
