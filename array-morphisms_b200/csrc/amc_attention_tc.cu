@@ -200,9 +200,10 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
 //   S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) PV1(1) S1(2) | ...
 // so the next S of one group runs while the other group is in its softmax.
 // S_g(j+1) is issued into the columns that hold P_g(j) right after PV_g(j):
-// the MMAs of one thread execute in issue order.  P is written back over S
-// (rounded to tf32) and is the A operand of P V straight from tensor memory;
-// O accumulates in tensor memory.  The running maximum is raised lazily
+// the MMAs of one thread execute in issue order.  Q (rounded, written once
+// by the row threads) and P (written back over S, rounded to tf32) are the A
+// operands straight from tensor memory, so the products read only K and V^T
+// from shared memory; O accumulates in tensor memory.  The running maximum is raised lazily
 // (only when a score exceeds it by more than 2^8), and O is rescaled in place
 // then, after that group's previous P V product has completed.  The decision
 // is taken per warp, so the warp-collective tensor-memory accesses stay
@@ -258,7 +259,7 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tslot;   // S_g at g*128, O_g at 256 + g*64
+  const uint32_t tmem = *tslot;   // S_g at g*128, O_g at 256 + g*64, Q_g at 384 + g*64
 
   if (warp == 8) {
     if (lane == 0) {
@@ -288,14 +289,15 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
     if (lane == 0) {
       const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
       const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
-      const uint64_t qd = sdesc(smem_addr(sm + kQ3Off), 16, 1024);
       const uint64_t kd = sdesc(smem_addr(sm + kK3Off), 16, 1024);
       const uint64_t vd = sdesc(smem_addr(sm + kV3Off), 16, 1024);
+      // S = Q K^T with Q (the A operand) in tensor memory, so only K is read
+      // from shared memory
       auto issue_s = [&](int g, int j) {
-        const uint64_t kb = desc_add(kd, (j & 1) * 32768), qg = desc_add(qd, g * 32768);
+        const uint64_t kb = desc_add(kd, (j & 1) * 32768);
 #pragma unroll
         for (int k = 0; k < kD / 8; ++k)
-          mma_tf32(tmem + g * 128, desc_add(qg, kstep_off(k, 16384)), desc_add(kb, kstep_off(k, 16384)), id_s, k > 0);
+          mma_tf32_ts(tmem + g * 128, tmem + 384 + g * 64 + k * 8, desc_add(kb, kstep_off(k, 16384)), id_s, k > 0);
         mma_commit(&s_full[g]);
       };
       auto issue_pv = [&](int g, int j) {
@@ -342,20 +344,27 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t t_s = tmem + g * 128 + lane_base, t_o = tmem + 256 + g * 64 + lane_base;
     bool ok = mbar_wait(q_full, 0);
-    if (ok) {
-      // round this thread's Q row to the nearest tf32 in place (both 128 B halves)
-      unsigned char* qg = sm + kQ3Off + g * 32768;
+    if (!ok) *abort_flag = 1;
+    {
+      // this thread's Q row, rounded to the nearest tf32, into its tensor-memory
+      // lane: columns 0-63 of Q_g (the staged row is 128-byte swizzled: logical
+      // 16-byte chunk c of row t sits at chunk c ^ (t & 7))
+      const unsigned char* qrow = sm + kQ3Off + g * 32768 + t * 128;
+#pragma unroll
       for (int r = 0; r < 2; ++r) {
-        float4* row = reinterpret_cast<float4*>(qg + r * 16384 + t * 128);
+        float v[32];
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          float4 v = row[c];
-          row[c] = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
+          const float4 x = *reinterpret_cast<const float4*>(qrow + r * 16384 + ((c ^ (t & 7)) << 4));
+          v[4 * c] = round_tf32(x.x);
+          v[4 * c + 1] = round_tf32(x.y);
+          v[4 * c + 2] = round_tf32(x.z);
+          v[4 * c + 3] = round_tf32(x.w);
         }
+        tmem_st32(tmem + 384 + g * 64 + lane_base + 32 * r, v);
       }
-      fence_proxy_async();
-    } else {
-      *abort_flag = 1;
+      tmem_st_wait();
+      tc_fence_before();
     }
     mbar_arrive(q_ready);
     // m: the exponent offset in use (log2 units), raised only when a score
