@@ -12,8 +12,9 @@
 //                      the threads (one per key) form P^T and dS^T and write
 //                      them back over S^T / dP^T, then dV += P^T dO and
 //                      dK += dS^T Q take them as the A operand from TMEM;
-//   k_attn_bwd_dq_tc   one CTA per 128 queries (Q, dO resident); streams
-//                      64-key tiles: S, dP, dS as above, dQ += dS K.
+//   k_attn_bwd_dq_tc   one CTA per 128 queries (Q, dO resident in tensor
+//                      memory as the A operands); streams 64-key tiles:
+//                      S, dP, dS as above, dQ += dS K.
 // Every operand is K-major in 128-byte-swizzled shared memory, so the
 // products whose contraction runs over queries or keys read transposed,
 // tf32-rounded copies (Q^T, dO^T, K^T) that a pre-pass writes together with
@@ -346,10 +347,11 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
   uint64_t* f_empty = qd_full + 4;   // [3]
   uint64_t* b_full = qd_full + 7;    // [2] K_j^T landed
   uint64_t* b_empty = qd_full + 9;   // [2]
-  uint64_t* s_full = qd_full + 11;   // [3]
-  uint64_t* p_full = qd_full + 14;   // [3] dS written back
-  uint64_t* t_free = qd_full + 17;   // [3]
+  uint64_t* s_full = qd_full + 11;   // [2] per tensor-memory buffer
+  uint64_t* p_full = qd_full + 14;   // [2] dS written back
+  uint64_t* t_free = qd_full + 17;   // [2]
   uint64_t* acc_full = qd_full + 20;
+  uint64_t* qd_ready = qd_full + 21; // Q and dO rows in tensor memory
   uint32_t* tslot = (uint32_t*)(sm + kQBar + 192);
   volatile int* abort_flag = (volatile int*)(sm + kQBar + 196);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -370,6 +372,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
       mbar_init(&b_empty[i], 1);
     }
     mbar_init(acc_full, 1);
+    mbar_init(qd_ready, kRowThreads);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -379,7 +382,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t t_dq = tmem + 384;
+  // S/dP buffers at 0 and 128, dQ at 256, Q at 320, dO at 384 (the A
+  // operands of the S and dP products, so those read only K_j and V_j from
+  // shared memory)
+  const uint32_t t_dq = tmem + 256, t_q = tmem + 320, t_do = tmem + 384;
 
   if (warp == 8) {
     if (lane == 0) {
@@ -416,27 +422,27 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
     // warp 10 issues the S/dP products, warp 11 the accumulating ones
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
-      const uint64_t dq0 = sdesc(smem_addr(sm + kQQ), 16, 1024), ddo0 = sdesc(smem_addr(sm + kQdO), 16, 1024);
       const uint64_t df0 = sdesc(smem_addr(sm + kQF), 16, 1024), db0 = sdesc(smem_addr(sm + kQB), 16, 1024);
+      // S = Q K_j^T, dP = dO V_j^T into buffer j % 2; K_j, V_j from stage j % 3
       auto sdp = [&](int j) -> bool {
-        const int s = j % 3;
-        if (!mbar_wait(&f_full[s], (uint32_t)(j / 3) & 1u)) return false;
-        if (j >= 3 && !mbar_wait(&t_free[s], (uint32_t)((j - 3) / 3) & 1u)) return false;
+        const int f = j % 3, s = j & 1;
+        if (!mbar_wait(&f_full[f], (uint32_t)(j / 3) & 1u)) return false;
+        if (j >= 2 && !mbar_wait(&t_free[s], (uint32_t)((j - 2) >> 1) & 1u)) return false;
         tc_fence_after();
         const uint32_t ts = tmem + s * 128;
-        const uint64_t st = desc_add(df0, s * 32768);
+        const uint64_t st = desc_add(df0, f * 32768);
 #pragma unroll
         for (int k = 0; k < kD / 8; ++k) {
-          mma_tf32(ts, desc_add(dq0, kstep_off(k, 16384)), desc_add(st, kstep_off(k, 8192)), id, k > 0);
-          mma_tf32(ts + 64, desc_add(ddo0, kstep_off(k, 16384)), desc_add(st, 16384 + kstep_off(k, 8192)), id, k > 0);
+          mma_tf32_ts(ts, t_q + k * 8, desc_add(st, kstep_off(k, 8192)), id, k > 0);
+          mma_tf32_ts(ts + 64, t_do + k * 8, desc_add(st, 16384 + kstep_off(k, 8192)), id, k > 0);
         }
         mma_commit(&s_full[s]);
-        mma_commit(&f_empty[s]);
+        mma_commit(&f_empty[f]);
         return true;
       };
       auto dq = [&](int j) -> bool {
-        const int s = j % 3, b = j & 1;
-        if (!mbar_wait(&p_full[s], (uint32_t)(j / 3) & 1u)) return false;
+        const int s = j & 1, b = j & 1;
+        if (!mbar_wait(&p_full[s], (uint32_t)(j >> 1) & 1u)) return false;
         if (!mbar_wait(&b_full[b], (uint32_t)(j >> 1) & 1u)) return false;
         tc_fence_after();
         const uint32_t ts = tmem + s * 128;
@@ -450,7 +456,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
       };
       bool ok = true;
       if (warp == 10) {
-        ok = mbar_wait(qd_full, 0);
+        ok = mbar_wait(qd_ready, 0);
         for (int j = 0; j < nt && ok && !*abort_flag; ++j) ok = sdp(j);
       } else {
         for (int j = 0; j < nt && ok && !*abort_flag; ++j) ok = dq(j);
@@ -463,10 +469,32 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
     const int g = warp >> 2, t = tid & 127;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const float2 e = LD[q0 + t];
-    bool ok = true;
+    bool ok = mbar_wait(qd_full, 0);
+    if (!ok) *abort_flag = 1;
+    {
+      // warpgroup 0 moves its Q row, warpgroup 1 its dO row (already rounded)
+      // into tensor memory lane t; the staged rows are 128-byte swizzled
+      const unsigned char* row = sm + (g ? kQdO : kQQ) + t * 128;
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const float4 x = *reinterpret_cast<const float4*>(row + r * 16384 + ((c ^ (t & 7)) << 4));
+          v[4 * c] = x.x;
+          v[4 * c + 1] = x.y;
+          v[4 * c + 2] = x.z;
+          v[4 * c + 3] = x.w;
+        }
+        tmem_st32((g ? t_do : t_q) + lane_base + 32 * r, v);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+    }
+    mbar_arrive(qd_ready);
     for (int j = 0; j < nt; ++j) {
-      const int s = j % 3;
-      ok = named_bar_and(1, kRowThreads, mbar_wait(&s_full[s], (uint32_t)(j / 3) & 1u) && !*abort_flag);
+      const int s = j & 1;
+      ok = named_bar_and(1, kRowThreads, ok && mbar_wait(&s_full[s], (uint32_t)(j >> 1) & 1u) && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
       const uint32_t ts = tmem + s * 128 + lane_base + 32 * g;
