@@ -268,12 +268,19 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
     for (int i = 0; i < nt; ++i) {
       const int s = i % 3;
       const uint32_t ph = (uint32_t)(i / 3) & 1u;
-      ok = named_bar_and(1, kRowThreads, mbar_wait(&s_full[s], ph) && mbar_wait(&f_full[s], ph) && !*abort_flag);
+      // (lse2, D) of this warpgroup's 32 query columns, two per 16-byte
+      // broadcast load, fetched as soon as the stage has landed and before the
+      // wait for S^T/dP^T, so their latency (the loads share the shared-memory
+      // port with the tensor-core operand reads) is hidden behind that wait
+      const bool landed = mbar_wait(&f_full[s], ph);
+      const float4* ld = reinterpret_cast<const float4*>(sm + kKVL + s * 512) + 16 * g;
+      float4 ev[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) ev[q] = ld[q];
+      mbar_arrive(&f_empty[s]);
+      ok = named_bar_and(1, kRowThreads, landed && mbar_wait(&s_full[s], ph) && !*abort_flag);
       if (!ok) break;
       tc_fence_after();
-      // (lse2, D) of two query columns per 16-byte load: these broadcast loads
-      // share the shared-memory port with the tensor-core operand reads
-      const float4* ld = reinterpret_cast<const float4*>(sm + kKVL + s * 512) + 16 * g;
       const uint32_t ts = tmem + s * 128 + lane_base + 32 * g;
       uint32_t sv[32], pv[32];
       tmem_ld32_nowait(ts, sv);
@@ -282,7 +289,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
       float po[32], dso[32];
 #pragma unroll
       for (int j = 0; j < 32; j += 2) {
-        const float4 e = ld[j >> 1];
+        const float4 e = ev[j >> 1];
         const float p0 = ex2_approx(fmaf(__uint_as_float(sv[j]), scale_log2, -e.x));
         const float p1 = ex2_approx(fmaf(__uint_as_float(sv[j + 1]), scale_log2, -e.z));
         po[j] = round_tf32_int(p0);
@@ -293,7 +300,6 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
       tmem_st32(ts, po);
       tmem_st32(ts + 64, dso);
       tmem_st_wait();
-      mbar_arrive(&f_empty[s]);
       tc_fence_before();
       mbar_arrive(&p_full[s]);
     }
