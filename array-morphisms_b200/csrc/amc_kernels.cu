@@ -299,6 +299,10 @@ __device__ __forceinline__ void acc_store(const Acc& A, void* out, int out_dtype
 }
 
 __device__ __forceinline__ void leaf_offsets(const ReduceArgs& a, long long o, long long r, long long* off) {
+  if (a.orank == 1 && a.rrank == 1) {   // one kept and one reduced axis: no index decomposition
+    for (int l = 0; l < a.nleaf; ++l) off[l] = o * a.leaf_o[l].strides[0] + r * a.leaf_r[l][0];
+    return;
+  }
   for (int l = 0; l < a.nleaf; ++l) off[l] = 0;
   long long rem = o;
   for (int d = a.orank - 1; d >= 0; --d) {
@@ -332,7 +336,43 @@ __device__ __forceinline__ void eval_src(const ReduceArgs& a, long long o, long 
 // Ordered ("sequential") reduction: CTA owns OT consecutive outputs.  All
 // threads evaluate a (OT x RC) tile of source values into shared memory in
 // parallel; then one thread per output folds its RC values in ascending r.
-// This reproduces the reference's accumulation order exactly.
+// This reproduces the reference's accumulation order exactly.  The fold is
+// one dependent chain per output, so its step is specialised (`fold`):
+//   1 sum/mean into f64 from an inexact source, 2 the same into f32 (rounded
+//   to f32 after every step, as the reference's typed output is re-read),
+//   3 sum/mean into s32/s64 from an exact source; 0 the generic step.
+template <int FOLD>
+__device__ __forceinline__ void fold_row(Acc& A, int op, int out_dtype, bool src_exact,
+                                         const unsigned long long* __restrict__ row, int rc) {
+  if (FOLD == 1) {
+    double acc = A.f;
+#pragma unroll 8
+    for (int rl = 0; rl < rc; ++rl) acc = __dadd_rn(acc, __longlong_as_double(row[rl]));
+    A.f = acc;
+  } else if (FOLD == 2) {
+    double acc = A.f;
+#pragma unroll 8
+    for (int rl = 0; rl < rc; ++rl) acc = (double)__double2float_rn(__dadd_rn(acc, __longlong_as_double(row[rl])));
+    A.f = acc;
+  } else if (FOLD == 3) {
+    long long acc = A.i;
+    if (out_dtype == AMC_S32) {
+#pragma unroll 8
+      for (int rl = 0; rl < rc; ++rl) acc = (int)(acc + (long long)row[rl]);
+    } else {
+#pragma unroll 8
+      for (int rl = 0; rl < rc; ++rl) acc += (long long)row[rl];
+    }
+    A.i = acc;
+  } else {
+    for (int rl = 0; rl < rc; ++rl) {
+      unsigned long long bits = row[rl];
+      acc_step(A, op, out_dtype, src_exact, __longlong_as_double(bits), (long long)bits);
+    }
+  }
+}
+
+template <int FOLD>
 __global__ void __launch_bounds__(256) k_reduce_seq(const __grid_constant__ ReduceArgs a, int OT, int RC, int ofast) {
   extern __shared__ unsigned long long smem_u64[];
   const bool src_exact = !dtype_is_float_d(a.src_dtype);
@@ -352,13 +392,8 @@ __global__ void __launch_bounds__(256) k_reduce_seq(const __grid_constant__ Redu
       smem_u64[ol * (RC + 1) + rl] = src_exact ? (unsigned long long)vi : __double_as_longlong(vf);
     }
     __syncthreads();
-    if (threadIdx.x < OT && o0 + threadIdx.x < a.O) {
-      const unsigned long long* row = smem_u64 + threadIdx.x * (RC + 1);
-      for (int rl = 0; rl < rc; ++rl) {
-        unsigned long long bits = row[rl];
-        acc_step(A, a.op, a.out_dtype, src_exact, __longlong_as_double(bits), (long long)bits);
-      }
-    }
+    if (threadIdx.x < OT && o0 + threadIdx.x < a.O)
+      fold_row<FOLD>(A, a.op, a.out_dtype, src_exact, smem_u64 + threadIdx.x * (RC + 1), rc);
     __syncthreads();
   }
   if (threadIdx.x < OT && o0 + threadIdx.x < a.O) acc_store(A, a.out, a.out_dtype, a.op, a.R, o0 + threadIdx.x);
@@ -458,7 +493,8 @@ int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scr
   if (a.R == 0) {
     // empty reduction: neutral element (and mean of nothing = 0/0 as the reference)
   }
-  // tile shape: outputs per CTA so that the grid covers the SMs, RC to fit smem
+  // tile shape: outputs per CTA so that the grid covers the SMs twice, RC to
+  // fit shared memory
   long long O = a.O;
   int OT = 256;
   while (OT > 1 && (O + OT - 1) / OT < (long long)sms * 2) OT >>= 1;
@@ -480,7 +516,16 @@ int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scr
   }
   size_t sm = (size_t)OT * (RC + 1) * 8;
   unsigned grid = (unsigned)((O + OT - 1) / OT);
-  k_reduce_seq<<<grid, 256, sm, s>>>(a, OT, RC, ofast);
+  const bool sumlike = a.op == AMC_RED_SUM || a.op == AMC_RED_MEAN;
+  const bool src_float = a.src_dtype == AMC_F32 || a.src_dtype == AMC_F64;
+  if (sumlike && src_float && a.out_dtype == AMC_F64)
+    k_reduce_seq<1><<<grid, 256, sm, s>>>(a, OT, RC, ofast);
+  else if (sumlike && src_float && a.out_dtype == AMC_F32)
+    k_reduce_seq<2><<<grid, 256, sm, s>>>(a, OT, RC, ofast);
+  else if (sumlike && !src_float && (a.out_dtype == AMC_S32 || a.out_dtype == AMC_S64))
+    k_reduce_seq<3><<<grid, 256, sm, s>>>(a, OT, RC, ofast);
+  else
+    k_reduce_seq<0><<<grid, 256, sm, s>>>(a, OT, RC, ofast);
   AMC_CUDA(cudaGetLastError());
   return AMC_OK;
 }
