@@ -112,12 +112,23 @@ __global__ void __launch_bounds__(kLinregBlock) k_linreg_partials_any(const doub
   }
 }
 
-__global__ void k_linreg_reduce(const double* __restrict__ partials, int n, int d, double* __restrict__ out) {
-  int k = blockIdx.x * blockDim.x + threadIdx.x;
-  if (k > d) return;
+// Sum of the n partial rows in a fixed order: a block takes 32 columns and 8
+// groups of rows; group g adds rows g, g+8, ... in ascending order, then the
+// 8 group sums are added in index order.  The loads of a group are
+// independent of the other groups', so the sum is not one n-long dependent
+// chain of loads.
+__global__ void __launch_bounds__(256) k_linreg_reduce(const double* __restrict__ partials, int n, int d,
+                                                       double* __restrict__ out) {
+  __shared__ double red[8][33];
+  const int l = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int k = blockIdx.x * 32 + l;
   double s = 0.0;
-  for (int b = 0; b < n; ++b) s += partials[(long long)b * (d + 1) + k];
-  out[k] = s;
+  if (k <= d)
+    for (int b = g; b < n; b += 8) s += __ldg(partials + (long long)b * (d + 1) + k);
+  red[g][l] = s;
+  __syncthreads();
+  if (g == 0 && k <= d)
+    out[k] = ((red[0][l] + red[1][l]) + (red[2][l] + red[3][l])) + ((red[4][l] + red[5][l]) + (red[6][l] + red[7][l]));
 }
 
 __global__ void k_linreg_update(double* __restrict__ w, const double* __restrict__ gl, int d, double n_total, double lr,
@@ -164,7 +175,7 @@ int amc_linreg_partials(const double* X, const double* y, const double* w, int64
 
 int amc_linreg_reduce(const double* partials, int32_t n, int32_t d, double* grad_loss, void* stream) {
   if (!partials || !grad_loss || n <= 0 || d <= 0) return fail(AMC_ERR_INVALID, "amc_linreg_reduce: bad arguments");
-  k_linreg_reduce<<<(d + 1 + 127) / 128, 128, 0, pick_stream(stream)>>>(partials, n, d, grad_loss);
+  k_linreg_reduce<<<(d + 1 + 31) / 32, 256, 0, pick_stream(stream)>>>(partials, n, d, grad_loss);
   AMC_CUDA(cudaGetLastError());
   return AMC_OK;
 }
