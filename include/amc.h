@@ -313,7 +313,15 @@ int amc_linreg_step_noalloc(const double* X, const double* y, double* w, int64_t
                             double* loss_out, void* stream);
 
 /* Scaled dot-product attention, streaming softmax (realization.scm:279-396):
- * Q (B, n, dk), K (B, n, dk), V (B, n, dv) row-major contiguous per block. */
+ * Q (B, n, dk), K (B, n, dk), V (B, n, dv) row-major contiguous per block;
+ * lse (B, n) receives the natural-log row log-sum-exp (may be NULL in the
+ * forward).  With dk = dv = 64, n a multiple of 128 and 16-byte-aligned
+ * pointers both directions run on the tcgen05 tensor cores with operands
+ * rounded to tf32 (within 2e-3 of the output scale); other shapes run f32
+ * SIMT kernels.  The backward uses no atomics: repeated calls give identical
+ * bits.  The reference has no attention gradient; the backward is the
+ * standard softmax-attention VJP.  Per-device scratch is allocated on first
+ * use and kept. */
 int amc_attention_fwd_f32(const float* Q, const float* K, const float* V, float* O, float* lse,
                           int64_t blocks, int32_t n, int32_t dk, int32_t dv, float scale, void* stream);
 int amc_attention_bwd_f32(const float* Q, const float* K, const float* V, const float* O, const float* dO,
@@ -321,7 +329,12 @@ int amc_attention_bwd_f32(const float* Q, const float* K, const float* V, const 
                           int64_t blocks, int32_t n, int32_t dk, int32_t dv, float scale, void* stream);
 
 /* 2-D convolution, NCHW, stride/pad, as the reference's im2col + GEMM
- * (realization.scm:166-252) and its adjoints via col2im (realization.scm:1196-1268). */
+ * (realization.scm:166-252) and its adjoints via col2im (realization.scm:1196-1268).
+ * C = K = 64, 3x3, stride 1, pad 1 (forward/data gradient: W <= 62, W % 4 == 0,
+ * H even; weight gradient: W % 4 == 0, H*W % 32 == 0) run as tcgen05 implicit
+ * GEMMs with operands rounded to tf32 (within 2e-3 of the output scale); other
+ * shapes run direct kernels with double accumulation (the reference's values).
+ * The weight gradient's split-K partials are summed in a fixed order. */
 int amc_conv2d_fwd_f32(const float* X, const float* W, float* Y, int32_t N, int32_t C, int32_t H, int32_t Wd,
                        int32_t K, int32_t KH, int32_t KW, int32_t SH, int32_t SW, int32_t PH, int32_t PW, void* stream);
 int amc_conv2d_dgrad_f32(const float* dY, const float* W, float* dX, int32_t N, int32_t C, int32_t H, int32_t Wd,
