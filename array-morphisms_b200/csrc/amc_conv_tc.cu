@@ -5,12 +5,12 @@
 // The reference forms im2col(X) explicitly and multiplies it by the
 // flattened weights per image (execute-conv2d-blas, realization.scm:166-252).
 // Here no column matrix exists:
-//   - a pre-pass writes the input as zero-bordered NHWC rows (N, H+2, W+2, 64),
-//     rounded to the nearest tf32;
 //   - an output tile is 2 output rows x 64 columns (128 positions = MMA M).
-//     The producer TMA-loads the 4 padded input rows it needs, 64 positions
-//     per row, each position's 32 channels a 128-byte row of a K-major,
-//     128-byte-swizzled tile (two tiles: channels 0-31 and 32-63);
+//     Four producer warps read the 4 input rows it needs straight from NCHW
+//     (64 positions per row from column -1, zero outside the image, rounded
+//     to the nearest tf32) and write each position's 32 channels as a
+//     128-byte row of a K-major, 128-byte-swizzled tile (two tiles: channels
+//     0-31 and 32-63); no padded copy of the input exists;
 //   - tap (kh, kw) of the tile is the same shared tile read from position
 //     kh*64 + kw on: its A descriptor starts (kh*64 + kw) * 128 bytes in, so
 //     all 9 taps are address offsets of one staged tile;
@@ -23,7 +23,7 @@
 //     pairs alternate so the epilogue of one tile overlaps the MMAs of the
 //     next.
 // Output columns 56..63 of a tile are computed on zero padding and dropped.
-// Warp roles: warp 0 producer, warps 1-2 MMA issuers, warps 4-7 epilogue.
+// Warp roles: warps 0-3 input producers, 4-7 epilogue, 8 weight loads (TMA), 9-10 MMA issuers.
 #include <cudaTypedefs.h>
 
 #include "amc_internal.h"
@@ -46,18 +46,18 @@ constexpr int kWOff = 0;                  // 9 taps x 2 chunks x 8 KB
 constexpr int kXOff = kWOff + 9 * 2 * 8192;         // 2 chunk regions
 constexpr int kBarOffC = kXOff + 2 * kRegion;
 constexpr int kConvSmem = kBarOffC + 256 + 1024;
-constexpr int kConvThreads = 256;
+constexpr int kConvThreads = 352;   // warps 0-3 input producers, 4-7 epilogue, 8 weights, 9-10 MMA
 
 __device__ int g_conv_error;
 
 }  // namespace
 
-__global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_constant__ CUtensorMap mX,
+__global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const float* __restrict__ X,
                                                                const __grid_constant__ CUtensorMap mW,
                                                                float* __restrict__ Y, int N, int H, int Wd) {
   extern __shared__ unsigned char conv_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)conv_sm_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* x_full = (uint64_t*)(sm + kBarOffC);   // [2] per channel chunk
+  uint64_t* x_full = (uint64_t*)(sm + kBarOffC);   // [2] per channel chunk (128 producer arrivals)
   uint64_t* x_empty = x_full + 2;     // [2]
   uint64_t* acc_full = x_full + 4;    // [2] per accumulator
   uint64_t* acc_empty = x_full + 6;   // [2]
@@ -67,11 +67,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pairs = H / 2;
   const int ntiles = N * pairs;
-  const int Hp = H + 2;
   if (tid == 0) {
     for (int t = 0; t < 9; ++t) mbar_init(&w_full[t], 1);
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&x_full[i], 1);
+      mbar_init(&x_full[i], 128);
       mbar_init(&x_empty[i], 1);
       mbar_init(&acc_full[i], 2);   // one commit from each chunk's MMA warp
       mbar_init(&acc_empty[i], 1);
@@ -86,38 +85,77 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
   tc_fence_after();
   const uint32_t tmem = *tslot;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      int li = 0;
-      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++li) {
-        const int n = tile / pairs, oh0 = (tile % pairs) * 2;
-        const int row = n * Hp + oh0;   // padded input rows oh0 .. oh0+3
-        for (int c = 0; c < 2; ++c) {
-          if (li > 0 && !mbar_wait(&x_empty[c], (uint32_t)(li - 1) & 1u)) { *abort_flag = 1; break; }
-          mbar_expect_tx(&x_full[c], 4 * kPosRow * 128);
-          // one 3-D box: 32 channels x 64 positions x 4 rows
-          asm volatile(
-              "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
-              ::"r"(smem_addr(sm + kXOff + c * kRegion)), "l"((uint64_t)&mX), "r"(32 * c), "r"(0), "r"(row),
-                "r"(smem_addr(&x_full[c])) : "memory");
+  if (warp < 4) {
+    // ---- producers: the tile's 4 input rows (oh0-1 .. oh0+2) x 64 positions
+    // (columns -1 .. 62) x 32 channels per chunk, zero outside the image,
+    // rounded to tf32, written as K-major 128-byte rows (position q at q*128,
+    // logical 16-byte chunk j of a row at j ^ (q & 7)).  Warp w takes the
+    // (row, channel-quad) pairs 8w .. 8w+7; each lane one position per half.
+    // The next chunk's values are loaded into registers before the wait for
+    // its buffer, so the global-load latency overlaps the products.
+    const size_t plane = (size_t)H * Wd;
+    float4 buf[16];
+    auto fetch = [&](int tile, int c) {
+      const int n = tile / pairs, oh0 = (tile % pairs) * 2;
+#pragma unroll
+      for (int pi = 0; pi < 8; ++pi) {
+        const int pr = warp * 8 + pi, r = pr >> 3, j = pr & 7;
+        const int ih = oh0 - 1 + r;
+        const bool rowok = ih >= 0 && ih < H;
+        const float* src = X + ((size_t)n * kC + 32 * c + 4 * j) * plane + (size_t)(rowok ? ih : 0) * Wd;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const int iw = lane + 32 * half - 1;
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (rowok && iw >= 0 && iw < Wd) {
+            v.x = __ldg(src + iw);
+            v.y = __ldg(src + plane + iw);
+            v.z = __ldg(src + 2 * plane + iw);
+            v.w = __ldg(src + 3 * plane + iw);
+          }
+          buf[pi * 2 + half] = v;
         }
-        if (li == 0) {
-          // the weights once, after the first input tile and tap by tap (boxes
-          // of 32 in-channels x 64 out-channels), so the first products start
-          // as soon as their tap has landed
-          for (int t = 0; t < 9; ++t) {
-            mbar_expect_tx(&w_full[t], 2 * 8192);
-            for (int c = 0; c < 2; ++c) tma_load_2d(sm + kWOff + (2 * t + c) * 8192, &mW, 0, (2 * t + c) * 64, &w_full[t]);
+      }
+    };
+    int li = 0, tile = blockIdx.x;
+    if (tile < ntiles) fetch(tile, 0);
+    for (; tile < ntiles; tile += gridDim.x, ++li) {
+      for (int c = 0; c < 2; ++c) {
+        if (li > 0 && !mbar_wait(&x_empty[c], (uint32_t)(li - 1) & 1u)) *abort_flag = 1;
+        if (*abort_flag) break;
+        unsigned char* region = sm + kXOff + c * kRegion;
+#pragma unroll
+        for (int pi = 0; pi < 8; ++pi) {
+          const int pr = warp * 8 + pi, r = pr >> 3, j = pr & 7;
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const int q = r * kPosRow + lane + 32 * half;
+            const float4 v = buf[pi * 2 + half];
+            *reinterpret_cast<float4*>(region + q * 128 + ((j ^ (q & 7)) << 4)) =
+                make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
           }
         }
-        if (*abort_flag) break;
+        fence_proxy_async();
+        mbar_arrive(&x_full[c]);
+        // next chunk: chunk 1 of this tile, or chunk 0 of the next tile
+        if (c == 0) fetch(tile, 1);
+        else if (tile + (int)gridDim.x < ntiles) fetch(tile + gridDim.x, 0);
+      }
+      if (*abort_flag) break;
+    }
+  } else if (warp == 8) {
+    if (lane == 0) {
+      // the weights once, tap by tap (boxes of 32 in-channels x 64 out-channels)
+      for (int t = 0; t < 9; ++t) {
+        mbar_expect_tx(&w_full[t], 2 * 8192);
+        for (int c = 0; c < 2; ++c) tma_load_2d(sm + kWOff + (2 * t + c) * 8192, &mW, 0, (2 * t + c) * 64, &w_full[t]);
       }
     }
-  } else if (warp == 1 || warp == 2) {
-    // warp 1 + c issues the products of input-channel chunk c into its own
+  } else if (warp == 9 || warp == 10) {
+    // warp 9 + c issues the products of input-channel chunk c into its own
     // accumulator (tensor memory a * 128 + c * 64); the epilogue adds the two
     if (lane == 0) {
-      const int c = warp - 1;
+      const int c = warp - 9;
       const uint32_t idesc = idesc_tf32(128, kC, false, false);
       const uint64_t xd = sdesc(smem_addr(sm + kXOff + c * kRegion), 16, 1024);
       const uint64_t wd = sdesc(smem_addr(sm + kWOff + c * 8192), 16, 1024);
@@ -147,7 +185,7 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
       }
       if (!ok) *abort_flag = 1;
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && warp < 8) {
     // epilogue warpgroup: TMEM lane q = output position q of the tile
     const int q = tid - 128;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
@@ -183,49 +221,10 @@ __global__ void __launch_bounds__(kConvThreads, 1) k_conv3x3_tc(const __grid_con
   tc_fence_before();
   __syncthreads();
   if (*abort_flag) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_wait(&x_full[i], 0, 1 << 14);
-      mbar_wait(&acc_full[i], 0, 1 << 14);
-    }
+    for (int i = 0; i < 2; ++i) mbar_wait(&acc_full[i], 0, 1 << 14);
     for (int t = 0; t < 9; ++t) mbar_wait(&w_full[t], 0, 1 << 14);
   }
   if (warp == 0) tmem_dealloc(tmem, 256);
-}
-
-// NCHW (N, 64, H, W) -> zero-bordered NHWC (N, H+2, W+2, 64), rounded to tf32.
-// One block per padded row: 16-byte loads of the 64 channel rows into shared
-// memory, then 16-byte stores of 4 channels per position.  Border rows and
-// columns are written as zeros.  Requires W % 4 == 0 and W <= 64.
-__global__ void __launch_bounds__(256) k_pad_nhwc(const float* __restrict__ X, float* __restrict__ Xp, int H, int Wd) {
-  __shared__ float t[kC][kPosRow + 1];
-  const int prow = blockIdx.x;                 // n * (H+2) + hp
-  const int Hp = H + 2, Wp = Wd + 2;
-  const int n = prow / Hp, hp = prow % Hp, h = hp - 1;
-  float4* dst4 = reinterpret_cast<float4*>(Xp + (size_t)prow * Wp * kC);
-  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (h < 0 || h >= H) {
-    for (int i = threadIdx.x; i < Wp * kC / 4; i += blockDim.x) dst4[i] = z;
-    return;
-  }
-  const int w4 = Wd / 4;
-  for (int i = threadIdx.x; i < kC * w4; i += blockDim.x) {
-    const int c = i / w4, q = i % w4;
-    const float4 v = *reinterpret_cast<const float4*>(X + (((size_t)n * kC + c) * H + h) * Wd + 4 * q);
-    t[c][4 * q] = v.x;
-    t[c][4 * q + 1] = v.y;
-    t[c][4 * q + 2] = v.z;
-    t[c][4 * q + 3] = v.w;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < Wd * (kC / 4); i += blockDim.x) {
-    const int w = i / (kC / 4), c4 = (i % (kC / 4)) * 4;
-    dst4[(size_t)(w + 1) * (kC / 4) + c4 / 4] =
-        make_float4(round_tf32(t[c4][w]), round_tf32(t[c4 + 1][w]), round_tf32(t[c4 + 2][w]), round_tf32(t[c4 + 3][w]));
-  }
-  if (threadIdx.x < kC / 4) {
-    dst4[threadIdx.x] = z;
-    dst4[(size_t)(Wp - 1) * (kC / 4) + threadIdx.x] = z;
-  }
 }
 
 // Weights (64 out, 64 in, 3, 3) -> [tap][in-chunk][out][32 in], rounded to tf32.
@@ -267,34 +266,13 @@ static bool conv_tc_shape(const ConvShape& s) {
 }
 
 static int conv_run(const float* in, const float* W, float* out, const ConvShape& s, int flip, cudaStream_t st) {
-  const int Hp = s.H + 2, Wp = s.W + 2;
-  const size_t xbytes = (size_t)s.N * Hp * Wp * kC * sizeof(float);
   void* scratch = nullptr;
-  int rc = conv_scratch(xbytes + 9 * kC * kC * sizeof(float) + 1024, &scratch);
+  int rc = conv_scratch(9 * kC * kC * sizeof(float) + 1024, &scratch);
   if (rc) return rc;
-  float* Xp = (float*)scratch;
-  float* Wt = (float*)(((uintptr_t)((char*)scratch + xbytes) + 1023) & ~(uintptr_t)1023);
-  k_pad_nhwc<<<(unsigned)(s.N * Hp), 256, 0, st>>>(in, Xp, s.H, s.W);
-  AMC_CUDA(cudaGetLastError());
+  float* Wt = (float*)(((uintptr_t)scratch + 1023) & ~(uintptr_t)1023);
   k_conv_weights<<<(9 * kC * kC + 255) / 256, 256, 0, st>>>(W, Wt, flip);
   AMC_CUDA(cudaGetLastError());
-  // X: 3-D (channels, positions of a padded row, padded rows), box 32 x 64 x 4
-  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-  if (!encode) {
-    cudaDriverEntryPointQueryResult q;
-    void* fn = nullptr;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn)
-      return fail(AMC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-    encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
-  }
-  CUtensorMap mX, mW;
-  cuuint64_t dims[3] = {(cuuint64_t)kC, (cuuint64_t)Wp, (cuuint64_t)s.N * Hp};
-  cuuint64_t strides[2] = {(cuuint64_t)kC * 4, (cuuint64_t)Wp * kC * 4};
-  cuuint32_t box[3] = {32, (cuuint32_t)kPosRow, 4};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult cr = encode(&mX, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, Xp, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return fail(AMC_ERR_CUDA, "conv: input tensor map failed");
+  CUtensorMap mW;
   rc = make_tmap_2d_f32(&mW, Wt, 9 * 2 * kC, 32, 32, 64);
   if (rc) return rc;
   static bool attr = false;
@@ -304,7 +282,7 @@ static int conv_run(const float* in, const float* W, float* out, const ConvShape
   }
   const int ntiles = s.N * (s.H / 2);
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
-  k_conv3x3_tc<<<grid, kConvThreads, kConvSmem, st>>>(mX, mW, out, s.N, s.H, s.W);
+  k_conv3x3_tc<<<grid, kConvThreads, kConvSmem, st>>>(in, mW, out, s.N, s.H, s.W);
   AMC_CUDA(cudaGetLastError());
   return AMC_OK;
 }
