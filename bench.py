@@ -515,7 +515,7 @@ def bench_other(args, ws, rank, local):
         unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward + data gradient + weight gradient TFLOP/s"
         pre = lambda: None
         cfg = {"workload": f"config 3: x ({N},64,56,56) f32, w (64,64,3,3), stride 1 pad 1; Y, dX and dW per step"}
-        launches = 8   # 2 x (NHWC pad, weights, kernel) + weight-gradient kernel + reduce
+        launches = 6   # 2 x (weights, kernel) + weight-gradient kernel + reduce
     else:
         raise SystemExit(f"unknown workload {wl}")
     for _ in range(args.warmup):
