@@ -311,7 +311,9 @@ int conv_dgrad_tc(const float* dY, const float* W, float* dX, const ConvShape& s
 //   - per K-chunk of 32 positions the TMA warp loads A = dY rows for kh = 0,
 //     1, 2 (row shifts of W positions are TMA coordinate offsets, zero-filled
 //     outside the plane), B1 = X (kw = 1) and two 4-column halo boxes of X;
-//   - warps 4-7 round A and B1 to the nearest tf32 in place and write the
+//   - warps 4-7 write A, rounded to the nearest tf32, into tensor memory
+//     (the products' A operand, read there by all three column taps instead
+//     of three times from shared memory), round B1 in place and write the
 //     column-shifted B0 and B2 (a 4-byte shift cannot start a descriptor);
 //   - warp 1 + kw issues the two M=128 products of column tap kw: kh rows
 //     (0,1) and (1,2); their 64-column accumulators stay in tensor memory
@@ -344,8 +346,9 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   uint64_t* ready = full + kWgStages;             // [kWgStages] rounded and shifted
   uint64_t* empty = full + 2 * kWgStages;         // [kWgStages] products done
   uint64_t* done = full + 3 * kWgStages;
-  uint32_t* tslot = (uint32_t*)(sm + kWgBarOff + 128);
-  volatile int* abort_flag = (volatile int*)(sm + kWgBarOff + 132);
+  uint64_t* tfree = done + 1;                     // [2] products read tensor-memory A buffer
+  uint32_t* tslot = (uint32_t*)(sm + kWgBarOff + 192);
+  volatile int* abort_flag = (volatile int*)(sm + kWgBarOff + 196);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int total = N * chunks_per_img;
   const int c0 = (int)((long long)total * blockIdx.x / gridDim.x);
@@ -357,6 +360,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
       mbar_init(&empty[i], 3);   // one commit from each column tap's MMA warp
     }
     mbar_init(done, 3);
+    for (int i = 0; i < 2; ++i) mbar_init(&tfree[i], 3);
     *abort_flag = 0;
     mbar_fence_init();
   }
@@ -366,6 +370,10 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  // accumulators at kw * 128 + blk * 64 (0..383); the A operands (dY rows,
+  // blocks kh (0,1) and (1,2), 32 positions each) at 384 + b * 64 + blk * 32
+  // for buffer b = chunk & 1
+  const uint32_t t_a = tmem + 384;
   if (warp == 0) {
     if (lane == 0) {
       for (int c = c0, it = 0; c < c1; ++c, ++it) {
@@ -393,14 +401,16 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
         if (!mbar_wait(&ready[st], (uint32_t)(it / kWgStages) & 1u)) { ok = false; break; }
         tc_fence_after();
         const uint64_t sd = desc_add(sdesc0, st * kWgStage);
+        const uint32_t ta = t_a + (uint32_t)((it & 1) * 64);
         const bool acc0 = it > 0;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
 #pragma unroll
           for (int blk = 0; blk < 2; ++blk)
-            mma_tf32(tmem + (uint32_t)(kw * 128 + blk * 64), desc_add(sd, blk * kWgBlk + k * 32),
-                     desc_add(sd, (3 + kw) * kWgBlk + k * 32), idesc, acc0 || k > 0);
+            mma_tf32_ts(tmem + (uint32_t)(kw * 128 + blk * 64), ta + blk * 32 + k * 8,
+                        desc_add(sd, (3 + kw) * kWgBlk + k * 32), idesc, acc0 || k > 0);
         mma_commit(&empty[st]);
+        mma_commit(&tfree[it & 1]);
         if (*abort_flag) break;
       }
       if (!ok) *abort_flag = 1;
@@ -411,24 +421,38 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
     // 16h..16h+15 of every block; logical 16-byte chunk j of row r sits at
     // chunk j ^ (r & 7) (the 128-byte swizzle)
     const int t = tid - 128, r = t >> 1, h = t & 1;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     bool okp = true;
     for (int c = c0, it = 0; c < c1 && okp; ++c, ++it) {
       const int st = it % kWgStages;
-      if (!mbar_wait(&full[st], (uint32_t)(it / kWgStages) & 1u) || *abort_flag) {
+      if (!mbar_wait(&full[st], (uint32_t)(it / kWgStages) & 1u) ||
+          (it >= 2 && !mbar_wait(&tfree[it & 1], (uint32_t)((it - 2) >> 1) & 1u)) || *abort_flag) {
         *abort_flag = 1;
         okp = false;
         break;
       }
       unsigned char* sb = sm + st * kWgStage;
+      // A into tensor memory: lane t of block blk holds dY row (t & 63) of
+      // row shift kh = blk + (t >> 6), its 32 positions rounded
+      {
+        const int ar = t & 63, asw = ar & 7;
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+          const unsigned char* arow = sb + (blk + (t >> 6)) * kWgBlk + ar * 128;
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 x4 = *reinterpret_cast<const float4*>(arow + ((i ^ asw) << 4));
+            v[4 * i] = round_tf32(x4.x);
+            v[4 * i + 1] = round_tf32(x4.y);
+            v[4 * i + 2] = round_tf32(x4.z);
+            v[4 * i + 3] = round_tf32(x4.w);
+          }
+          tmem_st32(t_a + (uint32_t)((it & 1) * 64 + blk * 32) + lane_base, v);
+        }
+      }
       unsigned char* row = sb + r * 128;
       const int sw = r & 7;
-#pragma unroll
-      for (int kh = 0; kh < 3; ++kh)
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float4* p = reinterpret_cast<float4*>(row + kh * kWgBlk + (((4 * h + i) ^ sw) << 4));
-          *p = round4(*p);
-        }
       float x[16];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -461,11 +485,12 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
             round4(make_float4(x[4 * i], x[4 * i + 1], x[4 * i + 2], x[4 * i + 3]));
         *reinterpret_cast<float4*>(row + 5 * kWgBlk + off) = make_float4(b2[4 * i], b2[4 * i + 1], b2[4 * i + 2], b2[4 * i + 3]);
       }
+      tmem_st_wait();
+      tc_fence_before();
       fence_proxy_async();
       mbar_arrive(&ready[st]);
     }
     // ---- epilogue: TMEM lane = row
-    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const bool ok = named_bar_and(1, 128, mbar_wait(done, 0) && !*abort_flag);
     if (ok && c1 > c0) {
       tc_fence_after();
@@ -494,6 +519,7 @@ __global__ void __launch_bounds__(256, 1) k_conv_wgrad_tc(const __grid_constant_
   if (*abort_flag) {
     for (int i = 0; i < kWgStages; ++i) mbar_wait(&full[i], 0, 1 << 14);
     mbar_wait(done, 0, 1 << 14);
+    for (int i = 0; i < 2; ++i) mbar_wait(&tfree[i], 0, 1 << 14);
   }
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
