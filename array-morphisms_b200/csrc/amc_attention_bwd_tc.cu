@@ -608,12 +608,10 @@ int attention_bwd_tc(const float* Q, const float* K, const float* V, const float
   if (!rc) rc = make_tmap_2d_f32(&mV64, Vr, rows, kD, kD, 64);
   if (!rc) rc = make_tmap_2d_f32(&mKt, Kt, trows, (uint64_t)n, (uint64_t)n, 64);
   if (rc) return rc;
-  static bool attrs = false;
-  if (!attrs) {
-    AMC_CUDA(cudaFuncSetAttribute(k_attn_bwd_dkv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kKVSmem));
-    AMC_CUDA(cudaFuncSetAttribute(k_attn_bwd_dq_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kQSmem));
-    attrs = true;
-  }
+  static std::atomic<uint64_t> attr_dkv{0}, attr_dq{0};
+  rc = smem_attr_once(k_attn_bwd_dkv_tc, kKVSmem, attr_dkv);
+  if (!rc) rc = smem_attr_once(k_attn_bwd_dq_tc, kQSmem, attr_dq);
+  if (rc) return rc;
   const float scale_log2 = scale * 1.4426950408889634f;
   const dim3 grid(n / kTile, (unsigned)blocks);
   k_attn_bwd_dkv_tc<<<grid, kThreadsB, kKVSmem, s>>>(mK128, mV128, mQ64, mdO64, mQt, mdOt, LD, dK, dV, n, scale_log2,

@@ -526,18 +526,14 @@ int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, f
   if (!rc) rc = make_tmap_2d_f32(&mVt, Vt, (uint64_t)blocks * kD, (uint64_t)n, (uint64_t)n, 64);
   if (rc) return rc;
   const float scale_log2 = scale * 1.4426950408889634f;
-  static bool attr2 = false, attr1 = false;
+  static std::atomic<uint64_t> attr3{0}, attr1{0};
   if (n % 256 == 0) {
-    if (!attr2) {
-      AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc3, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes));
-      attr2 = true;
-    }
+    int rca = smem_attr_once(k_attn_fwd_tc3, kSmem3Bytes, attr3);
+    if (rca) return rca;
     k_attn_fwd_tc3<<<dim3(n / 256, (unsigned)blocks), kThreads3, kSmem3Bytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
   } else {
-    if (!attr1) {
-      AMC_CUDA(cudaFuncSetAttribute(k_attn_fwd_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-      attr1 = true;
-    }
+    int rca = smem_attr_once(k_attn_fwd_tc, kSmemBytes, attr1);
+    if (rca) return rca;
     k_attn_fwd_tc<<<dim3(n / kBM, (unsigned)blocks), 128, kSmemBytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
   }
   e = cudaGetLastError();

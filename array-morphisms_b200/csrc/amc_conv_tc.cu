@@ -275,11 +275,9 @@ static int conv_run(const float* in, const float* W, float* out, const ConvShape
   CUtensorMap mW;
   rc = make_tmap_2d_f32(&mW, Wt, 9 * 2 * kC, 32, 32, 64);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    AMC_CUDA(cudaFuncSetAttribute(k_conv3x3_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kConvSmem));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  rc = smem_attr_once(k_conv3x3_tc, kConvSmem, attr);
+  if (rc) return rc;
   const int ntiles = s.N * (s.H / 2);
   const int grid = ntiles < num_sms() ? ntiles : num_sms();
   k_conv3x3_tc<<<grid, kConvThreads, kConvSmem, st>>>(in, mW, out, s.N, s.H, s.W);
@@ -571,11 +569,9 @@ int conv_wgrad_tc(const float* X, const float* dY, float* dW, const ConvShape& s
   if (!rc) rc = make_tmap_2d_f32(&mX, X, rows, (uint64_t)HW, (uint64_t)HW, 64);
   if (!rc) rc = make_tmap_2d_f32_box(&mXh, X, rows, (uint64_t)HW, (uint64_t)HW, 4, 64, false);
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    AMC_CUDA(cudaFuncSetAttribute(k_conv_wgrad_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kWgSmem));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  rc = smem_attr_once(k_conv_wgrad_tc, kWgSmem, attr);
+  if (rc) return rc;
   k_conv_wgrad_tc<<<grid, 256, kWgSmem, st>>>(mDY, mX, mXh, parts, s.N, HW, s.W, cpi);
   AMC_CUDA(cudaGetLastError());
   k_wgrad_reduce<<<kC * kC * 9 / 32, 256, 0, st>>>(parts, dW, grid, counts);

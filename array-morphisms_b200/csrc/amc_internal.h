@@ -52,6 +52,22 @@ int buf_alloc(int32_t dtype, int64_t nelem, uint64_t* out);
 
 cudaStream_t default_stream();
 inline cudaStream_t pick_stream(void* s) { return s ? (cudaStream_t)s : default_stream(); }
+
+// Raise the dynamic shared-memory limit of kernel `fn` to `bytes` on the
+// current device, once per device (a function attribute applies to one
+// device; `done` holds one bit per device ordinal).
+template <typename F>
+inline int smem_attr_once(F* fn, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return 0;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute");
+  done.fetch_or(bit, std::memory_order_release);
+  return 0;
+}
 int num_sms();
 
 // ------------------------------------------------------------------ device descriptors

@@ -59,11 +59,9 @@ __global__ void __launch_bounds__(128, 1) k_tc_peak(int iters, int warps) {
 
 template <int N>
 static int run_peak(int iters, int warps, cudaStream_t s, float* ms) {
-  static bool attr = false;
-  if (!attr) {
-    AMC_CUDA(cudaFuncSetAttribute(k_tc_peak<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, kPeakSmem));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr{0};
+  const int rc = smem_attr_once(k_tc_peak<N>, kPeakSmem, attr);
+  if (rc) return rc;
   const int sms = num_sms();
   cudaEvent_t a, b;
   AMC_CUDA(cudaEventCreate(&a));
