@@ -84,9 +84,44 @@ def max_over_ranks(ws, v: float) -> float:
 
 
 class Clocks:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled during the timed
+    region: NVML every 2 ms on a thread (short regions get samples too), or
+    nvidia-smi -lms 200 when NVML is unavailable.  Only reads settings."""
+
+    REASONS = (("hw_slowdown", 0x8), ("sw_power_cap", 0x4), ("sw_thermal_slowdown", 0x20),
+               ("hw_thermal_slowdown", 0x40))
 
     def __init__(self, gpu: int):
+        self.samples, self.mask, self.mx, self.p, self.h = [], 0, None, None, None
+        try:
+            import threading
+            import pynvml
+            import torch
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            try:   # the physical GPU behind CUDA device `gpu`
+                self.h = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + str(torch.cuda.get_device_properties(gpu).uuid))
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu)
+            self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.run = True
+            self.t = threading.Thread(target=self._loop, daemon=True)
+            self.t.start()
+        except Exception:
+            self.h = None
+            self._start_smi(gpu)
+
+    def _loop(self):
+        nv = self.nv
+        while self.run:
+            try:
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+                self.mask |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
+            except Exception:
+                pass
+            time.sleep(0.002)
+
+    def _start_smi(self, gpu):
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -98,6 +133,13 @@ class Clocks:
             self.p = None
 
     def stop(self):
+        if self.h is not None:
+            self.run = False
+            self.t.join(timeout=2)
+            sm = sorted(self.samples)
+            reasons = sorted(n for n, bit in self.REASONS if self.mask & bit)
+            return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": self.mx, "reasons": reasons,
+                    "samples": len(sm), "source": "nvml"}
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.25)
@@ -121,7 +163,7 @@ class Clocks:
                 continue
         sm.sort()
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------- reference arm / CPU baseline
