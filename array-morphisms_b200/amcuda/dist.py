@@ -7,7 +7,8 @@ across ranks:
     images for Y and dX) need no exchange;
   - a reduction that crosses the batch axis (the linear-regression gradient,
     the conv weight gradient) is combined with a deterministic all-reduce:
-    an all-gather of each rank's partial followed by a sum in rank order, so
+    an all-gather of each rank's partial followed by one fixed-order sum over
+    the rank axis, so
     results do not depend on the collective's internal reduction order.
 """
 from __future__ import annotations
@@ -25,18 +26,23 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
 
 
 def allreduce_fixed_order(t, group=None):
-    """In-place sum of `t` over ranks, added in rank order 0..world-1."""
+    """In-place sum of `t` over ranks in a fixed order: one all-gather of every
+    rank's copy into a (world, n) buffer, then one sum over the rank axis.
+    The result does not depend on the collective's internal reduction order
+    and is the same on every rank and every run."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
     if world == 1:
         return t
-    parts = [torch.empty_like(t) for _ in range(world)]
-    dist.all_gather(parts, t.contiguous(), group=group)
-    acc = parts[0].clone()
-    for p in parts[1:]:
-        acc += p
-    t.copy_(acc)
+    flat = t.contiguous().view(-1)
+    buf = torch.empty((world, flat.numel()), dtype=t.dtype, device=t.device)
+    try:
+        dist.all_gather_into_tensor(buf, flat, group=group)
+    except (RuntimeError, NotImplementedError, AttributeError):
+        parts = list(buf.unbind(0))
+        dist.all_gather(parts, flat, group=group)
+    t.copy_(buf.sum(dim=0).view_as(t))
     return t
 
 

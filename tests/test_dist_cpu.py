@@ -1,5 +1,5 @@
 """Multi-rank host logic on CPU: world_size 2 gloo ranks shard rows of the
-linear-regression problem and combine with the rank-ordered all-reduce; the
+linear-regression problem and combine with the fixed-order all-reduce; the
 result must match the unsharded oracle.  Also checks shard_range."""
 import os
 import socket
