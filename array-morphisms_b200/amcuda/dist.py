@@ -25,25 +25,41 @@ def shard_range(n: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
-def allreduce_fixed_order(t, group=None):
+class PendingReduce:
+    """An all-reduce started with async_op=True: wait() finishes it."""
+
+    def __init__(self, t, buf, work):
+        self.t, self.buf, self.work = t, buf, work
+
+    def wait(self):
+        if self.work is not None:
+            self.work.wait()   # orders the current stream after the collective
+            self.work = None
+        self.t.copy_(self.buf.sum(dim=0).view_as(self.t))
+        return self.t
+
+
+def allreduce_fixed_order(t, group=None, async_op: bool = False):
     """In-place sum of `t` over ranks in a fixed order: one all-gather of every
     rank's copy into a (world, n) buffer, then one sum over the rank axis.
     The result does not depend on the collective's internal reduction order
-    and is the same on every rank and every run."""
+    and is the same on every rank and every run.  With async_op=True the
+    all-gather is only started and a PendingReduce is returned; its wait()
+    orders the current stream after it and forms the sum, so independent work
+    can run in between."""
     import torch
     import torch.distributed as dist
     world = dist.get_world_size(group)
     if world == 1:
-        return t
+        return PendingReduce(t, t.view(1, -1), None) if async_op else t
     flat = t.contiguous().view(-1)
     buf = torch.empty((world, flat.numel()), dtype=t.dtype, device=t.device)
     try:
-        dist.all_gather_into_tensor(buf, flat, group=group)
+        work = dist.all_gather_into_tensor(buf, flat, group=group, async_op=async_op)
     except (RuntimeError, NotImplementedError, AttributeError):
-        parts = list(buf.unbind(0))
-        dist.all_gather(parts, flat, group=group)
-    t.copy_(buf.sum(dim=0).view_as(t))
-    return t
+        work = dist.all_gather(list(buf.unbind(0)), flat, group=group, async_op=async_op)
+    pending = PendingReduce(t, buf, work if async_op else None)
+    return pending if async_op else pending.wait()
 
 
 class ShardedLinearRegression:

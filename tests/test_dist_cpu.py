@@ -84,3 +84,34 @@ def test_sharded_linreg_matches_oracle_two_gloo_ranks():
         np.testing.assert_allclose(w, w_ref, rtol=1e-12, atol=1e-14)
         np.testing.assert_allclose(losses, l_ref, rtol=1e-12)
     np.testing.assert_array_equal(res[0][1], res[1][1])  # replicas stay identical
+
+
+def _async_worker(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    from amcuda.dist import allreduce_fixed_order
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        t = torch.arange(6, dtype=torch.float64) * (rank + 1)
+        p = allreduce_fixed_order(t, async_op=True)
+        p.wait()
+        out[rank] = t.tolist()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_allreduce_async_matches_sum():
+    """The started-then-waited form gives the same sum on every rank."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    mgr = ctx.Manager()
+    out = mgr.dict()
+    ps = [ctx.Process(target=_async_worker, args=(r, 2, port, out)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(60)
+        assert p.exitcode == 0
+    expect = [float(i * 3) for i in range(6)]
+    assert out[0] == expect and out[1] == expect
