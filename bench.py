@@ -547,14 +547,14 @@ def bench_other(args, ws, rank, local):
         yy, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(wt)
 
         def run():
-            # dW first: its sum over the batch shards (fixed-order all-reduce)
-            # runs on NCCL's stream while the forward and data gradient compute
-            W.conv2d_wgrad(x, dy, dw)
-            pending = allreduce_fixed_order(dw, async_op=True) if ws > 1 else None
             W.conv2d_fwd(x, wt, yy)
             W.conv2d_dgrad(dy, wt, dx)
-            if pending is not None:
-                pending.wait()
+            W.conv2d_wgrad(x, dy, dw)
+            if ws > 1:
+                # dW sums over the batch shards: fixed-order all-reduce.  It is
+                # not overlapped with the next pass: NCCL's kernel would hold SMs
+                # that the one-CTA-per-SM conv kernels wait for (measured slower).
+                allreduce_fixed_order(dw)
         work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
         unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward + data gradient + weight gradient TFLOP/s"
         pre = lambda: None
