@@ -83,6 +83,8 @@ constexpr int kMaxLeaves = 8;
 struct DProg {
   int32_t n;
   int32_t all_float;     // every load is f32/f64 and no ICONST: inexact-only evaluation
+  int32_t max_depth;     // deepest stack the program reaches
+  int32_t _pad;
   amc_insn code[AMC_PROG_MAX];
 };
 

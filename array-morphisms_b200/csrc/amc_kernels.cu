@@ -372,24 +372,97 @@ __device__ __forceinline__ void fold_row(Acc& A, int op, int out_dtype, bool src
   }
 }
 
+// Small float programs (at most 2 leaves, stack depth at most 3) of a
+// reduction over one kept and one reduced axis: the source values of kSmallV
+// elements are gathered first (all loads in flight together: the cost of an
+// element is one memory latency, not one per LOAD instruction), then the
+// program runs on named registers: the leaf values and the three stack slots
+// are selected by switches on warp-uniform indices, so nothing goes to local
+// memory.  Values and rounding are those of eval_prog_f.
+constexpr int kSmallV = 4;
+
+__device__ __forceinline__ double small_unary(int op, int cvt, double x) {
+  if (op == AMC_OP_CVT) return cvt == AMC_F64 ? x : cvt == AMC_F32 ? (double)__double2float_rn(x) : round_f(cvt, x);
+  return un_f(op, x);
+}
+
+__device__ __forceinline__ void eval_small(const ReduceArgs& a, const long long (&o)[kSmallV],
+                                           const long long (&r)[kSmallV], double (&out)[kSmallV]) {
+  double l0[kSmallV], l1[kSmallV];
+#pragma unroll
+  for (int v = 0; v < kSmallV; ++v) {
+    l0[v] = load_f(a.leaf_o[0].ptr, a.leaf_o[0].dtype, o[v] * a.leaf_o[0].strides[0] + r[v] * a.leaf_r[0][0]);
+    l1[v] = a.nleaf > 1
+                ? load_f(a.leaf_o[1].ptr, a.leaf_o[1].dtype, o[v] * a.leaf_o[1].strides[0] + r[v] * a.leaf_r[1][0])
+                : 0.0;
+  }
+#pragma unroll
+  for (int v = 0; v < kSmallV; ++v) {
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0;
+    int sp = 0;
+    for (int pc = 0; pc < a.prog.n; ++pc) {
+      const amc_insn I = a.prog.code[pc];
+      if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST) {
+        const double t = I.op == AMC_OP_CONST ? I.imm : (I.a == 0 ? l0[v] : l1[v]);
+        if (sp == 0) s0 = t;
+        else if (sp == 1) s1 = t;
+        else s2 = t;
+        ++sp;
+      } else if (I.op < AMC_OP_ADD) {
+        if (sp == 1) s0 = small_unary(I.op, I.a, s0);
+        else if (sp == 2) s1 = small_unary(I.op, I.a, s1);
+        else s2 = small_unary(I.op, I.a, s2);
+      } else {
+        if (sp == 2) s0 = bin_f(I.op, s0, s1);
+        else s1 = bin_f(I.op, s1, s2);
+        --sp;
+      }
+    }
+    out[v] = s0;
+  }
+}
+
 template <int FOLD>
-__global__ void __launch_bounds__(256) k_reduce_seq(const __grid_constant__ ReduceArgs a, int OT, int RC, int ofast) {
+__global__ void __launch_bounds__(256, 4) k_reduce_seq(const __grid_constant__ ReduceArgs a, int OT, int RC, int ofast) {
   extern __shared__ unsigned long long smem_u64[];
   const bool src_exact = !dtype_is_float_d(a.src_dtype);
+  const bool small = a.prog.all_float && a.prog.max_depth <= 3 && a.nleaf <= 2 && a.orank == 1 && a.rrank == 1;
   const long long o0 = (long long)blockIdx.x * OT;
   Acc A;
   acc_init(A, a.op, a.out_dtype);
   for (long long r0 = 0; r0 < a.R; r0 += RC) {
     int rc = (int)((a.R - r0) < RC ? (a.R - r0) : RC);
     int tile = OT * rc;
-    for (int e = threadIdx.x; e < tile; e += blockDim.x) {
-      int ol, rl;
-      if (ofast) { ol = e % OT; rl = e / OT; } else { ol = e / rc; rl = e % rc; }
-      long long o = o0 + ol;
-      if (o >= a.O) continue;
-      double vf; long long vi;
-      eval_src(a, o, r0 + rl, vf, vi);
-      smem_u64[ol * (RC + 1) + rl] = src_exact ? (unsigned long long)vi : __double_as_longlong(vf);
+    if (small) {
+      for (int e0 = threadIdx.x; e0 < tile; e0 += blockDim.x * kSmallV) {
+        long long oo[kSmallV], rr[kSmallV];
+        int slot[kSmallV];
+#pragma unroll
+        for (int k = 0; k < kSmallV; ++k) {
+          const int e = e0 + k * blockDim.x;
+          int ol = 0, rl = 0;
+          if (ofast) { ol = e % OT; rl = e / OT; } else { ol = e / rc; rl = e % rc; }
+          const bool valid = e < tile && o0 + ol < a.O;
+          slot[k] = valid ? ol * (RC + 1) + rl : -1;
+          oo[k] = valid ? o0 + ol : 0;   // element (0, 0) of every leaf: in bounds, unused
+          rr[k] = valid ? r0 + rl : 0;
+        }
+        double v[kSmallV];
+        eval_small(a, oo, rr, v);
+#pragma unroll
+        for (int k = 0; k < kSmallV; ++k)
+          if (slot[k] >= 0) smem_u64[slot[k]] = __double_as_longlong(v[k]);
+      }
+    } else {
+      for (int e = threadIdx.x; e < tile; e += blockDim.x) {
+        int ol, rl;
+        if (ofast) { ol = e % OT; rl = e / OT; } else { ol = e / rc; rl = e % rc; }
+        long long o = o0 + ol;
+        if (o >= a.O) continue;
+        double vf; long long vi;
+        eval_src(a, o, r0 + rl, vf, vi);
+        smem_u64[ol * (RC + 1) + rl] = src_exact ? (unsigned long long)vi : __double_as_longlong(vf);
+      }
     }
     __syncthreads();
     if (threadIdx.x < OT && o0 + threadIdx.x < a.O)

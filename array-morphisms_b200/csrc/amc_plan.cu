@@ -258,6 +258,13 @@ struct Builder {
     for (auto& L : leaves)
       if (!dtype_float(L.dtype)) allf = false;
     P.all_float = allf ? 1 : 0;
+    int sp = 0, mx = 0;
+    for (auto& I : prog) {
+      if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST || I.op == AMC_OP_ICONST) ++sp;
+      else if (I.op >= AMC_OP_ADD) --sp;   // binary operators and comparisons pop one
+      mx = sp > mx ? sp : mx;
+    }
+    P.max_depth = mx;
     for (size_t i = 0; i < prog.size(); ++i) P.code[i] = prog[i];
   }
 
