@@ -19,10 +19,13 @@
 // products whose contraction runs over queries or keys read transposed,
 // tf32-rounded copies (Q^T, dO^T, K^T) that a pre-pass writes together with
 // rounded copies of Q, K, V, dO and the per-row (lse * log2 e, D) pairs.
-// Three S/dP tensor-memory buffers let the MMAs of the next two tiles run
-// while the threads work on the current one; two warpgroups share each tile,
-// one taking its first 32 columns, the other the last 32.  Every wait is
-// bounded; on expiry the kernel records AMC_ERR_TIMEOUT, drains and returns.
+// S/dP tensor-memory buffers (three in the dK/dV kernel, two in the dQ
+// kernel, whose other columns hold Q and dO) let the products of the next
+// tiles run while the threads work on the current one; two warpgroups share
+// each tile, one taking its first 32 columns, the other the last 32.  One
+// warp issues the S/dP products, another the accumulating ones.  Every wait
+// is bounded; on expiry the kernel records AMC_ERR_TIMEOUT, drains and
+// returns.
 #include <cmath>
 #include <mutex>
 #include <unordered_map>

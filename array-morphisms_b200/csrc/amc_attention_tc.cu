@@ -1,6 +1,8 @@
 // Tensor-core attention forward (sm_100a, tcgen05 kind::tf32).
 //
-// One CTA computes 128 query rows of one (batch, head) block, one thread per
+// Two kernels: k_attn_fwd_tc3 (below: 256 query rows per CTA, n a multiple of
+// 256) and k_attn_fwd_tc for n a multiple of 128 only.  The latter:
+// one CTA computes 128 query rows of one (batch, head) block, one thread per
 // row.  For each 128-key tile:
 //   S  = Q K^T      tcgen05.mma M=128 N=128 K=64, operands K-major in shared
 //                   memory (TMA, 128-byte swizzle), accumulator in TMEM
