@@ -239,9 +239,89 @@ static unsigned grid_for(long long total, int block) {
   return (unsigned)g;
 }
 
+// ------------------------------------------------------------------ view copies
+// A pure copy (one leaf, same dtype) of a strided view in logical row-major
+// order whose innermost axis is not the source's unit-stride axis while
+// another axis t is (a transposed view): 32 x 32 tiles of (t, innermost) go
+// through shared memory, so the reads run along t and the writes along the
+// innermost output axis, both coalesced.  Values are copied bit for bit.
+template <typename T>
+__global__ void __launch_bounds__(256) k_copy_tiled(const __grid_constant__ MapArgs a, int t) {
+  __shared__ T tile[32][33];
+  const int r = a.rank, last = r - 1;
+  const long long nt = a.shape[t], nl = a.shape[last];
+  const long long tiles_l = (nl + 31) / 32, tiles_t = (nt + 31) / 32;
+  long long ostr[AMC_MAX_RANK];
+  long long acc = 1, batch = 1;
+  for (int d = r - 1; d >= 0; --d) {
+    ostr[d] = acc;
+    acc *= a.shape[d];
+    if (d != t && d != last) batch *= a.shape[d];
+  }
+  const T* src = (const T*)a.leaf[0].ptr;
+  T* out = (T*)a.out;
+  const long long st_t = a.leaf[0].strides[t], st_l = a.leaf[0].strides[last];
+  const long long ntile = batch * tiles_t * tiles_l;
+  for (long long tl = blockIdx.x; tl < ntile; tl += gridDim.x) {
+    long long rem = tl;
+    const long long il = rem % tiles_l;
+    rem /= tiles_l;
+    const long long it = rem % tiles_t;
+    rem /= tiles_t;
+    long long soff = 0, ooff = 0;
+    for (int d = r - 1; d >= 0; --d) {
+      if (d == t || d == last) continue;
+      const long long c = rem % a.shape[d];
+      rem /= a.shape[d];
+      soff += c * a.leaf[0].strides[d];
+      ooff += c * ostr[d];
+    }
+    const long long t0 = it * 32, l0 = il * 32;
+    for (int k = threadIdx.y; k < 32; k += 8) {   // reads: threadIdx.x along t
+      const long long ti = t0 + threadIdx.x, li = l0 + k;
+      if (ti < nt && li < nl) tile[k][threadIdx.x] = src[soff + ti * st_t + li * st_l];
+    }
+    __syncthreads();
+    for (int k = threadIdx.y; k < 32; k += 8) {   // writes: threadIdx.x along the innermost axis
+      const long long ti = t0 + k, li = l0 + threadIdx.x;
+      if (ti < nt && li < nl) out[ooff + ti * ostr[t] + li] = tile[threadIdx.x][k];
+    }
+    __syncthreads();
+  }
+}
+
+// The unit-stride source axis of a pure same-dtype view copy that the tiled
+// copy can take, or -1.
+static int tiled_copy_axis(const MapArgs& a) {
+  if (a.nleaf != 1 || a.rank < 2 || a.leaf[0].dtype != a.out_dtype) return -1;
+  const bool load_only = a.prog.n == 1 && a.prog.code[0].op == AMC_OP_LOAD && a.prog.code[0].a == 0;
+  const bool load_cvt_same = a.prog.n == 2 && a.prog.code[0].op == AMC_OP_LOAD && a.prog.code[0].a == 0 &&
+                             a.prog.code[1].op == AMC_OP_CVT && a.prog.code[1].a == a.out_dtype;
+  if (!load_only && !load_cvt_same) return -1;
+  const int last = a.rank - 1;
+  if (a.leaf[0].strides[last] == 1 || a.shape[last] < 2) return -1;
+  for (int d = 0; d < last; ++d)
+    if (a.leaf[0].strides[d] == 1 && a.shape[d] > 1) return d;
+  return -1;
+}
+
 int launch_map(const MapArgs& a, cudaStream_t s) {
   if (a.total == 0) return AMC_OK;
   if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "map: injected launch failure (AMC_FAULT=launch)");
+  const int t = tiled_copy_axis(a);
+  if (t >= 0) {
+    const int esz = dtype_size(a.out_dtype);
+    const long long tiles = (a.total / (a.shape[t] * a.shape[a.rank - 1])) * ((a.shape[t] + 31) / 32) *
+                            ((a.shape[a.rank - 1] + 31) / 32);
+    // one tile per CTA where the grid allows: many resident CTAs hide the
+    // load latency that each tile's barrier exposes
+    const long long cap = 0x7fffffffLL;
+    const unsigned g = (unsigned)(tiles < cap ? (tiles < 1 ? 1 : tiles) : cap);
+    if (esz == 8) k_copy_tiled<unsigned long long><<<g, dim3(32, 8), 0, s>>>(a, t);
+    else k_copy_tiled<unsigned int><<<g, dim3(32, 8), 0, s>>>(a, t);
+    AMC_CUDA(cudaGetLastError());
+    return AMC_OK;
+  }
   unsigned g = grid_for(a.total, 256);
   if (a.prog.all_float) k_map<true><<<g, 256, 0, s>>>(a);
   else k_map<false><<<g, 256, 0, s>>>(a);

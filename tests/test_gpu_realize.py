@@ -214,6 +214,22 @@ def test_conv_pattern_lowering(amc, C, H, W, K, ksz, stride, pad, tol):
     assert np.max(np.abs(got - ref)) <= tol * np.max(np.abs(ref))
 
 
+@pytest.mark.parametrize("shape,perm,dt", [((100, 70), (1, 0), "f64"), ((3, 50, 40), (0, 2, 1), "s32"),
+                                           ((20, 33, 45), (2, 0, 1), "f32"), ((7, 5, 64, 3), (1, 3, 0, 2), "s64")])
+def test_transposed_view_copy(amc, shape, perm, dt):
+    """A reshape of a transposed view copies it in logical row-major order
+    (execute-affine-morphism, realization.scm:849-862); the copy goes through
+    shared-memory tiles when the source's unit-stride axis is not innermost.
+    Bit-exact against the oracle."""
+    rng = np.random.default_rng(21)
+    x = _rand(rng, shape, dt)
+    n = int(np.prod(shape))
+    e = amc.morph_reshape(amc.morph_transpose(amc.morph_from_numpy(x), perm), (n,))
+    got, ref = amc.realize(e).values(), oracle.realize(e).values()
+    assert np.array_equal(np.asarray(got), np.asarray(ref))
+    assert np.array_equal(np.asarray(got).reshape(-1), np.transpose(x, perm).reshape(-1))
+
+
 def test_plan_rejects_bad_trees(amc):
     a = amc.morph_from_numpy(np.zeros((4, 4)))
     with pytest.raises(ValueError):
