@@ -110,7 +110,7 @@ SIGNATURES = {
     "amc_conv2d_fwd_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
     "amc_conv2d_dgrad_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
     "amc_conv2d_wgrad_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
-    "amc_tc_peak_tf32": [_I32, _I32, _I32, _P, _P],
+    "amc_tc_peak_tf32": [_I32, _I32, _I32, _I32, _P, _P],
 }
 
 _lib = None

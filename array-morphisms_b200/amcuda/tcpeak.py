@@ -2,10 +2,12 @@
 
     python -m amcuda.tcpeak        (with array-morphisms_b200 on sys.path)
 
-Each row: M=128 x N x K=8 products issued back to back from shared-memory
-operands by 1, 2 or 4 threads per SM (amc_tc_peak_tf32).  The N=256 row is
-the dense TF32 peak; the smaller N rows show the per-instruction issue floor
-that the attention and convolution tiles (N=64) run against."""
+Each row: M=128 x N x K=8 products issued back to back by 1, 2 or 4 threads
+per SM (amc_tc_peak_tf32), B read from shared memory and A from shared memory
+("smem") or tensor memory ("tmem").  The N=256 row is the dense TF32 peak.
+The last column is the shared-memory operand bytes per product over the
+clocks it took: at about 128 B/clock the product is bound by the
+shared-memory read port, not by the pipe."""
 from __future__ import annotations
 
 
@@ -23,17 +25,20 @@ def main() -> None:
         pass
     import torch
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    print("| N | issuing threads/SM | TFLOP/s | SM clocks per MMA |")
-    print("|---|---|---|---|")
-    for n in (32, 64, 128, 256):
-        for w in (1, 2, 4):
-            if n * w > 512:
-                continue
-            tf = W.tc_peak_tf32(4000, n, w)
-            per = ""
-            if clk_ghz:
-                per = f"{2 * 128 * n * 8 * sms * clk_ghz * 1e9 / (tf * 1e12):.1f}"
-            print(f"| {n} | {w} | {tf:.1f} | {per} |")
+    print("| A from | N | issuing threads/SM | TFLOP/s | SM clocks per MMA | shared-memory B/clock |")
+    print("|---|---|---|---|---|---|")
+    for a_tmem in (False, True):
+        for n in (32, 64, 128, 256):
+            for w in (1, 2, 4):
+                if n * w > (480 if a_tmem else 512):
+                    continue
+                tf = W.tc_peak_tf32(4000, n, w, a_tmem)
+                per = bw = ""
+                if clk_ghz:
+                    clocks = 2 * 128 * n * 8 * sms * clk_ghz * 1e9 / (tf * 1e12)
+                    smem_bytes = n * 32 + (0 if a_tmem else 128 * 32)
+                    per, bw = f"{clocks:.1f}", f"{smem_bytes / clocks:.0f}"
+                print(f"| {'tmem' if a_tmem else 'smem'} | {n} | {w} | {tf:.1f} | {per} | {bw} |")
     if clk_ghz:
         print(f"\nSM clock sampled after the sweep: {clk_ghz * 1000:.0f} MHz, {sms} SMs")
 

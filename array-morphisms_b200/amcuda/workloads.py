@@ -281,11 +281,12 @@ def c1_inputs_morph(dtype="f64", n=1 << 20):
     return morph_from_numpy(x, dtype), morph_from_numpy(y, dtype)
 
 
-def tc_peak_tf32(iters: int = 4000, n: int = 256, warps: int = 1, stream=None) -> float:
+def tc_peak_tf32(iters: int = 4000, n: int = 256, warps: int = 1, a_tmem: bool = False, stream=None) -> float:
     """TFLOP/s reached by back-to-back tcgen05 kind::tf32 products of M=128,
-    N=n from `warps` issuing threads per SM (amc_tc_peak_tf32).  The default
+    N=n from `warps` issuing threads per SM (amc_tc_peak_tf32), with A read
+    from shared memory or, if `a_tmem`, from tensor memory.  The default
     shape gives the dense TF32 peak, the roofline denominator of the
     tensor-core kernels."""
     out = C.c_double(0.0)
-    A.call("amc_tc_peak_tf32", n, warps, iters, C.byref(out), _stream(stream))
+    A.call("amc_tc_peak_tf32", n, warps, int(bool(a_tmem)), iters, C.byref(out), _stream(stream))
     return out.value

@@ -240,5 +240,9 @@ int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 // 128-byte swizzle, plain row-major boxes.
 int make_tmap_2d_f32_box(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                          uint32_t box_cols, uint32_t box_rows, bool swizzle128);
+// Any of the 0-, 32- and 128-byte swizzles; a swizzled box row is exactly the
+// swizzle width (8 floats for 32 bytes: the K-major SW32 operand layout).
+int make_tmap_2d_f32_swz(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                         uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
 
 }  // namespace amc

@@ -345,10 +345,12 @@ int amc_conv2d_wgrad_f32(const float* X, const float* dY, float* dW, int32_t N, 
 /* Tensor-core throughput probe (diagnostic; no reference counterpart): one
  * CTA per SM, `warps` (1..4) threads each issue iters x 4 back-to-back
  * tcgen05.mma kind::tf32 products of M=128, N=n (32, 64, 128 or 256), K=8
- * from shared memory into their own accumulator; *tflops receives the rate
- * reached.  n=256 with one warp gives the dense TF32 peak, the roofline
- * denominator of the tensor-core kernels.  Synchronizes the stream. */
-int amc_tc_peak_tf32(int32_t n, int32_t warps, int32_t iters, double* tflops, void* stream);
+ * into their own accumulator.  B is read from shared memory; A from shared
+ * memory (a_tmem = 0) or from tensor memory (a_tmem = 1).  *tflops receives
+ * the rate reached.  n=256 with one warp and a_tmem = 0 gives the dense TF32
+ * peak, the roofline denominator of the tensor-core kernels.  Synchronizes
+ * the stream. */
+int amc_tc_peak_tf32(int32_t n, int32_t warps, int32_t a_tmem, int32_t iters, double* tflops, void* stream);
 
 #ifdef __cplusplus
 }

@@ -257,3 +257,6 @@ def test_tc_peak_probe(amc):
     from amcuda import workloads as W
     v = W.tc_peak_tf32(2000)
     assert 300.0 < v < 3000.0, v
+    # the same products with A read from tensor memory
+    v = W.tc_peak_tf32(2000, 64, 2, a_tmem=True)
+    assert 300.0 < v < 3000.0, v
