@@ -552,6 +552,471 @@ __global__ void __launch_bounds__(256, 4) k_reduce_seq(const __grid_constant__ R
   if (threadIdx.x < OT && o0 + threadIdx.x < a.O) acc_store(A, a.out, a.out_dtype, a.op, a.R, o0 + threadIdx.x);
 }
 
+// Staged ordered reduction for one kept and one reduced axis with outputs
+// adjacent in memory and a small program (at most 2 leaves, stack depth 3),
+// float or exact.  k_reduce_seq gives each CTA only a couple of outputs when
+// there are few of them, so every warp load uses a fraction of a 32-byte
+// sector from many rows and the L2 request rate, not bandwidth, bounds the
+// gather.  Here a CTA owns OT (8) consecutive outputs, so a warp load covers
+// whole sectors, and the raw leaf values of the whole (OT x rc) tile are
+// copied into shared memory with cp.async, all in flight at once and holding
+// no registers.  The program then runs from shared memory (values and
+// rounding as eval_prog / eval_prog_f), and the fold is the same ascending
+// chain as k_reduce_seq, with its shared loads issued a batch ahead.
+__device__ __forceinline__ void cp_async_elem(void* dst, const void* src, int bytes) {
+  if (bytes == 8)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Named barrier over `count` threads (whole warps).
+__device__ __forceinline__ void named_bar(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+__device__ __forceinline__ int dtype_bytes_d(int d) { return (d == AMC_F32 || d == AMC_S32 || d == AMC_U32) ? 4 : 8; }
+
+__device__ __forceinline__ double raw_f(unsigned long long raw, int dtype) {
+  return dtype == AMC_F32 ? (double)__int_as_float((int)(unsigned)raw) : __longlong_as_double((long long)raw);
+}
+__device__ __forceinline__ Num raw_num(unsigned long long raw, int dtype) {
+  switch (dtype) {
+    case AMC_F32: return nfl((double)__int_as_float((int)(unsigned)raw));
+    case AMC_F64: return nfl(__longlong_as_double((long long)raw));
+    case AMC_S32: return nex((long long)(int)(unsigned)raw);
+    case AMC_U32: return nex((long long)(unsigned)raw);
+    default: return nex((long long)raw);
+  }
+}
+
+// One element of a small program on named registers (stack slots s0..s2).
+template <bool EXACT>
+__device__ __forceinline__ void eval_staged(const DProg& P, const DLeaf* L, unsigned long long r0,
+                                            unsigned long long r1, double& vf, long long& vi) {
+  if (!EXACT) {
+    const double l0 = raw_f(r0, L[0].dtype), l1 = raw_f(r1, L[1].dtype);
+    double s0 = 0.0, s1 = 0.0, s2 = 0.0;
+    int sp = 0;
+    for (int pc = 0; pc < P.n; ++pc) {
+      const amc_insn I = P.code[pc];
+      if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST) {
+        const double t = I.op == AMC_OP_CONST ? I.imm : (I.a == 0 ? l0 : l1);
+        if (sp == 0) s0 = t;
+        else if (sp == 1) s1 = t;
+        else s2 = t;
+        ++sp;
+      } else if (I.op < AMC_OP_ADD) {
+        if (sp == 1) s0 = small_unary(I.op, I.a, s0);
+        else if (sp == 2) s1 = small_unary(I.op, I.a, s1);
+        else s2 = small_unary(I.op, I.a, s2);
+      } else {
+        if (sp == 2) s0 = bin_f(I.op, s0, s1);
+        else s1 = bin_f(I.op, s1, s2);
+        --sp;
+      }
+    }
+    vf = s0;
+    vi = 0;
+  } else {
+    const Num l0 = raw_num(r0, L[0].dtype), l1 = raw_num(r1, L[1].dtype);
+    Num s0 = nex(0), s1 = nex(0), s2 = nex(0);
+    int sp = 0;
+    for (int pc = 0; pc < P.n; ++pc) {
+      const amc_insn I = P.code[pc];
+      if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST || I.op == AMC_OP_ICONST) {
+        const Num t = I.op == AMC_OP_CONST ? nfl(I.imm) : I.op == AMC_OP_ICONST ? nex((long long)I.imm) : (I.a == 0 ? l0 : l1);
+        if (sp == 0) s0 = t;
+        else if (sp == 1) s1 = t;
+        else s2 = t;
+        ++sp;
+      } else if (I.op == AMC_OP_CVT) {
+        if (sp == 1) s0 = round_store(I.a, s0);
+        else if (sp == 2) s1 = round_store(I.a, s1);
+        else s2 = round_store(I.a, s2);
+      } else if (I.op < AMC_OP_ADD) {
+        if (sp == 1) s0 = un_op(I.op, s0);
+        else if (sp == 2) s1 = un_op(I.op, s1);
+        else s2 = un_op(I.op, s2);
+      } else {
+        if (sp == 2) s0 = bin_op(I.op, s0, s1);
+        else s1 = bin_op(I.op, s1, s2);
+        --sp;
+      }
+    }
+    vf = as_f(s0);
+    vi = trunc_i(s0);
+  }
+}
+
+// fold of one output row with the shared loads issued a batch of 8 ahead of
+// the dependent additions (same order and rounding as fold_row)
+template <int FOLD>
+__device__ __forceinline__ void fold_row_pipelined(Acc& A, int op, int out_dtype, bool src_exact,
+                                                   const unsigned long long* __restrict__ row, int rc) {
+  if (FOLD == 0) {
+    fold_row<0>(A, op, out_dtype, src_exact, row, rc);
+    return;
+  }
+  constexpr int B = 8;
+  unsigned long long cur[B], nxt[B];
+  int rl = 0;
+  if (rc >= B) {
+#pragma unroll
+    for (int k = 0; k < B; ++k) cur[k] = row[k];
+  }
+  for (; rl + B <= rc; rl += B) {
+    const bool more = rl + 2 * B <= rc;
+    if (more) {
+#pragma unroll
+      for (int k = 0; k < B; ++k) nxt[k] = row[rl + B + k];
+    }
+    if (FOLD == 1) {
+      double acc = A.f;
+#pragma unroll
+      for (int k = 0; k < B; ++k) acc = __dadd_rn(acc, __longlong_as_double(cur[k]));
+      A.f = acc;
+    } else if (FOLD == 2) {
+      double acc = A.f;
+#pragma unroll
+      for (int k = 0; k < B; ++k) acc = (double)__double2float_rn(__dadd_rn(acc, __longlong_as_double(cur[k])));
+      A.f = acc;
+    } else if (out_dtype == AMC_S32) {
+      // truncation to 32 bits commutes with addition, so a 32-bit wrapping
+      // sum equals truncating the 64-bit sum after every step
+      unsigned acc = (unsigned)A.i;
+#pragma unroll
+      for (int k = 0; k < B; ++k) acc += (unsigned)cur[k];
+      A.i = (long long)(int)acc;
+    } else {
+      long long acc = A.i;
+#pragma unroll
+      for (int k = 0; k < B; ++k) acc += (long long)cur[k];
+      A.i = acc;
+    }
+    if (more) {
+#pragma unroll
+      for (int k = 0; k < B; ++k) cur[k] = nxt[k];
+    }
+  }
+  if (rl < rc) fold_row<FOLD>(A, op, out_dtype, src_exact, row + rl, rc - rl);
+}
+
+// V elements per dispatch of each program instruction: the op and stack-slot
+// switches run once for V independent elements, which also gives the V
+// dependent chains instruction-level parallelism.  Values and rounding are
+// those of eval_prog_f (float programs) and eval_prog (integer-only programs:
+// integer leaves, ICONST, integer stores, NEG ABS ADD SUB MUL MAX MIN, where
+// every value stays exact).
+template <int V>
+__device__ __forceinline__ void vec_push_f(double (&d)[V], const amc_insn& I, const double (&l0)[V], const double (&l1)[V]) {
+#pragma unroll
+  for (int k = 0; k < V; ++k) d[k] = I.op == AMC_OP_CONST ? I.imm : (I.a == 0 ? l0[k] : l1[k]);
+}
+template <int V>
+__device__ __forceinline__ void vec_unary_f(int op, int cvt, double (&t)[V]) {
+  switch (op) {
+    case AMC_OP_CVT:
+      if (cvt == AMC_F64) break;
+      if (cvt == AMC_F32) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) t[k] = (double)__double2float_rn(t[k]);
+        break;
+      }
+#pragma unroll
+      for (int k = 0; k < V; ++k) t[k] = round_f(cvt, t[k]);
+      break;
+    case AMC_OP_NEG:
+#pragma unroll
+      for (int k = 0; k < V; ++k) t[k] = -t[k];
+      break;
+    case AMC_OP_ABS:
+#pragma unroll
+      for (int k = 0; k < V; ++k) t[k] = fabs(t[k]);
+      break;
+    default:
+#pragma unroll
+      for (int k = 0; k < V; ++k) t[k] = un_f(op, t[k]);
+  }
+}
+template <int V>
+__device__ __forceinline__ void vec_binary_f(int op, double (&x)[V], const double (&y)[V]) {
+  switch (op) {
+    case AMC_OP_ADD:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = __dadd_rn(x[k], y[k]);
+      break;
+    case AMC_OP_SUB:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = __dsub_rn(x[k], y[k]);
+      break;
+    case AMC_OP_MUL:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = __dmul_rn(x[k], y[k]);
+      break;
+    default:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = bin_f(op, x[k], y[k]);
+  }
+}
+template <int V>
+__device__ __forceinline__ void eval_vec_f(const DProg& P, const double (&l0)[V], const double (&l1)[V], double (&out)[V]) {
+  double s0[V], s1[V], s2[V];
+  int sp = 0;
+  for (int pc = 0; pc < P.n; ++pc) {
+    const amc_insn I = P.code[pc];
+    if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST) {
+      if (sp == 0) vec_push_f(s0, I, l0, l1);
+      else if (sp == 1) vec_push_f(s1, I, l0, l1);
+      else vec_push_f(s2, I, l0, l1);
+      ++sp;
+    } else if (I.op < AMC_OP_ADD) {
+      if (sp == 1) vec_unary_f(I.op, I.a, s0);
+      else if (sp == 2) vec_unary_f(I.op, I.a, s1);
+      else vec_unary_f(I.op, I.a, s2);
+    } else {
+      if (sp == 2) vec_binary_f(I.op, s0, s1);
+      else vec_binary_f(I.op, s1, s2);
+      --sp;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < V; ++k) out[k] = s0[k];
+}
+
+template <int V>
+__device__ __forceinline__ void vec_push_i(long long (&d)[V], const amc_insn& I, const long long (&l0)[V],
+                                           const long long (&l1)[V]) {
+#pragma unroll
+  for (int k = 0; k < V; ++k) d[k] = I.op == AMC_OP_ICONST ? (long long)I.imm : (I.a == 0 ? l0[k] : l1[k]);
+}
+__device__ __forceinline__ long long store_int(int dtype, long long t) {
+  switch (dtype) {
+    case AMC_S32: return (int)t;
+    case AMC_U32: return (unsigned)(t < 0 ? -t : t);
+    case AMC_U64: return t < 0 ? -t : t;
+    default: return t;
+  }
+}
+template <int V>
+__device__ __forceinline__ void vec_unary_i(int op, int cvt, long long (&t)[V]) {
+  switch (op) {
+    case AMC_OP_CVT:
+      if (cvt == AMC_S32) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) t[k] = (int)t[k];
+      } else if (cvt != AMC_S64) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) t[k] = store_int(cvt, t[k]);
+      }
+      break;
+    case AMC_OP_NEG:
+#pragma unroll
+      for (int k = 0; k < V; ++k) t[k] = -t[k];
+      break;
+    default:   // ABS
+#pragma unroll
+      for (int k = 0; k < V; ++k) t[k] = t[k] < 0 ? -t[k] : t[k];
+  }
+}
+template <int V>
+__device__ __forceinline__ void vec_binary_i(int op, long long (&x)[V], const long long (&y)[V]) {
+  switch (op) {
+    case AMC_OP_ADD:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = x[k] + y[k];
+      break;
+    case AMC_OP_SUB:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = x[k] - y[k];
+      break;
+    case AMC_OP_MUL:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = x[k] * y[k];
+      break;
+    case AMC_OP_MAX:
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = x[k] > y[k] ? x[k] : y[k];
+      break;
+    default:   // MIN
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[k] = x[k] < y[k] ? x[k] : y[k];
+  }
+}
+template <int V>
+__device__ __forceinline__ void eval_vec_i(const DProg& P, const long long (&l0)[V], const long long (&l1)[V],
+                                           long long (&out)[V]) {
+  long long s0[V], s1[V], s2[V];
+  int sp = 0;
+  for (int pc = 0; pc < P.n; ++pc) {
+    const amc_insn I = P.code[pc];
+    if (I.op == AMC_OP_LOAD || I.op == AMC_OP_ICONST) {
+      if (sp == 0) vec_push_i(s0, I, l0, l1);
+      else if (sp == 1) vec_push_i(s1, I, l0, l1);
+      else vec_push_i(s2, I, l0, l1);
+      ++sp;
+    } else if (I.op < AMC_OP_ADD) {
+      if (sp == 1) vec_unary_i(I.op, I.a, s0);
+      else if (sp == 2) vec_unary_i(I.op, I.a, s1);
+      else vec_unary_i(I.op, I.a, s2);
+    } else {
+      if (sp == 2) vec_binary_i(I.op, s0, s1);
+      else vec_binary_i(I.op, s1, s2);
+      --sp;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < V; ++k) out[k] = s0[k];
+}
+__device__ __forceinline__ long long raw_i(unsigned long long raw, int dtype) {
+  switch (dtype) {
+    case AMC_S32: return (long long)(int)(unsigned)raw;
+    case AMC_U32: return (long long)(unsigned)raw;
+    default: return (long long)raw;
+  }
+}
+
+// Host check: the program keeps every value an exact integer (eval_vec_i).
+static bool prog_int_only(const ReduceArgs& a) {
+  for (int l = 0; l < a.nleaf; ++l)
+    if (a.leaf_o[l].dtype == AMC_F32 || a.leaf_o[l].dtype == AMC_F64) return false;
+  for (int pc = 0; pc < a.prog.n; ++pc) {
+    const amc_insn& I = a.prog.code[pc];
+    switch (I.op) {
+      case AMC_OP_LOAD: case AMC_OP_ICONST: case AMC_OP_NEG: case AMC_OP_ABS: case AMC_OP_ADD: case AMC_OP_SUB:
+      case AMC_OP_MUL: case AMC_OP_MAX: case AMC_OP_MIN:
+        break;
+      case AMC_OP_CVT:
+        if (I.a == AMC_F32 || I.a == AMC_F64) return false;
+        break;
+      default:
+        return false;
+    }
+  }
+  return true;
+}
+
+constexpr int kStOT = 8;          // outputs per CTA
+constexpr int kStSC = 96;         // reduced positions per sub-chunk (static shared memory < 48 KB)
+constexpr int kStWorkers = 224;   // warps 1-7 copy and evaluate; warp 0 folds
+
+template <int MODE, int V>
+__device__ __forceinline__ void staged_eval_chunk(const ReduceArgs& a, const unsigned long long* __restrict__ raw0,
+                                                  const unsigned long long* __restrict__ raw1,
+                                                  unsigned long long* __restrict__ vals, long long o0, int tile,
+                                                  int wt, bool src_exact) {
+  const int nl = a.nleaf;
+  const int dt0 = a.leaf_o[0].dtype, dt1 = nl > 1 ? a.leaf_o[1].dtype : dt0;
+  for (int e0 = wt; e0 < tile; e0 += kStWorkers * V) {
+    int slot[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      const int e = e0 + k * kStWorkers;
+      const bool valid = e < tile && o0 + (e & (kStOT - 1)) < a.O;
+      slot[k] = valid ? (e & (kStOT - 1)) * (kStSC + 1) + e / kStOT : -1;
+    }
+    if (MODE == 0) {
+      double l0[V], l1[V], out[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const int e = e0 + k * kStWorkers;
+        l0[k] = slot[k] >= 0 ? raw_f(raw0[e], dt0) : 0.0;
+        l1[k] = (slot[k] >= 0 && nl > 1) ? raw_f(raw1[e], dt1) : 0.0;
+      }
+      eval_vec_f<V>(a.prog, l0, l1, out);
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (slot[k] >= 0)
+          vals[slot[k]] = src_exact ? (unsigned long long)(long long)trunc(out[k])
+                                    : (unsigned long long)__double_as_longlong(out[k]);
+    } else if (MODE == 1) {
+      long long l0[V], l1[V], out[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        const int e = e0 + k * kStWorkers;
+        l0[k] = slot[k] >= 0 ? raw_i(raw0[e], dt0) : 0;
+        l1[k] = (slot[k] >= 0 && nl > 1) ? raw_i(raw1[e], dt1) : 0;
+      }
+      eval_vec_i<V>(a.prog, l0, l1, out);
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (slot[k] >= 0)
+          vals[slot[k]] = src_exact ? (unsigned long long)out[k]
+                                    : (unsigned long long)__double_as_longlong((double)out[k]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (slot[k] < 0) continue;
+        const int e = e0 + k * kStWorkers;
+        double vf;
+        long long vi;
+        eval_staged<true>(a.prog, a.leaf_o, raw0[e], nl > 1 ? raw1[e] : 0ull, vf, vi);
+        vals[slot[k]] = src_exact ? (unsigned long long)vi : (unsigned long long)__double_as_longlong(vf);
+      }
+    }
+  }
+}
+
+template <int FOLD, int MODE>
+__global__ void __launch_bounds__(256) k_reduce_staged(const __grid_constant__ ReduceArgs a) {
+  __shared__ unsigned long long raw[2][2][kStOT * kStSC];        // [buffer][leaf][position][output]
+  __shared__ unsigned long long vals[2][kStOT * (kStSC + 1)];    // [buffer][output][position]
+  const int tid = threadIdx.x;
+  const bool src_exact = !dtype_is_float_d(a.src_dtype);
+  const long long o0 = (long long)blockIdx.x * kStOT;
+  const int nch = (int)((a.R + kStSC - 1) / kStSC);
+  if (tid < 32) {
+    // fold warp: sub-chunk j once the workers have evaluated it
+    Acc A;
+    acc_init(A, a.op, a.out_dtype);
+    for (int j = 0; j < nch; ++j) {
+      named_bar(2, 256);
+      const int rc = (int)((a.R - (long long)j * kStSC) < kStSC ? (a.R - (long long)j * kStSC) : kStSC);
+      if (tid < kStOT && o0 + tid < a.O)
+        fold_row_pipelined<FOLD>(A, a.op, a.out_dtype, src_exact, vals[j & 1] + tid * (kStSC + 1), rc);
+    }
+    if (tid < kStOT && o0 + tid < a.O) acc_store(A, a.out, a.out_dtype, a.op, a.R, o0 + tid);
+    return;
+  }
+  // workers: copy sub-chunk j+1 (cp.async, outputs fastest so a warp covers
+  // whole sectors) while evaluating sub-chunk j
+  const int wt = tid - 32;
+  const int nl = a.nleaf;
+  const int b0 = dtype_bytes_d(a.leaf_o[0].dtype), b1 = nl > 1 ? dtype_bytes_d(a.leaf_o[1].dtype) : 8;
+  const char* p0 = (const char*)a.leaf_o[0].ptr;
+  const char* p1 = nl > 1 ? (const char*)a.leaf_o[1].ptr : p0;
+  const long long so0 = a.leaf_o[0].strides[0], sr0 = a.leaf_r[0][0];
+  const long long so1 = nl > 1 ? a.leaf_o[1].strides[0] : 0, sr1 = nl > 1 ? a.leaf_r[1][0] : 0;
+  auto copy = [&](int j) {
+    const long long r0 = (long long)j * kStSC;
+    const int rc = (int)((a.R - r0) < kStSC ? (a.R - r0) : kStSC);
+    const int tile = kStOT * rc;
+    unsigned long long* d0 = raw[j & 1][0];
+    unsigned long long* d1 = raw[j & 1][1];
+    for (int e = wt; e < tile; e += kStWorkers) {
+      const long long o = o0 + (e & (kStOT - 1));
+      if (o >= a.O) continue;
+      const long long r = r0 + e / kStOT;
+      cp_async_elem(d0 + e, p0 + (o * so0 + r * sr0) * b0, b0);
+      if (nl > 1) cp_async_elem(d1 + e, p1 + (o * so1 + r * sr1) * b1, b1);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  copy(0);
+  for (int j = 0; j < nch; ++j) {
+    if (j + 1 < nch) {
+      copy(j + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    named_bar(1, kStWorkers);   // sub-chunk j has landed for every worker
+    const long long r0 = (long long)j * kStSC;
+    const int rc = (int)((a.R - r0) < kStSC ? (a.R - r0) : kStSC);
+    staged_eval_chunk<MODE, 4>(a, raw[j & 1][0], raw[j & 1][1], vals[j & 1], o0, kStOT * rc, wt, src_exact);
+    // hand sub-chunk j to the fold warp; it arrives here after folding j-1,
+    // so vals[j & 1] is free again from the next iteration on
+    named_bar(2, 256);
+  }
+}
+
 // Tree reduction for few outputs over long axes: pass 1 gives each CTA of
 // grid (G, O) a contiguous r-range, folded per thread in ascending order and
 // combined across the block in a fixed tree; pass 2 folds the G partials of
@@ -667,10 +1132,36 @@ int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scr
   } else if (a.orank == 0) {
     ofast = 0;
   }
-  size_t sm = (size_t)OT * (RC + 1) * 8;
-  unsigned grid = (unsigned)((O + OT - 1) / OT);
   const bool sumlike = a.op == AMC_RED_SUM || a.op == AMC_RED_MEAN;
   const bool src_float = a.src_dtype == AMC_F32 || a.src_dtype == AMC_F64;
+  // staged form: few outputs, adjacent in memory, small program
+  if (OT < 8 && ofast && a.orank == 1 && a.rrank == 1 && a.nleaf >= 1 && a.nleaf <= 2 && a.prog.max_depth <= 3 &&
+      a.prog.n > 0) {
+    bool adjacent = true;
+    for (int l = 0; l < a.nleaf; ++l) {
+      const long long so = a.leaf_o[l].strides[0];
+      adjacent = adjacent && (so == 0 || so == 1 || so == -1);
+    }
+    if (adjacent) {
+      const unsigned gs = (unsigned)((O + kStOT - 1) / kStOT);
+      const int mode = a.prog.all_float ? 0 : prog_int_only(a) ? 1 : 2;
+#define AMC_STAGED(F)                                                                           \
+  do {                                                                                          \
+    if (mode == 0) k_reduce_staged<F, 0><<<gs, 256, 0, s>>>(a);                                 \
+    else if (mode == 1) k_reduce_staged<F, 1><<<gs, 256, 0, s>>>(a);                            \
+    else k_reduce_staged<F, 2><<<gs, 256, 0, s>>>(a);                                           \
+  } while (0)
+      if (sumlike && src_float && a.out_dtype == AMC_F64) AMC_STAGED(1);
+      else if (sumlike && src_float && a.out_dtype == AMC_F32) AMC_STAGED(2);
+      else if (sumlike && !src_float && (a.out_dtype == AMC_S32 || a.out_dtype == AMC_S64)) AMC_STAGED(3);
+      else AMC_STAGED(0);
+#undef AMC_STAGED
+      AMC_CUDA(cudaGetLastError());
+      return AMC_OK;
+    }
+  }
+  size_t sm = (size_t)OT * (RC + 1) * 8;
+  unsigned grid = (unsigned)((O + OT - 1) / OT);
   if (sumlike && src_float && a.out_dtype == AMC_F64)
     k_reduce_seq<1><<<grid, 256, sm, s>>>(a, OT, RC, ofast);
   else if (sumlike && src_float && a.out_dtype == AMC_F32)

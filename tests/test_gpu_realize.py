@@ -120,6 +120,27 @@ def test_fused_chains_match_oracle_bitwise(amc, dtype):
         _same(amc.realize(e).values(), oracle.realize(e).values())
 
 
+@pytest.mark.parametrize("dtype", ["f32", "f64", "s32", "s64"])
+@pytest.mark.parametrize("R,O", [(1, 5), (7, 8), (512, 13), (3000, 1000)])
+def test_staged_reduction_bitwise(amc, dtype, R, O):
+    """Reductions over the leading axis of an (R, O) tree with few outputs
+    (the staged ordered reduction: 8 adjacent outputs per CTA, leaf values
+    copied into shared memory, ascending fold); R = 3000 takes several
+    chunks.  Bit-exact against the oracle."""
+    rng = np.random.default_rng(R + O)
+    x = amc.morph_from_numpy(_rand(rng, (R, O), dtype))
+    y = amc.morph_from_numpy(_rand(rng, (R, O), dtype))
+    exprs = [
+        amc.morph_reduce("sum", amc.morph_add(amc.morph_mul(x, x), y), (0,)),
+        amc.morph_reduce("mean", amc.morph_abs(x), (0,)),
+        amc.morph_reduce("sum", amc.morph_map(lambda v: v - 3, x), (0,), True),
+    ]
+    if dtype in ("f32", "f64"):
+        exprs.append(amc.morph_reduce("max", amc.morph_sub(x, y), (0,)))
+    for e in exprs:
+        _same(amc.realize(e).values(), oracle.realize(e).values())
+
+
 def test_transcendentals_within_f64_tolerance(amc):
     rng = np.random.default_rng(5)
     a = amc.morph_from_numpy(rng.uniform(0.1, 3.0, (64, 33)))
