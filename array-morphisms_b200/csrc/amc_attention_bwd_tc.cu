@@ -15,10 +15,13 @@
 //   k_attn_bwd_dq_tc   one CTA per 128 queries (Q, dO resident in tensor
 //                      memory as the A operands); streams 64-key tiles:
 //                      S, dP, dS as above, dQ += dS K.
-// Every operand is K-major in 128-byte-swizzled shared memory, so the
-// products whose contraction runs over queries or keys read transposed,
-// tf32-rounded copies (Q^T, dO^T, K^T) that a pre-pass writes together with
-// rounded copies of Q, K, V, dO and the per-row (lse * log2 e, D) pairs.
+// A pre-pass writes tf32-rounded copies of Q, K, V, dO and the per-row
+// (lse * log2 e, D) pairs.  The S/dP products read K-major tiles of those
+// copies (128-byte swizzle).  The products whose contraction runs over
+// queries or keys (dV, dK: over queries; dQ: over keys) read the same rows
+// as MN-major operands: a second tensor map with the 128-byte swizzle in
+// 32-byte atoms, the only MN-major layout tf32 products accept.  No
+// transposed copy is written.
 // S/dP tensor-memory buffers (three in the dK/dV kernel, two in the dQ
 // kernel, whose other columns hold Q and dO) let the products of the next
 // tiles run while the threads work on the current one; two warpgroups share
@@ -49,7 +52,7 @@ constexpr int kRowThreads = 256;
 constexpr int kKVK = 0;                          // K tile, 2 x 16 KB (dims 0-31, 32-63)
 constexpr int kKVV = 32768;                      // V tile
 constexpr int kKVF = 65536;                      // 3 stages x (Q_i 16 KB + dO_i 16 KB)
-constexpr int kKVB = kKVF + 3 * 32768;           // 2 stages x (Q_i^T 16 KB + dO_i^T 16 KB)
+constexpr int kKVB = kKVF + 3 * 32768;           // 2 stages x (Q_i 16 KB + dO_i 16 KB), MN-major
 constexpr int kKVL = kKVB + 2 * 32768;           // 3 stages x 64 (lse2, D) pairs
 constexpr int kKVBar = kKVL + 3 * 512;
 constexpr int kKVSmem = kKVBar + 256 + 1024;
@@ -58,7 +61,7 @@ constexpr int kKVSmem = kKVBar + 256 + 1024;
 constexpr int kQQ = 0;                           // Q tile, 2 x 16 KB
 constexpr int kQdO = 32768;                      // dO tile
 constexpr int kQF = 65536;                       // 3 stages x (K_j 16 KB + V_j 16 KB)
-constexpr int kQB = kQF + 3 * 32768;             // 2 stages x K_j^T 16 KB
+constexpr int kQB = kQF + 3 * 32768;             // 2 stages x K_j 16 KB, MN-major
 constexpr int kQBar = kQB + 2 * 16384;
 constexpr int kQSmem = kQBar + 256 + 1024;
 
@@ -71,16 +74,13 @@ __device__ int g_attn_bwd_error;
 
 // ------------------------------------------------------------------ pre-pass
 // One block per 32 rows of one (batch, head) block: rounded copies of Q, K,
-// V, dO; transposed rounded copies of Q, K, dO ((blocks*64, n), rows = dims);
-// LD[row] = (lse * log2 e, sum_d dO * O).
+// V, dO; LD[row] = (lse * log2 e, sum_d dO * O).
 __global__ void __launch_bounds__(256) k_attn_bwd_prep(const float* __restrict__ Q, const float* __restrict__ K,
                                                        const float* __restrict__ V, const float* __restrict__ O,
                                                        const float* __restrict__ dO, const float* __restrict__ lse,
                                                        float* __restrict__ Qr, float* __restrict__ Kr,
                                                        float* __restrict__ Vr, float* __restrict__ dOr,
-                                                       float* __restrict__ Qt, float* __restrict__ Kt,
-                                                       float* __restrict__ dOt, float2* __restrict__ LD, int n) {
-  __shared__ float t[3][32][kD + 1];
+                                                       float2* __restrict__ LD, int n) {
   const int tid = threadIdx.x;
   const int bh = blockIdx.y, r0 = blockIdx.x * 32;
   const size_t base4 = ((size_t)bh * n + r0) * (kD / 4);
@@ -95,12 +95,7 @@ __global__ void __launch_bounds__(256) k_attn_bwd_prep(const float* __restrict__
 #pragma unroll
     for (int a = 0; a < 3; ++a) {
       const float4 v = src[a][i];
-      const float4 r = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
-      dst[a][i] = r;
-      t[a][row][c] = r.x;
-      t[a][row][c + 1] = r.y;
-      t[a][row][c + 2] = r.z;
-      t[a][row][c + 3] = r.w;
+      dst[a][i] = make_float4(round_tf32(v.x), round_tf32(v.y), round_tf32(v.z), round_tf32(v.w));
     }
     const float4 v = reinterpret_cast<const float4*>(V)[base4 + i];
     reinterpret_cast<float4*>(Vr)[base4 + i] =
@@ -116,23 +111,13 @@ __global__ void __launch_bounds__(256) k_attn_bwd_prep(const float* __restrict__
       LD[r] = make_float2(lse[r] * 1.4426950408889634f, d);
     }
   }
-  __syncthreads();
-  const int tx = tid & 31, ty = tid >> 5;
-  float* tdst[3] = {Qt, Kt, dOt};
-#pragma unroll
-  for (int a = 0; a < 3; ++a)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const int d = ty + 8 * k;
-      tdst[a][((size_t)bh * kD + d) * n + r0 + tx] = t[a][tx][d];
-    }
 }
 
 // ------------------------------------------------------------------ dK, dV
 __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
     const __grid_constant__ CUtensorMap mK, const __grid_constant__ CUtensorMap mV,
     const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mdO,
-    const __grid_constant__ CUtensorMap mQt, const __grid_constant__ CUtensorMap mdOt,
+    const __grid_constant__ CUtensorMap mQmn, const __grid_constant__ CUtensorMap mdOmn,
     const float2* __restrict__ LD, float* __restrict__ dK, float* __restrict__ dV, int n, float scale_log2,
     float scale) {
   extern __shared__ unsigned char bkv_sm_raw[];
@@ -140,7 +125,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
   uint64_t* kv_full = (uint64_t*)(sm + kKVBar);
   uint64_t* f_full = kv_full + 1;    // [3] Q_i, dO_i, LD_i landed
   uint64_t* f_empty = kv_full + 4;   // [3] S/dP products done and LD read
-  uint64_t* b_full = kv_full + 7;    // [2] Q_i^T, dO_i^T landed
+  uint64_t* b_full = kv_full + 7;    // [2] MN-major Q_i, dO_i landed
   uint64_t* b_empty = kv_full + 9;   // [2]
   uint64_t* s_full = kv_full + 11;   // [3] S^T, dP^T in tensor memory
   uint64_t* p_full = kv_full + 14;   // [3] P^T, dS^T written back
@@ -207,8 +192,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         unsigned char* st = sm + kKVB + b * 32768;
         mbar_expect_tx(&b_full[b], 32768);
         for (int r = 0; r < 2; ++r) {
-          tma_load_2d(st + r * 8192, &mQt, i * kStream + 32 * r, bh * kD, &b_full[b]);
-          tma_load_2d(st + 16384 + r * 8192, &mdOt, i * kStream + 32 * r, bh * kD, &b_full[b]);
+          tma_load_2d(st + r * 8192, &mQmn, 32 * r, bh * n + i * kStream, &b_full[b]);
+          tma_load_2d(st + 16384 + r * 8192, &mdOmn, 32 * r, bh * n + i * kStream, &b_full[b]);
         }
       }
     }
@@ -216,8 +201,10 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
     // warp 10 issues the S/dP products, warp 11 the accumulating ones
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
+      const uint32_t id_mn = idesc_tf32(kTile, 64, false, true);   // B MN-major
       const uint64_t dk0 = sdesc(smem_addr(sm + kKVK), 16, 1024), dv0 = sdesc(smem_addr(sm + kKVV), 16, 1024);
-      const uint64_t df0 = sdesc(smem_addr(sm + kKVF), 16, 1024), db0 = sdesc(smem_addr(sm + kKVB), 16, 1024);
+      // B-stage: region r (8 KB) holds dims 32r..32r+31 of 64 query rows
+      const uint64_t df0 = sdesc(smem_addr(sm + kKVF), 16, 1024), db0 = sdesc_mn(smem_addr(sm + kKVB), 8192);
       // S^T = K Q_i^T and dP^T = V dO_i^T into buffer i % 3
       auto sdp = [&](int i) -> bool {
         const int s = i % 3;
@@ -235,7 +222,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         mma_commit(&f_empty[s]);
         return true;
       };
-      // dV += P^T dO_i, dK += dS^T Q_i (A operands from tensor memory)
+      // dV += P^T dO_i, dK += dS^T Q_i (A operands from tensor memory; B
+      // MN-major, K step k = query rows 8k..8k+7)
       auto dvdk = [&](int i) -> bool {
         const int s = i % 3, b = i & 1;
         if (!mbar_wait(&p_full[s], (uint32_t)(i / 3) & 1u)) return false;
@@ -246,8 +234,8 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
         const bool acc0 = i > 0;
 #pragma unroll
         for (int k = 0; k < kStream / 8; ++k) {
-          mma_tf32_ts(t_dv, ts + k * 8, desc_add(st, 16384 + kstep_off(k, 8192)), id, acc0 || k > 0);
-          mma_tf32_ts(t_dk, ts + 64 + k * 8, desc_add(st, kstep_off(k, 8192)), id, acc0 || k > 0);
+          mma_tf32_ts(t_dv, ts + k * 8, desc_add(st, 16384 + k * 1024), id_mn, acc0 || k > 0);
+          mma_tf32_ts(t_dk, ts + 64 + k * 8, desc_add(st, k * 1024), id_mn, acc0 || k > 0);
         }
         mma_commit(&b_empty[b]);
         mma_commit(&t_free[s]);
@@ -347,14 +335,14 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dkv_tc(
 __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
     const __grid_constant__ CUtensorMap mQ, const __grid_constant__ CUtensorMap mdO,
     const __grid_constant__ CUtensorMap mK, const __grid_constant__ CUtensorMap mV,
-    const __grid_constant__ CUtensorMap mKt, const float2* __restrict__ LD, float* __restrict__ dQ, int n,
+    const __grid_constant__ CUtensorMap mKmn, const float2* __restrict__ LD, float* __restrict__ dQ, int n,
     float scale_log2, float scale) {
   extern __shared__ unsigned char bq_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)bq_sm_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* qd_full = (uint64_t*)(sm + kQBar);
   uint64_t* f_full = qd_full + 1;    // [3] K_j, V_j landed
   uint64_t* f_empty = qd_full + 4;   // [3]
-  uint64_t* b_full = qd_full + 7;    // [2] K_j^T landed
+  uint64_t* b_full = qd_full + 7;    // [2] MN-major K_j landed
   uint64_t* b_empty = qd_full + 9;   // [2]
   uint64_t* s_full = qd_full + 11;   // [2] per tensor-memory buffer
   uint64_t* p_full = qd_full + 14;   // [2] dS written back
@@ -424,14 +412,15 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         if (*abort_flag) break;
         unsigned char* st = sm + kQB + b * 16384;
         mbar_expect_tx(&b_full[b], 16384);
-        for (int r = 0; r < 2; ++r) tma_load_2d(st + r * 8192, &mKt, j * kStream + 32 * r, bh * kD, &b_full[b]);
+        for (int r = 0; r < 2; ++r) tma_load_2d(st + r * 8192, &mKmn, 32 * r, bh * n + j * kStream, &b_full[b]);
       }
     }
   } else if (warp >= 10) {
     // warp 10 issues the S/dP products, warp 11 the accumulating ones
     if (lane == 0) {
       const uint32_t id = idesc_tf32(kTile, 64, false, false);
-      const uint64_t df0 = sdesc(smem_addr(sm + kQF), 16, 1024), db0 = sdesc(smem_addr(sm + kQB), 16, 1024);
+      const uint32_t id_mn = idesc_tf32(kTile, 64, false, true);   // B MN-major
+      const uint64_t df0 = sdesc(smem_addr(sm + kQF), 16, 1024), db0 = sdesc_mn(smem_addr(sm + kQB), 8192);
       // S = Q K_j^T, dP = dO V_j^T into buffer j % 2; K_j, V_j from stage j % 3
       auto sdp = [&](int j) -> bool {
         const int f = j % 3, s = j & 1;
@@ -458,7 +447,7 @@ __global__ void __launch_bounds__(kThreadsB, 1) k_attn_bwd_dq_tc(
         const uint64_t st = desc_add(db0, b * 16384);
         const bool acc0 = j > 0;
 #pragma unroll
-        for (int k = 0; k < kStream / 8; ++k) mma_tf32_ts(t_dq, ts + 64 + k * 8, desc_add(st, kstep_off(k, 8192)), id, acc0 || k > 0);
+        for (int k = 0; k < kStream / 8; ++k) mma_tf32_ts(t_dq, ts + 64 + k * 8, desc_add(st, k * 1024), id_mn, acc0 || k > 0);
         mma_commit(&b_empty[b]);
         mma_commit(&t_free[s]);
         return true;
@@ -588,28 +577,25 @@ int attention_bwd_tc(const float* Q, const float* K, const float* V, const float
   *handled = true;
   const size_t telems = (size_t)rows * kD;
   float* scr = nullptr;
-  int rc = bwd_scratch((7 * telems + 2 * rows) * sizeof(float), (void**)&scr);
+  int rc = bwd_scratch((4 * telems + 2 * rows) * sizeof(float), (void**)&scr);
   if (rc) return rc;
-  float *Qr = scr, *Kr = Qr + telems, *Vr = Kr + telems, *dOr = Vr + telems, *Qt = dOr + telems, *Kt = Qt + telems,
-        *dOt = Kt + telems;
-  float2* LD = reinterpret_cast<float2*>(dOt + telems);
-  k_attn_bwd_prep<<<dim3(n / 32, (unsigned)blocks), 256, 0, s>>>(Q, K, V, O, dO, lse, Qr, Kr, Vr, dOr, Qt, Kt, dOt,
-                                                                 LD, n);
+  float *Qr = scr, *Kr = Qr + telems, *Vr = Kr + telems, *dOr = Vr + telems;
+  float2* LD = reinterpret_cast<float2*>(dOr + telems);
+  k_attn_bwd_prep<<<dim3(n / 32, (unsigned)blocks), 256, 0, s>>>(Q, K, V, O, dO, lse, Qr, Kr, Vr, dOr, LD, n);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "k_attn_bwd_prep");
-  CUtensorMap mK128, mV128, mQ64, mdO64, mQt, mdOt, mQ128, mdO128, mK64, mV64, mKt;
-  const uint64_t trows = (uint64_t)blocks * kD;
+  CUtensorMap mK128, mV128, mQ64, mdO64, mQmn, mdOmn, mQ128, mdO128, mK64, mV64, mKmn;
   rc = make_tmap_2d_f32(&mK128, Kr, rows, kD, kD, 128);
   if (!rc) rc = make_tmap_2d_f32(&mV128, Vr, rows, kD, kD, 128);
   if (!rc) rc = make_tmap_2d_f32(&mQ64, Qr, rows, kD, kD, 64);
   if (!rc) rc = make_tmap_2d_f32(&mdO64, dOr, rows, kD, kD, 64);
-  if (!rc) rc = make_tmap_2d_f32(&mQt, Qt, trows, (uint64_t)n, (uint64_t)n, 64);
-  if (!rc) rc = make_tmap_2d_f32(&mdOt, dOt, trows, (uint64_t)n, (uint64_t)n, 64);
+  if (!rc) rc = make_tmap_2d_f32_swz(&mQmn, Qr, rows, kD, kD, 32, 64, TmapSwizzle::k128Atom32);
+  if (!rc) rc = make_tmap_2d_f32_swz(&mdOmn, dOr, rows, kD, kD, 32, 64, TmapSwizzle::k128Atom32);
   if (!rc) rc = make_tmap_2d_f32(&mQ128, Qr, rows, kD, kD, 128);
   if (!rc) rc = make_tmap_2d_f32(&mdO128, dOr, rows, kD, kD, 128);
   if (!rc) rc = make_tmap_2d_f32(&mK64, Kr, rows, kD, kD, 64);
   if (!rc) rc = make_tmap_2d_f32(&mV64, Vr, rows, kD, kD, 64);
-  if (!rc) rc = make_tmap_2d_f32(&mKt, Kt, trows, (uint64_t)n, (uint64_t)n, 64);
+  if (!rc) rc = make_tmap_2d_f32_swz(&mKmn, Kr, rows, kD, kD, 32, 64, TmapSwizzle::k128Atom32);
   if (rc) return rc;
   static std::atomic<uint64_t> attr_dkv{0}, attr_dq{0};
   rc = smem_attr_once(k_attn_bwd_dkv_tc, kKVSmem, attr_dkv);
@@ -617,11 +603,11 @@ int attention_bwd_tc(const float* Q, const float* K, const float* V, const float
   if (rc) return rc;
   const float scale_log2 = scale * 1.4426950408889634f;
   const dim3 grid(n / kTile, (unsigned)blocks);
-  k_attn_bwd_dkv_tc<<<grid, kThreadsB, kKVSmem, s>>>(mK128, mV128, mQ64, mdO64, mQt, mdOt, LD, dK, dV, n, scale_log2,
+  k_attn_bwd_dkv_tc<<<grid, kThreadsB, kKVSmem, s>>>(mK128, mV128, mQ64, mdO64, mQmn, mdOmn, LD, dK, dV, n, scale_log2,
                                                      scale);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "k_attn_bwd_dkv_tc");
-  k_attn_bwd_dq_tc<<<grid, kThreadsB, kQSmem, s>>>(mQ128, mdO128, mK64, mV64, mKt, LD, dQ, n, scale_log2, scale);
+  k_attn_bwd_dq_tc<<<grid, kThreadsB, kQSmem, s>>>(mQ128, mdO128, mK64, mV64, mKmn, LD, dQ, n, scale_log2, scale);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "k_attn_bwd_dq_tc");
   return AMC_OK;

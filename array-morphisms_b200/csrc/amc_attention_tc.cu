@@ -9,10 +9,13 @@
 //   P  = exp(scale*S - m) with the running row max m and sum l (online
 //        softmax of the reference's 3-pass %attn-2d!, realization.scm:279-326)
 //   O_t = P V       tcgen05.mma M=128 N=64 K=128; P is written by the threads
-//                   into shared memory in the K-major swizzled layout, V comes
-//                   pre-transposed (V^T, keys contiguous) so it is K-major too
+//                   into shared memory in the K-major swizzled layout; V is
+//                   an MN-major operand (its rows are the contraction axis):
+//                   the TMA writes it with the 128-byte swizzle in 32-byte
+//                   atoms, the only MN-major layout tf32 products accept
 //   O  = O * exp(m_old - m) + O_t   in registers
-// K and V^T tiles are double-buffered: the TMA for tile j+2 is issued as soon
+// K and V are read from tf32-rounded copies that one pre-pass writes.
+// K and V tiles are double-buffered: the TMA for tile j+2 is issued as soon
 // as the P V product of tile j has consumed its buffer.  Every mbarrier wait is
 // bounded; on expiry the CTA records AMC_ERR_TIMEOUT and leaves after its MMAs
 // and copies have drained.
@@ -34,7 +37,7 @@ constexpr int kD = 64;     // head dim
 // shared memory map (bytes, from a 1024-aligned base)
 constexpr int kQOff = 0;                         // 2 x 16 KB   (dims 0-31, 32-63)
 constexpr int kKOff = kQOff + 2 * 16384;         // 2 bufs x 2 x 16 KB
-constexpr int kVOff = kKOff + 2 * 2 * 16384;     // 2 bufs x 4 x 8 KB (keys 0-31 .. 96-127), 64 dim rows each
+constexpr int kVOff = kKOff + 2 * 2 * 16384;     // 2 bufs x 2 x 16 KB (dims 0-31, 32-63), 128 key rows each (MN-major)
 constexpr int kPOff = kVOff + 2 * 4 * 8192;      // 4 x 16 KB   (keys 0-31 .. 96-127)
 constexpr int kBarOff = kPOff + 4 * 16384;
 constexpr int kSmemBytes = kBarOff + 128 + 1024; // barriers, tmem slot, alignment slack
@@ -47,7 +50,7 @@ __device__ __forceinline__ void fail_timeout() { atomicExch(&g_attn_error, AMC_E
 
 __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ CUtensorMap mQ,
                                                        const __grid_constant__ CUtensorMap mK,
-                                                       const __grid_constant__ CUtensorMap mVt, float* __restrict__ O,
+                                                       const __grid_constant__ CUtensorMap mV, float* __restrict__ O,
                                                        float* __restrict__ lse, int n, float scale_log2) {
   extern __shared__ unsigned char attn_sm_raw[];
   unsigned char* sm = (unsigned char*)(((uintptr_t)attn_sm_raw + 1023) & ~(uintptr_t)1023);
@@ -80,7 +83,7 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
   auto load_kv = [&](int j, int b) {
     mbar_expect_tx(&bar_kv[b], 2 * 16384 + 4 * 8192);
     for (int r = 0; r < 2; ++r) tma_load_2d(sm + kKOff + b * 32768 + r * 16384, &mK, 32 * r, bh * n + j * kBN, &bar_kv[b]);
-    for (int r = 0; r < 4; ++r) tma_load_2d(sm + kVOff + b * 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &bar_kv[b]);
+    for (int r = 0; r < 2; ++r) tma_load_2d(sm + kVOff + b * 32768 + r * 16384, &mV, 32 * r, bh * n + j * kBN, &bar_kv[b]);
   };
   if (tid == 0) {
     mbar_expect_tx(bar_q, 2 * 16384);
@@ -91,7 +94,7 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
   bool ok = __syncthreads_and(mbar_wait(bar_q, 0));
 
   const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
-  const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
+  const uint32_t id_o = idesc_tf32(kBM, kD, false, true);   // V MN-major
   float m = -INFINITY, l = 0.f;
   float o[kD];
 #pragma unroll
@@ -153,10 +156,10 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
     tc_fence_after();
     if (tid == 0) {
       const uint64_t pd = sdesc(smem_addr(sm + kPOff), 16, 1024);
-      const uint64_t vd = sdesc(smem_addr(sm + kVOff + b * 32768), 16, 1024);
+      const uint64_t vd = sdesc_mn(smem_addr(sm + kVOff + b * 32768), 16384);
 #pragma unroll
       for (int k = 0; k < kBN / 8; ++k)
-        mma_tf32(t_o, desc_add(pd, kstep_off(k, 16384)), desc_add(vd, kstep_off(k, 8192)), id_o, k > 0);
+        mma_tf32(t_o, desc_add(pd, kstep_off(k, 16384)), desc_add(vd, k * 1024), id_o, k > 0);
       mma_commit(bar_o);
     }
     ok = __syncthreads_and(mbar_wait(bar_o, (uint32_t)j & 1u));
@@ -197,14 +200,14 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
 
 // ------------------------------------------------------------------ two-group kernel, one MMA warp
 // 256 query rows per CTA in two groups of 128 (warpgroups 0 and 1, one
-// thread per row) that share the K and V^T tiles.  Warp 8 loads Q and K,
-// warp 10 loads V^T, warp 9 alone issues the tensor-core work, in the order
+// thread per row) that share the K and V tiles.  Warp 8 loads Q and K,
+// warp 10 loads V (MN-major), warp 9 alone issues the tensor-core work, in the order
 //   S0(0) S1(0) | PV0(0) S0(1) PV1(0) S1(1) | PV0(1) S0(2) PV1(1) S1(2) | ...
 // so the next S of one group runs while the other group is in its softmax.
 // S_g(j+1) is issued into the columns that hold P_g(j) right after PV_g(j):
 // the MMAs of one thread execute in issue order.  Q (rounded, written once
 // by the row threads) and P (written back over S, rounded to tf32) are the A
-// operands straight from tensor memory, so the products read only K and V^T
+// operands straight from tensor memory, so the products read only K and V
 // from shared memory; O accumulates in tensor memory.  The running maximum is raised lazily
 // (only when a score exceeds it by more than 2^8), and O is rescaled in place
 // then, after that group's previous P V product has completed.  The decision
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(128, 1) k_attn_fwd_tc(const __grid_constant__ 
 namespace {
 constexpr int kQ3Off = 0;                        // 2 groups x 2 x 16 KB
 constexpr int kK3Off = 2 * 32768;                // 2 bufs x K 32 KB
-constexpr int kV3Off = kK3Off + 2 * 32768;       // 2 bufs x V^T 32 KB
+constexpr int kV3Off = kK3Off + 2 * 32768;       // 2 bufs x V 32 KB (dims 0-31, 32-63; MN-major)
 constexpr int kBar3Off = kV3Off + 2 * 32768;
 constexpr int kSmem3Bytes = kBar3Off + 256 + 1024;
 constexpr int kThreads3 = 352;
@@ -221,7 +224,7 @@ constexpr int kThreads3 = 352;
 
 __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_constant__ CUtensorMap mQ,
                                                               const __grid_constant__ CUtensorMap mK,
-                                                              const __grid_constant__ CUtensorMap mVt,
+                                                              const __grid_constant__ CUtensorMap mV,
                                                               float* __restrict__ O, float* __restrict__ lse, int n,
                                                               float scale_log2) {
   extern __shared__ unsigned char attn3_sm_raw[];
@@ -283,16 +286,17 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
         if (j >= 2 && !mbar_wait(&v_empty[b], (uint32_t)((j - 2) >> 1) & 1u)) { *abort_flag = 1; break; }
         if (*abort_flag) break;
         mbar_expect_tx(&v_full[b], 32768);
-        for (int r = 0; r < 4; ++r)
-          tma_load_2d(sm + kV3Off + b * 32768 + r * 8192, &mVt, j * kBN + 32 * r, bh * kD, &v_full[b]);
+        for (int r = 0; r < 2; ++r)
+          tma_load_2d(sm + kV3Off + b * 32768 + r * 16384, &mV, 32 * r, bh * n + j * kBN, &v_full[b]);
       }
     }
   } else if (warp == 9) {
     if (lane == 0) {
       const uint32_t id_s = idesc_tf32(kBM, kBN, false, false);
-      const uint32_t id_o = idesc_tf32(kBM, kD, false, false);
+      const uint32_t id_o = idesc_tf32(kBM, kD, false, true);   // V MN-major
       const uint64_t kd = sdesc(smem_addr(sm + kK3Off), 16, 1024);
-      const uint64_t vd = sdesc(smem_addr(sm + kV3Off), 16, 1024);
+      // V tiles MN-major: dims 0-31 and 32-63 are two 16 KB blocks of 128 key rows
+      const uint64_t vd = sdesc_mn(smem_addr(sm + kV3Off), 16384);
       // S = Q K^T with Q (the A operand) in tensor memory, so only K is read
       // from shared memory
       auto issue_s = [&](int g, int j) {
@@ -307,7 +311,7 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
         const bool acc0 = j > 0;
 #pragma unroll
         for (int k = 0; k < kBN / 8; ++k)
-          mma_tf32_ts(tmem + 256 + g * 64, tmem + g * 128 + k * 8, desc_add(vb, kstep_off(k, 8192)), id_o,
+          mma_tf32_ts(tmem + 256 + g * 64, tmem + g * 128 + k * 8, desc_add(vb, k * 1024), id_o,
                       acc0 || k > 0);
         mma_commit(&o_done[g]);
       };
@@ -458,30 +462,20 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// K -> a copy rounded to the nearest tf32 (the tensor core would truncate).
-__global__ void k_round_tf32(const float4* __restrict__ src, float4* __restrict__ dst, long long n4) {
+// K and V -> copies rounded to the nearest tf32 (the tensor core would
+// truncate), in one pass over both.
+__global__ void k_round_tf32_2(const float4* __restrict__ K, const float4* __restrict__ V, float4* __restrict__ Kr,
+                               float4* __restrict__ Vr, long long n4) {
   long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (; i < n4; i += stride) {
-    const float4 v = src[i];
-    dst[i] = make_float4(round_tf32_int(v.x), round_tf32_int(v.y), round_tf32_int(v.z), round_tf32_int(v.w));
+    const float4 k = K[i], v = V[i];
+    Kr[i] = make_float4(round_tf32_int(k.x), round_tf32_int(k.y), round_tf32_int(k.z), round_tf32_int(k.w));
+    Vr[i] = make_float4(round_tf32_int(v.x), round_tf32_int(v.y), round_tf32_int(v.z), round_tf32_int(v.w));
   }
 }
 
-// V (rows = blocks*n, 64) -> V^T per block: (blocks*64, n), keys contiguous,
-// rounded to the nearest tf32.
-__global__ void k_transpose_v(const float* __restrict__ V, float* __restrict__ Vt, int n) {
-  __shared__ float t[32][33];
-  const int bh = blockIdx.z, k0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  const float* src = V + (size_t)bh * n * kD;
-  float* dst = Vt + (size_t)bh * kD * n;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) t[i][threadIdx.x] = src[(size_t)(k0 + i) * kD + d0 + threadIdx.x];
-  __syncthreads();
-  for (int i = threadIdx.y; i < 32; i += blockDim.y)
-    dst[(size_t)(d0 + i) * n + k0 + threadIdx.x] = round_tf32(t[threadIdx.x][i]);
-}
-
-// Per-device V^T scratch, grown on demand and kept (it is reused by every call
+// Per-device scratch for the rounded K and V, grown on demand and kept (it is reused by every call
 // on that device; calls on one device are stream-ordered by the caller).
 static int vt_scratch(size_t bytes, void** out) {
   static std::mutex mu;
@@ -511,32 +505,32 @@ int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, f
   const uint64_t rows = (uint64_t)blocks * n;
   if (rows > 0x7fffffffull) return AMC_OK;
   *handled = true;
-  float* Vt = nullptr;
+  float* Kr = nullptr;
   const size_t tbytes = (size_t)rows * kD * sizeof(float);
-  int rc0 = vt_scratch(2 * tbytes, (void**)&Vt);
+  int rc0 = vt_scratch(2 * tbytes, (void**)&Kr);
   if (rc0) return rc0;
-  float* Kr = Vt + (size_t)rows * kD;
-  k_transpose_v<<<dim3(n / 32, kD / 32, (unsigned)blocks), dim3(32, 8), 0, s>>>(V, Vt, n);
+  float* Vr = Kr + (size_t)rows * kD;
+  k_round_tf32_2<<<(unsigned)(num_sms() * 8), 256, 0, s>>>((const float4*)K, (const float4*)V, (float4*)Kr, (float4*)Vr,
+                                                          (long long)(rows * kD / 4));
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "k_transpose_v");
-  k_round_tf32<<<(unsigned)(num_sms() * 8), 256, 0, s>>>((const float4*)K, (float4*)Kr, (long long)(rows * kD / 4));
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "k_round_tf32");
-  CUtensorMap mQ, mK, mVt;
+  if (e != cudaSuccess) return cuda_fail(e, "k_round_tf32_2");
+  // K tiles K-major (128-byte swizzle); V tiles MN-major (128-byte swizzle in
+  // 32-byte atoms): the P V product contracts over keys, the rows of V
+  CUtensorMap mQ, mK, mV;
   int rc = make_tmap_2d_f32(&mQ, Q, rows, kD, kD, 128);
   if (!rc) rc = make_tmap_2d_f32(&mK, Kr, rows, kD, kD, 128);
-  if (!rc) rc = make_tmap_2d_f32(&mVt, Vt, (uint64_t)blocks * kD, (uint64_t)n, (uint64_t)n, 64);
+  if (!rc) rc = make_tmap_2d_f32_swz(&mV, Vr, rows, kD, kD, 32, 128, TmapSwizzle::k128Atom32);
   if (rc) return rc;
   const float scale_log2 = scale * 1.4426950408889634f;
   static std::atomic<uint64_t> attr3{0}, attr1{0};
   if (n % 256 == 0) {
     int rca = smem_attr_once(k_attn_fwd_tc3, kSmem3Bytes, attr3);
     if (rca) return rca;
-    k_attn_fwd_tc3<<<dim3(n / 256, (unsigned)blocks), kThreads3, kSmem3Bytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
+    k_attn_fwd_tc3<<<dim3(n / 256, (unsigned)blocks), kThreads3, kSmem3Bytes, s>>>(mQ, mK, mV, O, lse, n, scale_log2);
   } else {
     int rca = smem_attr_once(k_attn_fwd_tc, kSmemBytes, attr1);
     if (rca) return rca;
-    k_attn_fwd_tc<<<dim3(n / kBM, (unsigned)blocks), 128, kSmemBytes, s>>>(mQ, mK, mVt, O, lse, n, scale_log2);
+    k_attn_fwd_tc<<<dim3(n / kBM, (unsigned)blocks), 128, kSmemBytes, s>>>(mQ, mK, mV, O, lse, n, scale_log2);
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "k_attn_fwd_tc");

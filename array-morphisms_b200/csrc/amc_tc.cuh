@@ -208,6 +208,23 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo_bytes, ui
   return d;
 }
 
+// Shared-memory descriptor of an MN-major tf32 operand: 128-byte swizzle with
+// 32-byte atoms (layout type 1, what a TMA box with the 128B_ATOM_32B swizzle
+// writes).  Rows of 128 bytes run along K, each holding 32 consecutive M/N
+// elements, with 32-byte chunk c of row r at c ^ (r & 3).  `mn_atom_bytes` is
+// the distance between successive 32-element M/N blocks (LBO); 4-row K
+// groups are 512 bytes apart (SBO).  With the plain 128-byte swizzle an
+// MN-major tf32 operand reads as zeros.
+__device__ __forceinline__ uint64_t sdesc_mn(uint32_t saddr, uint32_t mn_atom_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((mn_atom_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= (uint64_t)1 << 46;   // version
+  d |= (uint64_t)1 << 61;   // SWIZZLE_128B_BASE32B
+  return d;
+}
+
 // Byte offset of K step k (8 tf32 = 32 bytes) in a K-major operand stored as
 // 32-column (128-byte) regions of region_bytes each.
 __host__ __device__ constexpr uint32_t kstep_off(int k, int region_bytes) {
@@ -240,9 +257,12 @@ int make_tmap_2d_f32(CUtensorMap* map, const void* base, uint64_t rows, uint64_t
 // 128-byte swizzle, plain row-major boxes.
 int make_tmap_2d_f32_box(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                          uint32_t box_cols, uint32_t box_rows, bool swizzle128);
-// Any of the 0-, 32- and 128-byte swizzles; a swizzled box row is exactly the
-// swizzle width (8 floats for 32 bytes: the K-major SW32 operand layout).
+// Swizzles a tensor map can write: none, 32 bytes (16-byte chunks within 32),
+// 128 bytes (16-byte chunks within 128: the K-major operand layout) and 128
+// bytes with 32-byte atoms (the MN-major tf32 operand layout).  A swizzled
+// box row is exactly the swizzle span.
+enum class TmapSwizzle { kNone, k32, k128, k128Atom32 };
 int make_tmap_2d_f32_swz(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
-                         uint32_t box_cols, uint32_t box_rows, int swizzle_bytes);
+                         uint32_t box_cols, uint32_t box_rows, TmapSwizzle swizzle);
 
 }  // namespace amc

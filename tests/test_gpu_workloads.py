@@ -193,8 +193,8 @@ def _attn_ref(q, k, v, scale):
     return p @ v.astype(np.float64)
 
 
-@pytest.mark.parametrize("shape", [(2, 3, 128, 64), (1, 2, 96, 64), (2, 1, 256, 32), (1, 2, 512, 64),
-                                   (1, 2, 2048, 64)])
+@pytest.mark.parametrize("shape", [(2, 3, 128, 64), (1, 2, 96, 64), (2, 1, 256, 32), (1, 2, 384, 64),
+                                   (1, 2, 512, 64), (1, 2, 2048, 64)])
 def test_attention_entry_points(amc, shape):
     """Forward against the oracle's 3-pass kernel; backward against the
     double-precision VJP.  Tolerance 2e-3 of the output scale (TF32 tensor
