@@ -599,14 +599,14 @@ __device__ __forceinline__ Num raw_num(unsigned long long raw, int dtype) {
 
 // One element of a small program on named registers (stack slots s0..s2).
 template <bool EXACT>
-__device__ __forceinline__ void eval_staged(const DProg& P, const DLeaf* L, unsigned long long r0,
+__device__ __forceinline__ void eval_staged(const amc_insn* code, int n, const DLeaf* L, unsigned long long r0,
                                             unsigned long long r1, double& vf, long long& vi) {
   if (!EXACT) {
     const double l0 = raw_f(r0, L[0].dtype), l1 = raw_f(r1, L[1].dtype);
     double s0 = 0.0, s1 = 0.0, s2 = 0.0;
     int sp = 0;
-    for (int pc = 0; pc < P.n; ++pc) {
-      const amc_insn I = P.code[pc];
+    for (int pc = 0; pc < n; ++pc) {
+      const amc_insn I = code[pc];
       if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST) {
         const double t = I.op == AMC_OP_CONST ? I.imm : (I.a == 0 ? l0 : l1);
         if (sp == 0) s0 = t;
@@ -629,8 +629,8 @@ __device__ __forceinline__ void eval_staged(const DProg& P, const DLeaf* L, unsi
     const Num l0 = raw_num(r0, L[0].dtype), l1 = raw_num(r1, L[1].dtype);
     Num s0 = nex(0), s1 = nex(0), s2 = nex(0);
     int sp = 0;
-    for (int pc = 0; pc < P.n; ++pc) {
-      const amc_insn I = P.code[pc];
+    for (int pc = 0; pc < n; ++pc) {
+      const amc_insn I = code[pc];
       if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST || I.op == AMC_OP_ICONST) {
         const Num t = I.op == AMC_OP_CONST ? nfl(I.imm) : I.op == AMC_OP_ICONST ? nex((long long)I.imm) : (I.a == 0 ? l0 : l1);
         if (sp == 0) s0 = t;
@@ -772,11 +772,12 @@ __device__ __forceinline__ void vec_binary_f(int op, double (&x)[V], const doubl
   }
 }
 template <int V>
-__device__ __forceinline__ void eval_vec_f(const DProg& P, const double (&l0)[V], const double (&l1)[V], double (&out)[V]) {
+__device__ __forceinline__ void eval_vec_f(const amc_insn* code, int n, const double (&l0)[V], const double (&l1)[V],
+                                           double (&out)[V]) {
   double s0[V], s1[V], s2[V];
   int sp = 0;
-  for (int pc = 0; pc < P.n; ++pc) {
-    const amc_insn I = P.code[pc];
+  for (int pc = 0; pc < n; ++pc) {
+    const amc_insn I = code[pc];
     if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST) {
       if (sp == 0) vec_push_f(s0, I, l0, l1);
       else if (sp == 1) vec_push_f(s1, I, l0, l1);
@@ -856,12 +857,12 @@ __device__ __forceinline__ void vec_binary_i(int op, long long (&x)[V], const lo
   }
 }
 template <int V>
-__device__ __forceinline__ void eval_vec_i(const DProg& P, const long long (&l0)[V], const long long (&l1)[V],
-                                           long long (&out)[V]) {
+__device__ __forceinline__ void eval_vec_i(const amc_insn* code, int n, const long long (&l0)[V],
+                                           const long long (&l1)[V], long long (&out)[V]) {
   long long s0[V], s1[V], s2[V];
   int sp = 0;
-  for (int pc = 0; pc < P.n; ++pc) {
-    const amc_insn I = P.code[pc];
+  for (int pc = 0; pc < n; ++pc) {
+    const amc_insn I = code[pc];
     if (I.op == AMC_OP_LOAD || I.op == AMC_OP_ICONST) {
       if (sp == 0) vec_push_i(s0, I, l0, l1);
       else if (sp == 1) vec_push_i(s1, I, l0, l1);
@@ -913,7 +914,8 @@ constexpr int kStSC = 96;         // reduced positions per sub-chunk (static sha
 constexpr int kStWorkers = 224;   // warps 1-7 copy and evaluate; warp 0 folds
 
 template <int MODE, int V>
-__device__ __forceinline__ void staged_eval_chunk(const ReduceArgs& a, const unsigned long long* __restrict__ raw0,
+__device__ __forceinline__ void staged_eval_chunk(const ReduceArgs& a, const amc_insn* code,
+                                                  const unsigned long long* __restrict__ raw0,
                                                   const unsigned long long* __restrict__ raw1,
                                                   unsigned long long* __restrict__ vals, long long o0, int tile,
                                                   int wt, bool src_exact) {
@@ -935,7 +937,7 @@ __device__ __forceinline__ void staged_eval_chunk(const ReduceArgs& a, const uns
         l0[k] = slot[k] >= 0 ? raw_f(raw0[e], dt0) : 0.0;
         l1[k] = (slot[k] >= 0 && nl > 1) ? raw_f(raw1[e], dt1) : 0.0;
       }
-      eval_vec_f<V>(a.prog, l0, l1, out);
+      eval_vec_f<V>(code, a.prog.n, l0, l1, out);
 #pragma unroll
       for (int k = 0; k < V; ++k)
         if (slot[k] >= 0)
@@ -949,7 +951,7 @@ __device__ __forceinline__ void staged_eval_chunk(const ReduceArgs& a, const uns
         l0[k] = slot[k] >= 0 ? raw_i(raw0[e], dt0) : 0;
         l1[k] = (slot[k] >= 0 && nl > 1) ? raw_i(raw1[e], dt1) : 0;
       }
-      eval_vec_i<V>(a.prog, l0, l1, out);
+      eval_vec_i<V>(code, a.prog.n, l0, l1, out);
 #pragma unroll
       for (int k = 0; k < V; ++k)
         if (slot[k] >= 0)
@@ -962,7 +964,7 @@ __device__ __forceinline__ void staged_eval_chunk(const ReduceArgs& a, const uns
         const int e = e0 + k * kStWorkers;
         double vf;
         long long vi;
-        eval_staged<true>(a.prog, a.leaf_o, raw0[e], nl > 1 ? raw1[e] : 0ull, vf, vi);
+        eval_staged<true>(code, a.prog.n, a.leaf_o, raw0[e], nl > 1 ? raw1[e] : 0ull, vf, vi);
         vals[slot[k]] = src_exact ? (unsigned long long)vi : (unsigned long long)__double_as_longlong(vf);
       }
     }
@@ -973,7 +975,10 @@ template <int FOLD, int MODE>
 __global__ void __launch_bounds__(256) k_reduce_staged(const __grid_constant__ ReduceArgs a) {
   __shared__ unsigned long long raw[2][2][kStOT * kStSC];        // [buffer][leaf][position][output]
   __shared__ unsigned long long vals[2][kStOT * (kStSC + 1)];    // [buffer][output][position]
+  __shared__ amc_insn code[AMC_PROG_MAX];   // the program, read by every evaluation step
   const int tid = threadIdx.x;
+  for (int i = tid; i < a.prog.n; i += blockDim.x) code[i] = a.prog.code[i];
+  __syncthreads();
   const bool src_exact = !dtype_is_float_d(a.src_dtype);
   const long long o0 = (long long)blockIdx.x * kStOT;
   const int nch = (int)((a.R + kStSC - 1) / kStSC);
@@ -1025,7 +1030,7 @@ __global__ void __launch_bounds__(256) k_reduce_staged(const __grid_constant__ R
     named_bar(1, kStWorkers);   // sub-chunk j has landed for every worker
     const long long r0 = (long long)j * kStSC;
     const int rc = (int)((a.R - r0) < kStSC ? (a.R - r0) : kStSC);
-    staged_eval_chunk<MODE, 4>(a, raw[j & 1][0], raw[j & 1][1], vals[j & 1], o0, kStOT * rc, wt, src_exact);
+    staged_eval_chunk<MODE, 4>(a, code, raw[j & 1][0], raw[j & 1][1], vals[j & 1], o0, kStOT * rc, wt, src_exact);
     // hand sub-chunk j to the fold warp; it arrives here after folding j-1,
     // so vals[j & 1] is free again from the next iteration on
     named_bar(2, 256);

@@ -248,16 +248,21 @@ struct Builder {
     return e;
   }
 
-  static void fill_prog(DProg& P, const std::vector<amc_insn>& prog, const std::vector<View>& leaves) {
-    P.n = (int32_t)prog.size();
+  static void fill_prog(DProg& P, const std::vector<amc_insn>& prog_in, const std::vector<View>& leaves) {
     bool allf = true;
-    for (auto& I : prog) {
+    for (auto& I : prog_in) {
       if (I.op == AMC_OP_ICONST) allf = false;
       if (I.op == AMC_OP_CVT && !dtype_float(I.a)) allf = false;
     }
     for (auto& L : leaves)
       if (!dtype_float(L.dtype)) allf = false;
     P.all_float = allf ? 1 : 0;
+    // In an all-float program every value is a double, so a store to f64 is
+    // the identity and is dropped (config 1's square-then-add carries two).
+    std::vector<amc_insn> prog;
+    for (auto& I : prog_in)
+      if (!(allf && I.op == AMC_OP_CVT && I.a == AMC_F64)) prog.push_back(I);
+    P.n = (int32_t)prog.size();
     int sp = 0, mx = 0;
     for (auto& I : prog) {
       if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST || I.op == AMC_OP_ICONST) ++sp;
