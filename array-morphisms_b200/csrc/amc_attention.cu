@@ -158,20 +158,6 @@ int attention_fwd_simt(const float* Q, const float* K, const float* V, float* O,
 
 using namespace amc;
 
-namespace amc {
-// Tensor-core paths; weak defaults decline every shape.
-__attribute__((weak)) int attention_fwd_tc(const float*, const float*, const float*, float*, float*, long long, int,
-                                           int, int, float, cudaStream_t, bool* handled) {
-  *handled = false;
-  return AMC_OK;
-}
-__attribute__((weak)) int attention_bwd_tc(const float*, const float*, const float*, const float*, const float*,
-                                           const float*, float*, float*, float*, long long, int, int, int, float,
-                                           cudaStream_t, bool* handled) {
-  *handled = false;
-  return AMC_OK;
-}
-}  // namespace amc
 
 extern "C" {
 

@@ -92,10 +92,6 @@ int conv_fwd_tc(const float* X, const float* W, float* Y, const ConvShape& s, cu
 int conv_dgrad_tc(const float* dY, const float* W, float* dX, const ConvShape& s, cudaStream_t st, bool* handled);
 int conv_wgrad_tc(const float* X, const float* dY, float* dW, const ConvShape& s, cudaStream_t st, bool* handled);
 
-// Weak defaults: the tensor-core translation unit overrides these.
-__attribute__((weak)) int conv_fwd_tc(const float*, const float*, float*, const ConvShape&, cudaStream_t, bool* h) { *h = false; return AMC_OK; }
-__attribute__((weak)) int conv_dgrad_tc(const float*, const float*, float*, const ConvShape&, cudaStream_t, bool* h) { *h = false; return AMC_OK; }
-__attribute__((weak)) int conv_wgrad_tc(const float*, const float*, float*, const ConvShape&, cudaStream_t, bool* h) { *h = false; return AMC_OK; }
 
 }  // namespace amc
 

@@ -186,6 +186,11 @@ int launch_attention_generic(const AttnArgs& a, cudaStream_t s);
 // n a multiple of 128; sets *handled = false (and launches nothing) otherwise.
 int attention_fwd_tc(const float* Q, const float* K, const float* V, float* O, float* lse, long long blocks, int n,
                      int dk, int dv, float scale, cudaStream_t s, bool* handled);
+// Tensor-core attention backward for the same operands (n a multiple of 128);
+// sets *handled = false (and launches nothing) for other shapes.
+int attention_bwd_tc(const float* Q, const float* K, const float* V, const float* O, const float* dO,
+                     const float* lse, float* dQ, float* dK, float* dV, long long blocks, int n, int dk, int dv,
+                     float scale, cudaStream_t s, bool* handled);
 
 // Windowed FIR (the polyphase filter-bank reduction).
 struct FirArgs {
