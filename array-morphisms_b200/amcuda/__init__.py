@@ -18,6 +18,10 @@ from .morph import (Concrete, Expr, Morphism, attention_morphism, broadcast_shap
                     morph_reshape, morph_sigmoid, morph_sin, morph_slice, morph_split, morph_sqrt, morph_squeeze,
                     morph_stack, morph_sub, morph_tan, morph_tanh, morph_transpose, morph_unsqueeze, morph_unstack,
                     promote_types)
+from .batch import (add_batch_dimension, batch_fold, batch_map, batch_reduce, batch_scan, batch_size,  # noqa: E402
+                    batch_zip, batched, broadcast_to_batch, concat_batch, extract_batch_element,
+                    make_batch_aware_binop, morph_add_batch, morph_batch_matmul, morph_div_batch, morph_mul_batch,
+                    morph_sub_batch, remove_batch_dimension, stack_into_batch)
 from .realize import DeviceBuffer, Plan, force_morphism, init, morph_to_list, realize, to_numpy  # noqa: E402
 from .context import (MorphismContext, context_stats, finalize_context, make_morphism_context, plan_ctx,  # noqa: E402
                       realize_ctx, reset_context)

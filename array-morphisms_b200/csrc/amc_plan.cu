@@ -395,7 +395,8 @@ struct Builder {
     for (int d = 0; d < nd.rank; ++d) e.shape[d] = nd.shape[d];
     // operand programs become sub-programs; record where each starts
     std::vector<std::vector<amc_insn>> sub(nd.n_in);
-    for (int k = 0; k < nd.n_in; ++k) {
+    bool plain = false;   // an operand fits neither inlined nor as one more leaf
+    for (int k = 0; k < nd.n_in && !plain; ++k) {
       Val x;
       int rc = get(nd.in[k], x);
       if (rc) return rc;
@@ -413,20 +414,26 @@ struct Builder {
         mv.view = m;
         trial = e;
         trial.prog.clear();
-        if (!inline_operand(trial, mv, e.rank, e.shape)) return err(AMC_ERR_INVALID, "operand shape does not broadcast");
+        // still no room when the operands before it took every leaf slot
+        // (a long chain such as a fold over a batch): fall back below
+        if (!inline_operand(trial, mv, e.rank, e.shape)) {
+          plain = true;
+          break;
+        }
       }
       e.leaves = trial.leaves;
       sub[k] = trial.prog;
     }
     // splice: each LOAD k of the node program becomes operand k's sub-program
     std::vector<amc_insn> prog;
-    for (int i = 0; i < nd.prog_len; ++i) {
-      const amc_insn& I = nd.prog[i];
-      if (I.op == AMC_OP_LOAD) prog.insert(prog.end(), sub[I.a].begin(), sub[I.a].end());
-      else prog.push_back(I);
-    }
-    if (prog.size() > AMC_PROG_MAX) {
-      // too long: materialise the operands and use plain loads
+    if (!plain)
+      for (int i = 0; i < nd.prog_len; ++i) {
+        const amc_insn& I = nd.prog[i];
+        if (I.op == AMC_OP_LOAD) prog.insert(prog.end(), sub[I.a].begin(), sub[I.a].end());
+        else prog.push_back(I);
+      }
+    if (plain || prog.size() > AMC_PROG_MAX) {
+      // too long, or too many leaves: materialise the operands and use plain loads
       e.leaves.clear();
       std::vector<View> ms;
       for (int k = 0; k < nd.n_in; ++k) {
