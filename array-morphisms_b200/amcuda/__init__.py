@@ -22,6 +22,10 @@ from .batch import (add_batch_dimension, batch_fold, batch_map, batch_reduce, ba
                     batch_zip, batched, broadcast_to_batch, concat_batch, extract_batch_element,
                     make_batch_aware_binop, morph_add_batch, morph_batch_matmul, morph_div_batch, morph_mul_batch,
                     morph_sub_batch, remove_batch_dimension, stack_into_batch)
+from .grad import (Var, accumulate_grad, backward, make_var, topo_sort, var_abs, var_add, var_cos,  # noqa: E402
+                   var_div, var_exp, var_grad, var_grad_fn, var_log, var_matmul, var_mean, var_mul, var_name,
+                   var_negate, var_parents, var_pow, var_relu, var_requires_grad, var_reshape, var_sigmoid,
+                   var_sin, var_sqrt, var_sub, var_sum, var_tanh, var_transpose, var_value, zero_grad)
 from .realize import DeviceBuffer, Plan, force_morphism, init, morph_to_list, realize, to_numpy  # noqa: E402
 from .context import (MorphismContext, context_stats, finalize_context, make_morphism_context, plan_ctx,  # noqa: E402
                       realize_ctx, reset_context)
