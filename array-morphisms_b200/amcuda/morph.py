@@ -130,6 +130,16 @@ class Concrete(Morphism):
             self._data = self._dev.download()
         return self._data
 
+    def host_changed(self) -> None:
+        """Declare that the host vector was written in place (as the reference
+        does with typed-vector-set! or the optimizer's in-place parameter
+        updates).  The device copy, uploaded once by the first realize that
+        read this array, is dropped, so the next realize uploads the new
+        values.  Views created before the call keep the old device copy."""
+        if self._data is None:
+            raise ValueError("host_changed: the array has no host vector yet (read .data first)")
+        self._dev = None
+
     def values(self) -> np.ndarray:
         """Logical values as a numpy array of this shape (a copy)."""
         flat = self.data

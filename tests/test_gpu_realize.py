@@ -259,3 +259,23 @@ def test_plan_rejects_bad_trees(amc):
     bad.shape = (17,)  # corrupt the node: the planner must refuse it
     with pytest.raises(amc.AmcError):
         amc.realize(bad)
+
+
+def test_leaf_residency_and_host_changed(amc):
+    """A concrete leaf is uploaded once and stays on the device across
+    realizes; after an in-place host write, host_changed() makes the next
+    realize see the new values (the in-place parameter updates of the
+    reference's training loops)."""
+    x = amc.morph_from_numpy(np.arange(6, dtype=np.float64))
+    e = amc.morph_reduce("sum", amc.morph_mul(x, x))
+    assert float(amc.realize(e).values()) == 55.0
+    dev = x._dev
+    assert dev is not None
+    assert float(amc.realize(e).values()) == 55.0 and x._dev is dev   # no re-upload
+    x.data[0] = 10.0
+    assert float(amc.realize(e).values()) == 55.0                     # device copy unchanged
+    x.host_changed()
+    assert float(amc.realize(e).values()) == 155.0
+    # a device-produced value is downloaded only when the host reads it
+    y = amc.realize(amc.morph_add(x, x))
+    assert y._data is None and list(y.values()) == [20.0, 2.0, 4.0, 6.0, 8.0, 10.0]
