@@ -24,8 +24,9 @@ OP = dict(LOAD=1, CONST=2, ICONST=3, CVT=4, NEG=10, ABS=11, FLOOR=12, CEIL=13, S
 RED = dict(sum=0, mean=1, prod=2, max=3, min=4)
 PAD = dict(constant=0, edge=1, reflect=2)
 NODE = dict(LEAF=1, RESHAPE=2, TRANSPOSE=3, SLICE=4, MAP=5, REDUCE=6, PAD=7, IM2COL=8, COL2IM=9, STACK=10,
-            CONCAT=11, MATMUL=12, MATVEC=13, DOT=14, ATTENTION=15)
+            CONCAT=11, MATMUL=12, MATVEC=13, DOT=14, ATTENTION=15, SCAN=16)
 PROG_MAX = 64
+STACK_MAX = 16
 NODE_MAX_IN = 4
 
 

@@ -14,8 +14,9 @@ from __future__ import annotations
 
 from typing import Callable, Sequence
 
-from .morph import (Expr, Morphism, morph_add, morph_concat, morph_div, morph_matmul, morph_mul, morph_reduce,
-                    morph_slice, morph_squeeze, morph_stack, morph_sub, morph_unsqueeze)
+from . import _abi as A
+from .morph import (DTYPES, Concrete, Expr, Morphism, morph_add, morph_concat, morph_div, morph_matmul, morph_mul,
+                    morph_reduce, morph_slice, morph_squeeze, morph_stack, morph_sub, morph_unsqueeze)
 
 __all__ = [
     "batched", "batch_size",
@@ -139,23 +140,98 @@ def batch_zip(fn: Callable[[Morphism, Morphism], Morphism], m1: Morphism, m2: Mo
     return morph_stack([fn(extract_batch_element(m1, i, 0), extract_batch_element(m2, i, 0)) for i in range(n)], 0)
 
 
+class _NotElementwise(Exception):
+    pass
+
+
+def _step_program(r: Morphism, acc: Morphism, e: Morphism, shape: tuple) -> list:
+    """The program of one fold step r = fn(acc, e) over LOAD 0 = acc and
+    LOAD 1 = e, spliced the way realize fuses map nodes (an inner map node's
+    value is rounded to its dtype with CVT).  Raises _NotElementwise unless r
+    is built from acc, e, size-1 constants and map nodes of the element shape
+    only."""
+    if r is acc:
+        return [(A.OP["LOAD"], 0, 0.0)]
+    if r is e:
+        return [(A.OP["LOAD"], 1, 0.0)]
+    if isinstance(r, Concrete) and r.size() == 1 and r.shape == (1,) * len(r.shape):
+        v = r.values().reshape(-1)[0]
+        if r.dtype in ("f32", "f64"):
+            return [(A.OP["CONST"], 0, float(v))]
+        if abs(int(v)) >= 1 << 53:
+            raise _NotElementwise
+        return [(A.OP["ICONST"], 0, float(int(v)))]
+    if not (isinstance(r, Expr) and "prog" in r.meta and "scan" not in r.meta and r.shape == shape):
+        raise _NotElementwise
+    prog = []
+    for (op, a, imm) in r.meta["prog"]:
+        if op == A.OP["LOAD"]:
+            o = r.operands[a]
+            prog += _step_program(o, acc, e, shape)
+            if isinstance(o, Expr) and o is not acc and o is not e:
+                prog.append((A.OP["CVT"], DTYPES[o.dtype], 0.0))
+        else:
+            prog.append((op, a, imm))
+    return prog
+
+
+def _fold_steps(fn, init, m: Morphism):
+    """Run batch-fold's loop (batch-ops.scm:278-300), returning every
+    accumulator and, when every step is the same element-wise program of
+    (acc, element) that keeps init's shape and dtype, that program (else
+    None): realize then runs the whole fold as one SCAN node."""
+    acc, accs, progs = init, [], []
+    elem = tuple(m.shape[1:])
+    ok = isinstance(init, Morphism) and tuple(init.shape) == elem
+    for i in range(m.shape[0]):
+        e = extract_batch_element(m, i, 0)
+        r = fn(acc, e)
+        if ok:
+            try:
+                if not isinstance(r, Expr) or r.shape != elem or r.dtype != init.dtype:
+                    raise _NotElementwise
+                p = _step_program(r, acc, e, elem)
+                ok = not progs or p == progs[0]
+                progs.append(p)
+            except _NotElementwise:
+                ok = False
+        acc = r
+        accs.append(acc)
+    prog = progs[0] if ok and progs else None
+    if prog is not None:
+        sp = depth = 0
+        for (op, _, _) in prog:
+            sp += 1 if op in (A.OP["LOAD"], A.OP["CONST"], A.OP["ICONST"]) else (-1 if op >= A.OP["ADD"] else 0)
+            depth = max(depth, sp)
+        if len(prog) > A.PROG_MAX or depth > A.STACK_MAX:
+            prog = None
+    return accs, prog
+
+
 def batch_fold(fn: Callable[[Morphism, Morphism], Morphism], init, m: Morphism):
     """batch-fold (batch-ops.scm:278-300): acc = fn(acc, element i) for i in
-    order along axis 0, starting from init; returns the final accumulator."""
-    acc = init
-    for i in range(m.shape[0]):
-        acc = fn(acc, extract_batch_element(m, i, 0))
+    order along axis 0, starting from init; returns the final accumulator.
+    The returned tree is the reference's; when the step is element-wise it
+    also records (init, m, step program) so realize runs one SCAN kernel."""
+    accs, prog = _fold_steps(fn, init, m)
+    if not accs:
+        return init
+    acc = accs[-1]
+    if prog is not None:
+        acc = Expr(acc.op, acc.operands, acc.shape, acc.dtype, dict(acc.meta, scan=(init, m, prog, False)),
+                   acc.batch_axis)
     return acc
 
 
 def batch_scan(fn: Callable[[Morphism, Morphism], Morphism], init, m: Morphism) -> Expr:
     """batch-scan (batch-ops.scm:302-322): every intermediate accumulator of
-    batch-fold, stacked along axis 0."""
-    acc, out = init, []
-    for i in range(m.shape[0]):
-        acc = fn(acc, extract_batch_element(m, i, 0))
-        out.append(acc)
-    return morph_stack(out, 0)
+    batch-fold, stacked along axis 0 (one SCAN kernel when the step is
+    element-wise, as for batch_fold)."""
+    accs, prog = _fold_steps(fn, init, m)
+    out = morph_stack(accs, 0)
+    if prog is not None and out.dtype == init.dtype:
+        out.meta["scan"] = (init, m, prog, True)
+    return out
 
 
 # --------------------------------------------------------------- batch-aware arithmetic

@@ -146,6 +146,21 @@ def serialize(root: Morphism) -> Serialized:
             _fill_shape(nd, m.shape)
             nd.leaf = _view(buf, m.dtype, m.shape, m.strides, m.offset)
             S.leaf_owner[buf.handle] = m
+        elif "scan" in m.meta:
+            # batch-fold / batch-scan of an element-wise step: one SCAN node
+            # over (init, x) in place of the tree of per-element map nodes
+            init, x, prog, keep = m.meta["scan"]
+            ins = [visit(init), visit(x)]
+            nd.kind = A.NODE["SCAN"]
+            nd.dtype = DTYPES[m.dtype]
+            _fill_shape(nd, m.shape)
+            nd.n_in = 2
+            nd.in_[0], nd.in_[1] = ins
+            nd.iparam[0] = 1 if keep else 0
+            arr = (A.Insn * len(prog))(*[A.Insn(o, a, imm) for (o, a, imm) in prog])
+            S.keep.append(arr)
+            nd.prog = C.cast(arr, C.POINTER(A.Insn))
+            nd.prog_len = len(prog)
         else:
             assert isinstance(m, Expr)
             ins = [visit(o) for o in m.operands]

@@ -119,6 +119,22 @@ struct ReduceArgs {
 };
 
 int launch_map(const MapArgs& a, cudaStream_t s);
+
+// Fold / scan over axis 0 of x: acc <- round(acc_dtype, prog(acc, x[i])) for
+// i = 0..n-1 from acc = init, at every element position (shape, P positions).
+// Leaf 0 is init, leaf 1 is x[0] (xstep apart along axis 0).
+struct ScanArgs {
+  int32_t rank;
+  int32_t keep;                   // 1: every accumulator, out (n, shape); 0: the last, out (shape)
+  int64_t shape[AMC_MAX_RANK];
+  int64_t P, n, xstep;
+  DLeaf leaf[2];
+  DProg prog;
+  void* out;
+  int32_t out_dtype;
+  int32_t acc_dtype;
+};
+int launch_scan(const ScanArgs& a, cudaStream_t s);
 int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scratch_bytes, size_t* scratch_need);
 
 struct PadArgs {
@@ -170,7 +186,17 @@ struct GemmArgs {
   void* C; int32_t c_dtype;
   double alpha, beta;            // C = alpha*AB + beta*C (beta=0 ignores C)
 };
+
+// GEMM whose result feeds only an element-wise map: the map runs in the
+// GEMM's store, with its leaf `leaf` standing for the GEMM result.
+struct GemmEpiArgs {
+  GemmArgs g;
+  MapArgs map;
+  int32_t leaf;
+  int32_t _pad;
+};
 int launch_gemm(const GemmArgs& a, cudaStream_t s);
+int launch_gemm_epi(const GemmEpiArgs& a, cudaStream_t s);
 
 struct AttnArgs {
   int64_t blocks;

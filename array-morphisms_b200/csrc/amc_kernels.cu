@@ -121,14 +121,19 @@ __device__ __forceinline__ Num bin_op(int op, const Num& a, const Num& b) {
   return nfl(NAN);
 }
 
-// Tagged evaluation (exact integers and doubles).
-__device__ Num eval_prog(const DProg& P, const DLeaf* L, const long long* off) {
+// Tagged evaluation (exact integers and doubles).  With OV, leaf `ov` is not
+// read from memory: its loads yield `ovv` (a GEMM epilogue's own product, a
+// scan's running accumulator).
+template <bool OV = false>
+__device__ Num eval_prog(const DProg& P, const DLeaf* L, const long long* off, int ov = -1, Num ovv = Num()) {
   Num st[AMC_STACK_MAX];
   int sp = 0;
   for (int pc = 0; pc < P.n; ++pc) {
     const amc_insn I = P.code[pc];
     switch (I.op) {
-      case AMC_OP_LOAD: st[sp++] = load_num(L[I.a].ptr, L[I.a].dtype, off[I.a]); break;
+      case AMC_OP_LOAD:
+        st[sp++] = (OV && I.a == ov) ? ovv : load_num(L[I.a].ptr, L[I.a].dtype, off[I.a]);
+        break;
       case AMC_OP_CONST: st[sp++] = nfl(I.imm); break;
       case AMC_OP_ICONST: st[sp++] = nex((long long)I.imm); break;
       case AMC_OP_CVT: st[sp - 1] = round_store(I.a, st[sp - 1]); break;
@@ -189,13 +194,14 @@ __device__ __forceinline__ double round_f(int dtype, double x) {
   }
 }
 
-__device__ double eval_prog_f(const DProg& P, const DLeaf* L, const long long* off) {
+template <bool OV = false>
+__device__ double eval_prog_f(const DProg& P, const DLeaf* L, const long long* off, int ov = -1, double ovv = 0.0) {
   double st[AMC_STACK_MAX];
   int sp = 0;
   for (int pc = 0; pc < P.n; ++pc) {
     const amc_insn I = P.code[pc];
     switch (I.op) {
-      case AMC_OP_LOAD: st[sp++] = load_f(L[I.a].ptr, L[I.a].dtype, off[I.a]); break;
+      case AMC_OP_LOAD: st[sp++] = (OV && I.a == ov) ? ovv : load_f(L[I.a].ptr, L[I.a].dtype, off[I.a]); break;
       case AMC_OP_CONST: st[sp++] = I.imm; break;
       case AMC_OP_CVT: st[sp - 1] = round_f(I.a, st[sp - 1]); break;
       default:
@@ -1329,16 +1335,61 @@ int launch_route(const RouteArgs& a, cudaStream_t s) {
   return AMC_OK;
 }
 
+// ------------------------------------------------------------------ scan / fold over the batch axis
+// One thread per element position p of the accumulator.  acc starts as
+// init[p]; step i evaluates the step program with leaf 0 = acc and leaf 1 =
+// x[i, p], and rounds the value to the accumulator's dtype, as the i-th map
+// node of the per-element tree stores it.  A scan stores every accumulator
+// (row i of the output), a fold only the last.
+template <bool ALLF>
+__global__ void __launch_bounds__(256) k_scan(const __grid_constant__ ScanArgs a) {
+  long long p = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (; p < a.P; p += stride) {
+    long long off[2] = {0, 0};
+    long long rem = p;
+    for (int d = a.rank - 1; d >= 0; --d) {
+      long long s = a.shape[d];
+      long long c = rem % s;
+      rem /= s;
+      off[0] += c * a.leaf[0].strides[d];
+      off[1] += c * a.leaf[1].strides[d];
+    }
+    if (ALLF) {
+      double acc = load_f(a.leaf[0].ptr, a.leaf[0].dtype, off[0]);
+      for (long long i = 0; i < a.n; ++i, off[1] += a.xstep) {
+        acc = round_f(a.acc_dtype, eval_prog_f<true>(a.prog, a.leaf, off, 0, acc));
+        if (a.keep) store_num(a.out, a.out_dtype, i * a.P + p, nfl(acc));
+      }
+      if (!a.keep) store_num(a.out, a.out_dtype, p, nfl(acc));
+    } else {
+      Num acc = load_num(a.leaf[0].ptr, a.leaf[0].dtype, off[0]);
+      for (long long i = 0; i < a.n; ++i, off[1] += a.xstep) {
+        acc = round_store(a.acc_dtype, eval_prog<true>(a.prog, a.leaf, off, 0, acc));
+        if (a.keep) store_num(a.out, a.out_dtype, i * a.P + p, acc);
+      }
+      if (!a.keep) store_num(a.out, a.out_dtype, p, acc);
+    }
+  }
+}
+
+int launch_scan(const ScanArgs& a, cudaStream_t s) {
+  if (a.P == 0 || a.n == 0) return AMC_OK;
+  if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "scan: injected launch failure (AMC_FAULT=launch)");
+  if (a.prog.all_float) k_scan<true><<<grid_for(a.P, 256), 256, 0, s>>>(a);
+  else k_scan<false><<<grid_for(a.P, 256), 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
 // ------------------------------------------------------------------ GEMM (double accumulation)
 // Tiles of 64x64 outputs, 4x4 per thread, K staged through shared memory as
 // doubles.  Each output accumulates a*b in ascending k from 0.0 with separate
 // multiply and add roundings, the reference's loop exactly.
-__global__ void __launch_bounds__(256) k_gemm(const __grid_constant__ GemmArgs a) {
+__device__ __forceinline__ void gemm_tile(const GemmArgs& a, long long m0, long long n0, int tx, int ty,
+                                          double (&acc)[4][4]) {
   __shared__ double As[16][64 + 1];
   __shared__ double Bs[16][64 + 1];
-  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  const long long m0 = (long long)blockIdx.y * 64, n0 = (long long)blockIdx.x * 64;
-  double acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -1366,6 +1417,13 @@ __global__ void __launch_bounds__(256) k_gemm(const __grid_constant__ GemmArgs a
     }
     __syncthreads();
   }
+}
+
+__global__ void __launch_bounds__(256) k_gemm(const __grid_constant__ GemmArgs a) {
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const long long m0 = (long long)blockIdx.y * 64, n0 = (long long)blockIdx.x * 64;
+  double acc[4][4];
+  gemm_tile(a, m0, n0, tx, ty, acc);
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -1380,11 +1438,57 @@ __global__ void __launch_bounds__(256) k_gemm(const __grid_constant__ GemmArgs a
     }
 }
 
+// GEMM with an element-wise epilogue.  Output element (m, n) is element
+// m*N + n of the map's contiguous output.  The map program's leaf `leaf` is
+// the GEMM result: its loads yield the product rounded to the GEMM's dtype,
+// the value a separate map launch would have read back from C, so the result
+// is bit-identical to the two launches and C is neither written nor read.
+__global__ void __launch_bounds__(256) k_gemm_epi(const __grid_constant__ GemmEpiArgs a) {
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  const long long m0 = (long long)blockIdx.y * 64, n0 = (long long)blockIdx.x * 64;
+  double acc[4][4];
+  gemm_tile(a.g, m0, n0, tx, ty, acc);
+  const MapArgs& e = a.map;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      long long m = m0 + ty * 4 + i, n = n0 + tx * 4 + j;
+      if (m < a.g.M && n < a.g.N) {
+        const double v = acc[i][j];
+        const double gv = a.g.c_dtype == AMC_F32 ? (double)__double2float_rn(v) : v;
+        const long long idx = m * a.g.N + n;
+        long long off[kMaxLeaves];
+        for (int l = 0; l < e.nleaf; ++l) off[l] = 0;
+        long long rem = idx;
+        for (int d = e.rank - 1; d >= 0; --d) {
+          long long s = e.shape[d];
+          long long c = rem % s;
+          rem /= s;
+          for (int l = 0; l < e.nleaf; ++l) off[l] += c * e.leaf[l].strides[d];
+        }
+        if (e.prog.all_float) store_num(e.out, e.out_dtype, idx, nfl(eval_prog_f<true>(e.prog, e.leaf, off, a.leaf, gv)));
+        else store_num(e.out, e.out_dtype, idx, eval_prog<true>(e.prog, e.leaf, off, a.leaf, nfl(gv)));
+      }
+    }
+}
+
 int launch_gemm(const GemmArgs& a, cudaStream_t s) {
   if (a.M == 0 || a.N == 0) return AMC_OK;
   if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "gemm: injected launch failure (AMC_FAULT=launch)");
   dim3 g((unsigned)((a.N + 63) / 64), (unsigned)((a.M + 63) / 64));
   k_gemm<<<g, 256, 0, s>>>(a);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
+}
+
+int launch_gemm_epi(const GemmEpiArgs& a, cudaStream_t s) {
+  if (a.g.M == 0 || a.g.N == 0) return AMC_OK;
+  if (a.map.total != a.g.M * a.g.N || a.leaf < 0 || a.leaf >= a.map.nleaf || a.g.alpha != 1.0 || a.g.beta != 0.0)
+    return fail(AMC_ERR_INVALID, "gemm epilogue: map does not cover the product");
+  if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "gemm: injected launch failure (AMC_FAULT=launch)");
+  dim3 g((unsigned)((a.g.N + 63) / 64), (unsigned)((a.g.M + 63) / 64));
+  k_gemm_epi<<<g, 256, 0, s>>>(a);
   AMC_CUDA(cudaGetLastError());
   return AMC_OK;
 }

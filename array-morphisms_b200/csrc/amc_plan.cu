@@ -139,6 +139,10 @@ struct Val {
   int64_t shape[AMC_MAX_RANK] = {0};
   std::vector<View> leaves;
   std::vector<amc_insn> prog;
+  // The buffer of a GEMM result that this value reads through a chain of
+  // single-use map nodes only: materialising the value may fold the chain
+  // into that GEMM's store (0: none).
+  uint64_t fuse_buf = 0;
 };
 
 static amc_insn ins(int op, int a = 0, double imm = 0.0) {
@@ -173,6 +177,26 @@ struct Builder {
   int32_t n;
   Plan* plan;
   std::vector<std::optional<Val>> memo;
+  std::vector<int> uses;   // operand references to each node (+1 for the root)
+  // The most recent GEMM step, while its result may still take an epilogue.
+  struct {
+    size_t step = 0;
+    uint64_t cbuf = 0, abuf = 0, bbuf = 0;
+    GemmArgs g;
+  } tail;
+
+  void count_uses() {
+    uses.assign(n, 0);
+    for (int i = 0; i < n; ++i) {
+      const amc_node& nd = nodes[i];
+      if (nd.kind == AMC_N_LEAF) continue;
+      const int32_t* in = nd.n_in > AMC_NODE_MAX_IN ? nd.in_ext : nd.in;
+      if (!in) continue;
+      for (int k = 0; k < nd.n_in; ++k)
+        if (in[k] >= 0 && in[k] < n) ++uses[in[k]];
+    }
+    ++uses[n - 1];
+  }
 
   int err(int code, const std::string& m) { return fail(code, "plan: " + m); }
 
@@ -274,7 +298,61 @@ struct Builder {
   }
 
   // Materialise a value into a fresh contiguous slot.
-  int materialize(const Val& x, View& out) {
+  // Fold an expression over the result of the GEMM step just emitted into
+  // that step: allowed when the expression is the GEMM result's only reader
+  // (fuse_buf, tracked through single-use nodes), no step came after the
+  // GEMM, and the expression reads the result exactly once, as the whole
+  // row-major (M, N) array in its own element order.
+  int try_fuse_gemm(const Val& e, View& out, bool& done) {
+    done = false;
+    if (!e.expr || !e.fuse_buf || e.fuse_buf != tail.cbuf || plan->steps.size() != tail.step + 1) return AMC_OK;
+    const int64_t total = numel(e.rank, e.shape);
+    if (total == 0 || total != tail.g.M * tail.g.N || tail.g.alpha != 1.0 || tail.g.beta != 0.0) return AMC_OK;
+    int gl = -1;
+    for (size_t l = 0; l < e.leaves.size(); ++l)
+      if (e.leaves[l].buf == tail.cbuf) {
+        if (gl >= 0) return AMC_OK;
+        gl = (int)l;
+      }
+    if (gl < 0) return AMC_OK;
+    const View& L = e.leaves[gl];
+    if (L.offset != 0 || L.dtype != tail.g.c_dtype || L.rank != e.rank) return AMC_OK;
+    int64_t rm[AMC_MAX_RANK];
+    row_major(e.rank, e.shape, rm);
+    for (int d = 0; d < e.rank; ++d)
+      if (e.shape[d] > 1 && L.strides[d] != rm[d]) return AMC_OK;
+    // the epilogue writes while the GEMM reads A and B: keep them live
+    std::vector<uint64_t> reads = reads_of(e.leaves);
+    reads.push_back(tail.abuf);
+    reads.push_back(tail.bbuf);
+    int rc = new_slot(e.dtype, e.rank, e.shape, reads, out);
+    if (rc) return rc;
+    GemmEpiArgs ga;
+    memset(&ga, 0, sizeof ga);
+    ga.g = tail.g;
+    MapArgs& a = ga.map;
+    a.rank = e.rank;
+    for (int d = 0; d < e.rank; ++d) a.shape[d] = e.shape[d];
+    a.total = total;
+    a.nleaf = (int32_t)e.leaves.size();
+    for (size_t l = 0; l < e.leaves.size(); ++l) a.leaf[l] = dleaf(e.leaves[l]);
+    fill_prog(a.prog, e.prog, e.leaves);
+    a.out = ptr_of(out.buf);
+    a.out_dtype = e.dtype;
+    collapse_map(a);
+    ga.leaf = gl;
+    plan->steps.back() = [ga](cudaStream_t s) { return launch_gemm_epi(ga, s); };
+    tail.cbuf = 0;
+    done = true;
+    return AMC_OK;
+  }
+
+  int materialize(const Val& x, View& out, bool may_fuse = false) {
+    if (may_fuse) {
+      bool done = false;
+      int rc = try_fuse_gemm(x, out, done);
+      if (rc || done) return rc;
+    }
     Val e = as_expr(x);
     int rc = new_slot(e.dtype, e.rank, e.shape, reads_of(e.leaves), out);
     if (rc) return rc;
@@ -337,7 +415,7 @@ struct Builder {
     int rc = get(idx, v);
     if (rc) return rc;
     if (!v.expr) { out = v.view; return AMC_OK; }
-    rc = materialize(v, out);
+    rc = materialize(v, out, uses[idx] == 1);
     if (rc) return rc;
     memo[idx] = Val();
     memo[idx]->view = out;
@@ -370,10 +448,10 @@ struct Builder {
     return true;
   }
 
-  int node_map(const amc_node& nd, Val& out) {
-    if (nd.n_in < 1 || nd.n_in > AMC_NODE_MAX_IN) return err(AMC_ERR_INVALID, "map node needs 1..4 operands");
-    if (!nd.prog || nd.prog_len <= 0 || nd.prog_len > AMC_PROG_MAX) return err(AMC_ERR_INVALID, "map node without a program");
-    // validate program stack discipline
+  // A node program over nd.n_in operands must load only those operands, stay
+  // within the stack and leave exactly one value.
+  int check_prog(const amc_node& nd) {
+    if (!nd.prog || nd.prog_len <= 0 || nd.prog_len > AMC_PROG_MAX) return err(AMC_ERR_INVALID, "node without a program");
     {
       int sp = 0;
       for (int i = 0; i < nd.prog_len; ++i) {
@@ -388,6 +466,13 @@ struct Builder {
       }
       if (sp != 1) return err(AMC_ERR_INVALID, "program must leave one value");
     }
+    return AMC_OK;
+  }
+
+  int node_map(const amc_node& nd, Val& out) {
+    if (nd.n_in < 1 || nd.n_in > AMC_NODE_MAX_IN) return err(AMC_ERR_INVALID, "map node needs 1..4 operands");
+    int prc = check_prog(nd);
+    if (prc) return prc;
     Val e;
     e.expr = true;
     e.dtype = nd.dtype;
@@ -405,7 +490,7 @@ struct Builder {
       if (!inline_operand(trial, x, e.rank, e.shape)) {
         View m;
         if (x.expr) {
-          rc = materialize(x, m);
+          rc = materialize(x, m, uses[nd.in[k]] == 1);
           if (rc) return rc;
         } else {
           m = x.view;
@@ -423,6 +508,7 @@ struct Builder {
       }
       e.leaves = trial.leaves;
       sub[k] = trial.prog;
+      if (!e.fuse_buf && x.fuse_buf && uses[nd.in[k]] == 1) e.fuse_buf = x.fuse_buf;
     }
     // splice: each LOAD k of the node program becomes operand k's sub-program
     std::vector<amc_insn> prog;
@@ -435,6 +521,7 @@ struct Builder {
     if (plain || prog.size() > AMC_PROG_MAX) {
       // too long, or too many leaves: materialise the operands and use plain loads
       e.leaves.clear();
+      e.fuse_buf = 0;
       std::vector<View> ms;
       for (int k = 0; k < nd.n_in; ++k) {
         View m;
@@ -915,6 +1002,57 @@ struct Builder {
   }
 
   // ----------------------------------------------------------- BLAS-shaped nodes
+  // batch-fold / batch-scan (batch-ops.scm:278-322) of an element-wise step:
+  // one thread per element position runs the n steps in order.
+  int node_scan(const amc_node& nd, Val& out) {
+    if (nd.n_in != 2) return err(AMC_ERR_INVALID, "scan needs init and the batched operand");
+    int rc = check_prog(nd);
+    if (rc) return rc;
+    View I, X;
+    rc = concrete(nd.in[0], I);
+    if (!rc) rc = concrete(nd.in[1], X);
+    if (rc) return rc;
+    if (X.rank < 1 || I.rank != X.rank - 1) return err(AMC_ERR_INVALID, "scan: init must have the element shape");
+    for (int d = 0; d < I.rank; ++d)
+      if (I.shape[d] != X.shape[d + 1]) return err(AMC_ERR_INVALID, "scan: init must have the element shape");
+    if (I.dtype != nd.dtype) return err(AMC_ERR_INVALID, "scan: the accumulator keeps the init dtype");
+    const bool keep = nd.iparam[0] != 0;
+    const int64_t n = X.shape[0];
+    if (n < 1) return err(AMC_ERR_INVALID, "scan over an empty batch");
+    const View& R = keep ? X : I;
+    if (nd.rank != R.rank) return err(AMC_ERR_INVALID, "scan result shape mismatch");
+    for (int d = 0; d < nd.rank; ++d)
+      if (nd.shape[d] != R.shape[d]) return err(AMC_ERR_INVALID, "scan result shape mismatch");
+    View o;
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, {I.buf, X.buf}, o);
+    if (rc) return rc;
+    View xe = X;   // element 0 of x: drop axis 0
+    xe.rank = X.rank - 1;
+    for (int d = 0; d < xe.rank; ++d) {
+      xe.shape[d] = X.shape[d + 1];
+      xe.strides[d] = X.strides[d + 1];
+    }
+    ScanArgs a;
+    memset(&a, 0, sizeof a);
+    a.rank = I.rank;
+    for (int d = 0; d < I.rank; ++d) a.shape[d] = I.shape[d];
+    a.P = numel(I.rank, I.shape);
+    a.n = n;
+    a.xstep = X.strides[0];
+    a.keep = keep ? 1 : 0;
+    a.leaf[0] = dleaf(I);
+    a.leaf[1] = dleaf(xe);
+    fill_prog(a.prog, std::vector<amc_insn>(nd.prog, nd.prog + nd.prog_len), {I, xe});
+    a.out = ptr_of(o.buf);
+    a.out_dtype = nd.dtype;
+    a.acc_dtype = I.dtype;
+    plan->steps.push_back([a](cudaStream_t s) { return launch_scan(a, s); });
+    plan->launches += 1;
+    out = Val();
+    out.view = o;
+    return AMC_OK;
+  }
+
   int node_gemm(const amc_node& nd, Val& out) {
     if (nd.n_in != 2) return err(AMC_ERR_INVALID, "matmul/matvec/dot need two operands");
     View A, B;
@@ -953,8 +1091,14 @@ struct Builder {
     g.C = ptr_of(o.buf);
     plan->steps.push_back([g](cudaStream_t s) { return launch_gemm(g, s); });
     plan->launches += 1;
+    tail.step = plan->steps.size() - 1;
+    tail.cbuf = o.buf;
+    tail.abuf = A.buf;
+    tail.bbuf = B.buf;
+    tail.g = g;
     out = Val();
     out.view = o;
+    out.fuse_buf = o.buf;
     return AMC_OK;
   }
 
@@ -1043,9 +1187,12 @@ struct Builder {
       case AMC_N_MATVEC:
       case AMC_N_DOT: rc = node_gemm(nd, v); break;
       case AMC_N_ATTENTION: rc = node_attention(nd, v); break;
+      case AMC_N_SCAN: rc = node_scan(nd, v); break;
       default: return err(AMC_ERR_INVALID, "unknown node kind");
     }
     if (rc) return rc;
+    if (nd.kind != AMC_N_MAP && nd.kind != AMC_N_MATMUL && nd.kind != AMC_N_MATVEC && nd.kind != AMC_N_DOT)
+      v.fuse_buf = 0;
     memo[i] = v;
     out = v;
     return AMC_OK;
@@ -1068,11 +1215,12 @@ int plan_create(void* ctx, const amc_node* nodes, int32_t n, uint64_t* out) {
   Plan* p = new Plan();
   p->ctx = ctx;
   Builder b{nodes, n, p, std::vector<std::optional<Val>>(n)};
+  b.count_uses();
   Val root;
   int rc = b.get(n - 1, root);
   if (!rc) {
     View res;
-    if (root.expr) rc = b.materialize(root, res);
+    if (root.expr) rc = b.materialize(root, res, b.uses[n - 1] == 1);
     else res = root.view;
     if (!rc) {
       amc_view& r = p->result;

@@ -148,6 +148,11 @@ typedef struct amc_insn {
  *   MATVEC     2 operands (M,N)x(N)
  *   DOT        2 operands (N)x(N) -> ()
  *   ATTENTION  3 operands Q K V, fparam[0] = scale   (blas-exec.scm:334-398)
+ *   SCAN       2 operands init (element shape E) and x (n, E...), prog over LOAD 0 = the
+ *              accumulator and LOAD 1 = element i; iparam[0] = 1 keeps every accumulator
+ *              (batch-scan, result (n, E...)), 0 the last (batch-fold, result E); the
+ *              accumulator is rounded to the init dtype after each step, as the per-element
+ *              tree of batch-ops.scm:278-322 stores it.  Replaces that tree of n map nodes.
  * The planner recognises reshape(matmul(W, im2col(X))) on one f32 (C, H, W)
  * image as a convolution (detect-conv2d-pattern, realization.scm:136-164) and
  * runs amc_conv2d_fwd_f32 on it; an ATTENTION node of contiguous f32 operands
@@ -167,6 +172,7 @@ typedef struct amc_insn {
 #define AMC_N_MATVEC   13
 #define AMC_N_DOT      14
 #define AMC_N_ATTENTION 15
+#define AMC_N_SCAN     16
 
 #define AMC_NODE_MAX_IN 4
 

@@ -170,3 +170,112 @@ def test_batch_trees_on_device_bitwise(amc, dt):
         got, ref = np.asarray(amc.realize(e).values()), np.asarray(oracle.values(e))
         assert got.shape == ref.shape and got.dtype == ref.dtype
         assert np.array_equal(got.reshape(-1).view(np.uint8), ref.reshape(-1).view(np.uint8)), "not bit-identical"
+
+
+# ------------------------------------------------------------------ fold / scan as one SCAN node
+
+_STEPS = {
+    "add": am.morph_add,
+    "e_minus_acc": lambda acc, e: am.morph_sub(e, acc),
+    "decay": lambda acc, e: am.morph_add(am.morph_map(lambda t: t * 0.5 - 1, acc), e),
+    "relu_sq": lambda acc, e: am.morph_relu(am.morph_add(acc, am.morph_mul(e, e))),
+    "lifted_const": lambda acc, e: acc * 3 + e,
+    "max_like": lambda acc, e: am.morph_add(am.morph_mul(am.morph_gt(acc, e), am.morph_sub(acc, e)), e),
+}
+
+
+def _scan_case(rng, dt, shape=(9, 4, 3)):
+    x = am.morph_from_numpy(_rand(rng, shape, dt))
+    init = am.morph_from_numpy(_rand(rng, shape[1:], dt))
+    return x, init
+
+
+@pytest.mark.parametrize("dt", ["f32", "f64", "s32"])
+@pytest.mark.parametrize("name", sorted(_STEPS))
+def test_fold_step_program_pinned_by_oracle_steps(dt, name):
+    """The compiled step program, applied by the oracle one step at a time
+    (acc <- map(prog, acc, x[i]) stored in the accumulator dtype), gives
+    bit-for-bit the reference's per-element tree for both fold and scan."""
+    from amcuda import batch as B
+    rng = np.random.default_rng(3)
+    x, init = _scan_case(rng, dt)
+    fn = _STEPS[name]
+    accs, prog = B._fold_steps(fn, init, x)
+    tree_fold = am.batch_fold(fn, init, x)
+    if accs[-1].dtype != init.dtype:
+        assert prog is None and "scan" not in tree_fold.meta      # the dtype changes: stays a tree
+        return
+    assert prog is not None and tree_fold.meta["scan"][2] == prog
+    acc = init
+    steps = []
+    for i in range(x.shape[0]):
+        e = am.extract_batch_element(x, i)
+        acc = oracle.realize(am.Expr("map", [acc, e], acc.shape, init.dtype, {"prog": prog}))
+        steps.append(oracle.values(acc))
+    ref = oracle.values(tree_fold)
+    assert np.array_equal(np.asarray(steps[-1]).view(np.uint8), np.asarray(ref).view(np.uint8))
+    scan = am.batch_scan(fn, init, x)
+    assert scan.meta["scan"][3] is True
+    assert np.array_equal(np.stack(steps).view(np.uint8), np.asarray(oracle.values(scan)).view(np.uint8))
+
+
+def test_fold_step_program_refusals():
+    from amcuda import batch as B
+    x = ml([float(i) for i in range(12)], (4, 3))
+    init = ml([0.0, 0.0, 0.0], (3,))
+    assert B._fold_steps(am.morph_add, init, x)[1] == [(1, 0, 0.0), (1, 1, 0.0), (40, 0, 0.0)]
+    # a step that is not element-wise, a shape that broadcasts, the identity on acc
+    assert B._fold_steps(lambda a, e: am.morph_add(a, am.morph_reduce("sum", e, [0], True)), init, x)[1] is None
+    assert B._fold_steps(am.morph_add, ml([0.0], (1,)), x)[1] is None
+    assert B._fold_steps(lambda a, e: a, init, x)[1] is None
+    # an operand from outside the step (a full-shape array) is not a constant
+    w = ml([1.0, 2.0, 3.0], (3,))
+    assert B._fold_steps(lambda a, e: am.morph_add(am.morph_mul(a, w), e), init, x)[1] is None
+    # an empty batch: the fold is init itself
+    assert am.batch_fold(am.morph_add, init, am.morph_from_numpy(np.zeros((0, 3)))) is init
+
+
+def _oracle_dag(m, memo):
+    """The oracle's value of a tree, each shared node realized once (a step
+    that reads the accumulator twice makes the per-element tree a DAG whose
+    paths double with every element)."""
+    if not isinstance(m, am.Expr):
+        return m
+    if id(m) not in memo:
+        ops = [_oracle_dag(o, memo) for o in m.operands]
+        memo[id(m)] = oracle.realize(am.Expr(m.op, ops, m.shape, m.dtype, m.meta, m.batch_axis))
+    return memo[id(m)]
+
+
+def _scan_device_cases(dt):
+    rng = np.random.default_rng(11)
+    x, init = _scan_case(rng, dt, (37, 33, 5))
+    xt = am.morph_transpose(am.morph_from_numpy(_rand(rng, (33, 5, 37), dt)), (2, 0, 1))
+    for name in sorted(_STEPS):
+        for src in (x, xt):
+            for tree in (am.batch_fold(_STEPS[name], init, src), am.batch_scan(_STEPS[name], init, src)):
+                yield name, tree, np.asarray(oracle.values(_oracle_dag(tree, {})))
+
+
+@pytest.mark.parametrize("dt", ["f32", "f64", "s32"])
+def test_scan_device_cases_oracle_cost(dt):
+    """The references of the device test below come from the oracle in
+    linear time (shared nodes realized once)."""
+    n = sum(1 for _ in _scan_device_cases(dt))
+    assert n == len(_STEPS) * 4
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dt", ["f32", "f64", "s32"])
+def test_scan_node_on_device_bitwise(amc, dt):
+    """Fold and scan of element-wise steps run as one SCAN launch, bit-exact
+    against the oracle's per-element tree; a strided (transposed) batch and
+    a dtype-changing step (left as a tree) too."""
+    for name, tree, ref in _scan_device_cases(dt):
+        p = amc.Plan(tree)
+        if "scan" in tree.meta:
+            assert p.stats()["launches"] == 1, name
+        p.execute()
+        got = np.asarray(p.result().values())
+        assert got.shape == ref.shape and got.dtype == ref.dtype
+        assert np.array_equal(got.reshape(-1).view(np.uint8), ref.reshape(-1).view(np.uint8)), name

@@ -279,3 +279,52 @@ def test_leaf_residency_and_host_changed(amc):
     # a device-produced value is downloaded only when the host reads it
     y = amc.realize(amc.morph_add(x, x))
     assert y._data is None and list(y.values()) == [20.0, 2.0, 4.0, 6.0, 8.0, 10.0]
+
+
+def _gemm_epilogue_trees(amc, dt):
+    """(name, tree, launches) for map-over-GEMM trees; launches is the plan's
+    launch count with the epilogue folded into the GEMM where it may be."""
+    rng = np.random.default_rng(23)
+    npdt = np.float32 if dt == "f32" else np.float64
+    A = amc.morph_from_numpy(rng.standard_normal((37, 29)).astype(npdt))
+    B = amc.morph_from_numpy(rng.standard_normal((29, 45)).astype(npdt))
+    b1 = amc.morph_from_numpy(rng.standard_normal((45,)).astype(npdt))
+    W2 = amc.morph_from_numpy(rng.standard_normal((45, 19)).astype(npdt))
+    b2 = amc.morph_from_numpy(rng.standard_normal((1, 19)).astype(npdt))
+    S = amc.morph_from_numpy(rng.standard_normal((40, 40)).astype(npdt))
+    v = amc.morph_from_numpy(rng.standard_normal((29,)).astype(npdt))
+    x = amc.morph_from_numpy(rng.standard_normal((300,)).astype(npdt))
+    X = amc.morph_from_numpy(rng.standard_normal((37, 45, 3)).astype(npdt))
+    h = amc.morph_matmul(A, B)
+    hs = amc.morph_matmul(S, S)
+    return [
+        ("relu_bias", amc.morph_relu(amc.morph_add(amc.morph_matmul(A, B), b1)), 1),
+        ("sigmoid_scale", amc.morph_sigmoid(amc.morph_map(lambda t: t * 0.5 - 0.25, amc.morph_matmul(A, B))), 1),
+        ("int_consts", amc.morph_map(lambda t: t * 2 + 1, amc.morph_matmul(A, B)), 1),
+        ("two_layers", amc.morph_relu(amc.morph_add(amc.morph_matmul(
+            amc.morph_relu(amc.morph_add(amc.morph_matmul(A, B), b1)), W2), b2)), 2),
+        ("matvec_tanh", amc.morph_tanh(amc.morph_map(lambda t: t - 1.5, amc.morph_matvec(A, v))), 1),
+        ("dot_exp", amc.morph_exp(amc.morph_map(lambda t: t * 0.001, amc.morph_dot(x, x))), 1),
+        # the GEMM result also read transposed: not folded
+        ("plus_transpose", amc.morph_add(hs, amc.morph_transpose(hs, (1, 0))), 2),
+        # two readers of the result (a map and a reduction): not folded
+        ("two_readers", amc.morph_add(amc.morph_relu(h), amc.morph_reduce("sum", h, [1], True)), None),
+        # a launch between the GEMM and the map: not folded
+        ("step_between", amc.morph_add(amc.morph_matmul(A, B), amc.morph_reduce("sum", X, [2])), 3),
+    ]
+
+
+@pytest.mark.parametrize("dt", ["f32", "f64"])
+def test_gemm_epilogue_fusion_bitwise(amc, dt):
+    """An element-wise map whose only input path to a GEMM result is through
+    single-use map nodes runs in the GEMM's store (one launch fewer); values
+    are bit-identical to the oracle's separate GEMM and map, and trees that
+    must not be folded keep the separate launches."""
+    for name, tree, launches in _gemm_epilogue_trees(amc, dt):
+        p = amc.Plan(tree)
+        if launches is not None:
+            assert p.stats()["launches"] == launches, name
+        p.execute()
+        got = p.result().values()
+        ref = oracle.realize(tree).values()
+        _same(got, ref)
