@@ -384,11 +384,17 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
 #pragma unroll
       for (int c = 0; c < 4; ++c) tmem_ld32_nowait(t_s + 32 * c, sr[c]);
       tmem_ld_wait();
-      float mraw = -INFINITY;
+      // row max and row sum over 8 independent partials: a single chain of
+      // 128 dependent operations per thread left the few softmax warps idle
+      float mx8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mx8[k] = -INFINITY;
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int i = 0; i < 32; ++i) mraw = fmaxf(mraw, __uint_as_float(sr[c][i]));
+        for (int i = 0; i < 32; ++i) mx8[i & 7] = fmaxf(mx8[i & 7], __uint_as_float(sr[c][i]));
+      const float mraw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                               fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mt = mraw * scale_log2;
       const bool up = mt > m + 8.f;
       if (__any_sync(0xffffffffu, up)) {
@@ -411,20 +417,22 @@ __global__ void __launch_bounds__(kThreads3, 1) k_attn_fwd_tc3(const __grid_cons
           }
         }
       }
-      float sum = 0.f;
+      float sm8[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sm8[k] = 0.f;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float p = ex2_approx(fmaf(__uint_as_float(sr[c][i]), scale_log2, -m));
-          sum += p;
+          sm8[i & 7] += p;
           v[i] = round_tf32_int(p);
         }
         tmem_st32(t_s + 32 * c, v);
       }
       tmem_st_wait();
-      l += sum;
+      l += ((sm8[0] + sm8[1]) + (sm8[2] + sm8[3])) + ((sm8[4] + sm8[5]) + (sm8[6] + sm8[7]));
       tc_fence_before();
       mbar_arrive(&p_full[g]);
     }
