@@ -66,6 +66,29 @@ def test_context_replay_of_multi_kernel_program(amc):
         _same(amc.realize_ctx(ctx, out).values(), r0)
 
 
+def test_context_replay_with_gemm_epilogues_and_scan(amc):
+    """Two GEMMs with folded epilogues feeding a SCAN node, traced, coloured
+    and replayed: the epilogue outputs are written while their GEMM reads A
+    and B, so colouring must keep those live; replay is bit-identical."""
+    from test_batch_ops import _oracle_dag
+    rng = np.random.default_rng(4)
+    x = amc.morph_from_numpy(rng.standard_normal((64, 48)))
+    w1 = amc.morph_from_numpy(rng.standard_normal((48, 32)))
+    b1 = amc.morph_from_numpy(rng.standard_normal((32,)))
+    w2 = amc.morph_from_numpy(rng.standard_normal((32, 16)))
+    h = amc.morph_relu(amc.morph_add(amc.morph_matmul(x, w1), b1))
+    y = amc.morph_map(lambda t: t * 0.5 - t * t * 0.01, amc.morph_matmul(h, w2))
+    out = amc.batch_scan(amc.morph_add, amc.morph_from_numpy(np.zeros(16)), y)
+    assert "scan" in out.meta and amc.Plan(out).stats()["launches"] == 3
+    ctx = amc.make_morphism_context()
+    r0 = amc.realize_ctx(ctx, out, pin_output=True).values()
+    _same(r0, oracle.values(_oracle_dag(out, {})))
+    amc.finalize_context(ctx)
+    for _ in range(3):
+        amc.reset_context(ctx)
+        _same(amc.realize_ctx(ctx, out).values(), r0)
+
+
 def test_context_replay_state_errors(amc):
     ctx = amc.make_morphism_context()
     with pytest.raises(amc.AmcError):
