@@ -255,6 +255,12 @@ def _scan_device_cases(dt):
         for src in (x, xt):
             for tree in (am.batch_fold(_STEPS[name], init, src), am.batch_scan(_STEPS[name], init, src)):
                 yield name, tree, np.asarray(oracle.values(_oracle_dag(tree, {})))
+    # one element, and a strided init (every other column of a wider array)
+    one = am.morph_from_numpy(_rand(rng, (1, 33, 5), dt))
+    wide = am.morph_from_numpy(_rand(rng, (33, 10), dt))
+    init_s = am.morph_slice(wide, [0, 0], [33, 10], [1, 2])
+    for tree in (am.batch_scan(am.morph_add, init, one), am.batch_fold(am.morph_sub, init_s, x)):
+        yield "edge", tree, np.asarray(oracle.values(_oracle_dag(tree, {})))
 
 
 @pytest.mark.parametrize("dt", ["f32", "f64", "s32"])
@@ -262,7 +268,7 @@ def test_scan_device_cases_oracle_cost(dt):
     """The references of the device test below come from the oracle in
     linear time (shared nodes realized once)."""
     n = sum(1 for _ in _scan_device_cases(dt))
-    assert n == len(_STEPS) * 4
+    assert n == len(_STEPS) * 4 + 2
 
 
 @pytest.mark.gpu

@@ -311,6 +311,12 @@ def _gemm_epilogue_trees(amc, dt):
         ("two_readers", amc.morph_add(amc.morph_relu(h), amc.morph_reduce("sum", h, [1], True)), None),
         # a launch between the GEMM and the map: not folded
         ("step_between", amc.morph_add(amc.morph_matmul(A, B), amc.morph_reduce("sum", X, [2])), 3),
+        # an empty contraction (K = 0): the epilogue sees zeros
+        ("k_zero", amc.morph_relu(amc.morph_add(amc.morph_matmul(
+            amc.morph_from_numpy(np.zeros((5, 0), npdt)), amc.morph_from_numpy(np.zeros((0, 7), npdt))),
+            amc.morph_from_numpy(np.arange(7, dtype=npdt) - 3))), 1),
+        # a comparison: the epilogue's output dtype (f64) differs from the GEMM's
+        ("compare", amc.morph_gt(amc.morph_matmul(A, B), amc.morph_from_list([0.0], (1,), dt)), 1),
     ]
 
 
