@@ -45,9 +45,12 @@ def promote_types(d1: str, d2: str) -> str:
 
 
 def infer_reduction_dtype(op: str, dtype: str) -> str:
-    """infer-reduction-dtype (core.scm:607-621)."""
+    """infer-reduction-dtype (core.scm:607-621): mean promotes integers to
+    f64, argmax/argmin give s32 indices, the rest keep the dtype."""
     if op == "mean":
         return dtype if dtype_floating(dtype) else "f64"
+    if op in ("argmax", "argmin"):
+        return "s32"
     return dtype
 
 
