@@ -143,6 +143,36 @@ case("matmul f32", B + ":839-845", ["matmul", inp([[1, 2], [3, 4]], [2, 2], "f32
      [[19, 22], [43, 50]], dtype="f32", tol=1e-4)
 case("dot with stride-2 slice operand", B + ":463-470",
      ["dot", ["slice", inp(list(range(10)), [10]), [0], [10], 2], inp([1, 1, 1, 1, 1], [5])], 20, shape=[])
+# the stride-aware kernels of test-blas.scm groups 4-6 and the strided GEMM
+# group: transposed and sliced operands, identities, zeros, scalars
+I2 = inp([[1, 0], [0, 1]], [2, 2])
+I3 = inp([[1, 0, 0], [0, 1, 0], [0, 0, 1]], [3, 3])
+src32 = inp([[1, 2], [3, 4], [5, 6]], [3, 2])
+case("gemm identity", B + ":332-336", ["matmul", inp([[1, 2, 3], [4, 5, 6], [7, 8, 9]], [3, 3]), I3],
+     [[1, 2, 3], [4, 5, 6], [7, 8, 9]])
+case("gemm zero", B + ":338-342", ["matmul", inp([[1, 2], [3, 4]], [2, 2]), inp([[0, 0], [0, 0]], [2, 2])],
+     [[0, 0], [0, 0]])
+case("gemm (3,4)x(4,2) shape", B + ":351-355",
+     ["matmul", inp(list(range(1, 13)), [3, 4]), inp(list(range(1, 9)), [4, 2])], shape=[3, 2])
+case("gemm transposed operand", B + ":357-366", ["matmul", ["transpose", src32, None], I3], [[1, 3, 5], [2, 4, 6]])
+case("gemm column-slice operand", B + ":368-377",
+     ["matmul", ["slice", inp([[1, 2, 3, 4], [5, 6, 7, 8], [9, 10, 11, 12]], [3, 4]), [0, 1], [3, 4], None], I3],
+     [[2, 3, 4], [6, 7, 8], [10, 11, 12]])
+case("gemv identity", B + ":393-397", ["matvec", I3, inp([2, 5, 7], [3])], [2, 5, 7])
+case("gemv zero", B + ":399-403", ["matvec", inp([[0, 0, 0], [0, 0, 0]], [2, 3]), inp([9, 9, 9], [3])], [0, 0])
+case("gemv (1,N) row", B + ":405-411", ["matvec", inp([[1, 2, 3, 4]], [1, 4]), inp([1, 2, 3, 4], [4])], [30])
+case("gemv transposed matrix", B + ":413-421", ["matvec", ["transpose", inp([[1, 2], [3, 4]], [2, 2]), None],
+                                                 inp([1, 0], [2])], [1, 2])
+case("dot orthogonal", B + ":438-442", ["dot", inp([1, 0, 0], [3]), inp([0, 1, 0], [3])], 0, shape=[])
+case("dot squared norm", B + ":444-448", ["dot", inp([3, 4], [2]), inp([3, 4], [2])], 25, shape=[])
+case("dot single element", B + ":450-454", ["dot", inp([3], [1]), inp([4], [1])], 12, shape=[])
+case("dot f32", B + ":456-462", ["dot", inp([1, 2, 3], [3], "f32"), inp([4, 5, 6], [3], "f32")], 32, shape=[],
+     dtype="f32", tol=1e-4)
+case("strided gemm G x B^T", B + ":1066-1075",
+     ["matmul", inp([[1, 2], [4, 5]], [2, 2]), ["transpose", inp([[1, 0], [0, 1], [1, 1]], [3, 2]), None]],
+     [[1, 2, 3], [4, 5, 9]])
+case("strided gemm A^T x G", B + ":1077-1087",
+     ["matmul", ["transpose", src32, None], inp([[1, 0, 1], [0, 1, 0], [1, 1, 0]], [3, 3])], [[6, 8, 1], [8, 10, 2]])
 conv_in = inp(list(range(1, 17)), [1, 4, 4])
 w1 = inp([1.0] * 9, [1, 1, 3, 3])
 case("conv2d non-batched values", B + ":914-921",
