@@ -214,6 +214,44 @@ case("attention batched rank 3", AT + ":290-315",
      ["attention", inp(Q3 + Q3, [2, 3, 4]), inp(K3 + K3, [2, 3, 4]), inp(V3 + V3, [2, 3, 4]), None], exp3 + exp3,
      shape=[2, 3, 4], tol=1e-10)
 
+case("attention explicit scale 1/sqrt(dk)", AT + ":366-376",
+     ["attention", inp(Q3, [3, 4]), inp(K3, [3, 4]), inp(V3, [3, 4]), 0.5], exp3, shape=[3, 4], tol=1e-10)
+# matmul(A, transpose(B)) through the zero-copy view equals the explicit
+# transpose: the product Q3 K3^T written out
+QKt = [sum(Q3[i * 4 + j] * K3[k * 4 + j] for j in range(4)) for i in range(3) for k in range(3)]
+case("matmul with a transposed view operand", AT + ":335-364",
+     ["matmul", inp(Q3, [3, 4]), ["transpose", inp(K3, [3, 4]), [1, 0]]], QKt, shape=[3, 3], tol=1e-12)
+Q8 = [0.5, -0.3, 1.2, 0.8, 0.1, 0.9, -0.4, 0.6, -0.7, 0.2, 0.5, -0.9, 1.1, -0.5, 0.3, 0.4,
+      -0.2, 0.8, -0.6, 1.0, 0.6, 0.1, 0.9, -0.3, -0.8, 0.4, -0.1, 0.7, 0.3, -0.9, 0.6, 0.2]
+K8 = [0.4, -0.1, 0.8, 0.3, 0.7, 0.5, -0.2, 0.9, -0.3, 1.0, 0.4, -0.6, 0.2, 0.6, 0.1, 0.5,
+      -0.9, 0.3, 0.7, 0.1, 0.5, -0.7, 0.2, 0.8, 0.1, 0.4, -0.5, 0.6, -0.4, 0.8, 0.3, -0.2]
+V8 = [0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8,
+      0.9, 1.0, 0.1, 0.2, 0.3, 0.4, 0.5, 0.6, 0.7, 0.8, 0.9, 1.0, 0.1, 0.3, 0.5, 0.7, 0.9, 0.2,
+      0.4, 0.6, 0.8, 1.0, 0.2, 0.4, 0.6, 0.8, 1.0, 0.2, 0.4, 0.6]
+case("attention n=8 dk=4 dv=6 cross-validation", AT + ":381-427",
+     ["attention", inp(Q8, [8, 4]), inp(K8, [8, 4]), inp(V8, [8, 6]), None],
+     ref_attention(Q8, K8, V8, 8, 4, 6, 0.5), shape=[8, 6], tol=1e-10)
+
+# tests/test-im2col.scm: buffer sizes and shapes, the one stated value set,
+# and im2col of a stacked batch
+IC = "tests/test-im2col.scm"
+img33 = inp([[[1, 2, 3], [4, 5, 6], [7, 8, 9]]], [1, 3, 3])
+case("im2col 3x3 k2 s1 shape", IC + ":42-53", ["im2col", img33, [2, 2], 1, 0], shape=[4, 4])
+case("im2col 4x4 ones k2 s2", IC + ":55-65", ["im2col", inp([1.0] * 16, [1, 4, 4]), [2, 2], 2, 0], [[1.0] * 4] * 4,
+     shape=[4, 4])
+case("im2col 2x2 k2 s1 p1 shape", IC + ":67-79", ["im2col", inp([[[1, 2], [3, 4]]], [1, 2, 2]), [2, 2], 1, 1],
+     shape=[4, 9])
+case("im2col 2 channels ones", IC + ":81-94", ["im2col", inp([1.0] * 18, [2, 3, 3]), [2, 2], 1, 0], [[1.0] * 4] * 8,
+     shape=[8, 4])
+case("im2col batched shape (2,1,3,3)", IC + ":111-119", ["im2col", inp([1.0] * 18, [2, 1, 3, 3]), [2, 2], 1, 0],
+     shape=[2, 4, 4])
+case("im2col 5x5 k3 s2 shape", IC + ":121-130", ["im2col", inp([1.0] * 25, [1, 5, 5]), [3, 3], 2, 0], shape=[9, 4])
+case("im2col 2x2 window values", IC + ":150-162", ["im2col", inp([[[1, 2], [3, 4]]], [1, 2, 2]), [2, 2], 1, 0],
+     [[1], [2], [3], [4]], shape=[4, 1])
+case("im2col of a stacked batch", IC + ":222-241",
+     ["im2col", ["stack", [img33, inp([[[9, 8, 7], [6, 5, 4], [3, 2, 1]]], [1, 3, 3])], 0], [2, 2], 1, 0],
+     shape=[2, 4, 4])
+
 out = Path(__file__).resolve().parent / "known_answers.json"
 out.write_text(json.dumps({"generator": "tests/golden/make_known_answers.py", "cases": cases}, indent=1))
 print(f"wrote {len(cases)} cases to {out}")

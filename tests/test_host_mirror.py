@@ -71,3 +71,16 @@ def test_attention_default_scale():
     q = m([0.0] * 12, (3, 4))
     att = am.attention_morphism(q, q, q)
     assert att.meta["scale"] == 0.5 and att.shape == (3, 4)
+
+
+def test_attention_constructor():
+    """test-attention.scm:151-196: output (n, dv) from V, dtype, scale in the
+    metadata, and the shape errors."""
+    q = m([0.0] * 12, (3, 4))
+    assert am.attention_morphism(q, q, m([0.0] * 18, (3, 6))).shape == (3, 6)
+    assert am.attention_morphism(q, q, q).dtype == "f64"
+    assert am.attention_morphism(q, q, q, 0.25).meta["scale"] == 0.25
+    with pytest.raises(ValueError):
+        am.attention_morphism(q, m([0.0] * 15, (3, 5)), q)
+    with pytest.raises(ValueError):
+        am.attention_morphism(q, q, m([0.0] * 8, (2, 4)))
