@@ -252,6 +252,32 @@ case("im2col of a stacked batch", IC + ":222-241",
      ["im2col", ["stack", [img33, inp([[[9, 8, 7], [6, 5, 4], [3, 2, 1]]], [1, 3, 3])], 0], [2, 2], 1, 0],
      shape=[2, 4, 4])
 
+# test-realization.scm: the stack kernel groups and the integration and
+# performance groups that state values or shapes
+img_b = inp([[[9, 8, 7], [6, 5, 4], [3, 2, 1]]], [1, 3, 3])
+case("stack two 1D arrays", R + ":460-468", ["stack", [inp([1, 2, 3], [3]), inp([4, 5, 6], [3])], 0],
+     [[1, 2, 3], [4, 5, 6]], shape=[2, 3])
+case("stack two 2D arrays", R + ":470-477", ["stack", [inp([[1, 2], [3, 4]], [2, 2]), inp([[5, 6], [7, 8]], [2, 2])], 0],
+     [[[1, 2], [3, 4]], [[5, 6], [7, 8]]], shape=[2, 2, 2])
+case("stack 3D images", R + ":489-496", ["stack", [img33, img_b], 0],
+     [[[[1, 2, 3], [4, 5, 6], [7, 8, 9]]], [[[9, 8, 7], [6, 5, 4], [3, 2, 1]]]], shape=[2, 1, 3, 3])
+case("col2im of im2col of a stacked batch", R + ":509-517",
+     ["col2im", ["im2col", ["stack", [img33, img_b], 0], [2, 2], 1, 0], [2, 1, 3, 3], [2, 2], 1, 0], shape=[2, 1, 3, 3])
+case("stacked matches direct batch", R + ":519-535",
+     ["stack", [inp([[[1, 2], [3, 4]]], [1, 2, 2]), inp([[[5, 6], [7, 8]]], [1, 2, 2])], 0],
+     [[[[1, 2], [3, 4]]], [[[5, 6], [7, 8]]]], shape=[2, 1, 2, 2])
+case("stack single array", R + ":539-544", ["stack", [inp([1, 2, 3], [3])], 0], [[1, 2, 3]], shape=[1, 3])
+case("stack promotes f32 and f64", R + ":546-554", ["stack", [inp([1, 2], [2], "f32"), inp([3, 4], [2])], 0],
+     [[1, 2], [3, 4]], dtype="f64")
+case("realize large array", R + ":641-646", ["mul", inp([1.0] * 10000, [10000]), inp([2.0], [1])], [2.0] * 10000)
+deep = inp([1.0] * 100, [100])
+for _ in range(10):
+    deep = ["add", deep, inp([0.1], [1])]
+acc = 1.0
+for _ in range(10):
+    acc = acc + 0.1
+case("realize deep operation chain", R + ":648-655", deep, [acc] * 100)
+
 out = Path(__file__).resolve().parent / "known_answers.json"
 out.write_text(json.dumps({"generator": "tests/golden/make_known_answers.py", "cases": cases}, indent=1))
 print(f"wrote {len(cases)} cases to {out}")
