@@ -278,6 +278,17 @@ for _ in range(10):
     acc = acc + 0.1
 case("realize deep operation chain", R + ":648-655", deep, [acc] * 100)
 
+# examples/example-08-polyphase-filter-bank.scm: the M=4 polyphase branches
+# of x[n] = n as strided slices, a nested stride-2 decimation, and the 4-tap
+# average of branch 0
+E8 = "examples/example-08-polyphase-filter-bank.scm"
+x16 = inp([float(v) for v in range(16)], [16])
+for mm in range(4):
+    case(f"polyphase branch {mm}", E8 + ":46-49", ["slice", x16, [mm], [16], 4], [float(mm + 4 * k) for k in range(4)])
+case("polyphase nested decimation", E8 + ":54", ["slice", ["slice", x16, [0], [16], 4], [0], [4], 2], [0.0, 8.0])
+case("polyphase 4-tap average", E8 + ":75-76",
+     ["reduce", "sum", ["mul", ["slice", x16, [0], [16], 4], inp([0.25] * 4, [4])], [], False], 6.0, shape=[])
+
 out = Path(__file__).resolve().parent / "known_answers.json"
 out.write_text(json.dumps({"generator": "tests/golden/make_known_answers.py", "cases": cases}, indent=1))
 print(f"wrote {len(cases)} cases to {out}")

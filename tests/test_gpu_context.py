@@ -126,3 +126,21 @@ def test_mixed_dtypes(amc):                                     # test-context.s
     r32, r64 = amc.realize_ctx(c32, b32), amc.realize_ctx(c64, b64)
     assert r32.dtype == "f32" and r32.values().tolist() == [2.0, 4.0]
     assert r64.dtype == "f64" and r64.values().tolist() == [2.0, 4.0]
+
+
+def test_example8_polyphase_allocations(amc):
+    """examples/example-08-polyphase-filter-bank.scm:57-83: the four strided
+    branches and a nested decimation allocate nothing under a context; the
+    4-tap average allocates its result only (the reference's product and
+    reduction nodes, 2 allocations, are one fused launch here)."""
+    x = amc.morph_from_list([float(v) for v in range(16)], (16,))
+    branches = [amc.morph_slice(x, [mm], [16], 4) for mm in range(4)]
+    dec = amc.morph_slice(branches[0], [0], [4], 2)
+    ctx = amc.make_morphism_context()
+    for b in branches + [dec]:
+        amc.realize_ctx(ctx, b)
+    assert stats(amc, ctx)["allocations"] == 0
+    filt = amc.morph_reduce("sum", amc.morph_mul(branches[0], amc.morph_from_list([0.25] * 4, (4,))))
+    ctx2 = amc.make_morphism_context()
+    r = amc.realize_ctx(ctx2, filt)
+    assert stats(amc, ctx2)["allocations"] == 1 and float(r.values()) == 6.0
