@@ -289,6 +289,29 @@ case("polyphase nested decimation", E8 + ":54", ["slice", ["slice", x16, [0], [1
 case("polyphase 4-tap average", E8 + ":75-76",
      ["reduce", "sum", ["mul", ["slice", x16, [0], [16], 4], inp([0.25] * 4, [4])], [], False], 6.0, shape=[])
 
+# examples/example-05-reshape-after-slice.scm: reshape of a stride-2 slice
+# reads it in logical order; rows of the reshaped view are x[0], x[2] and
+# x[4], x[6]
+E5 = "examples/example-05-reshape-after-slice.scm"
+x8 = inp([float(v) for v in range(8)], [8])
+ds = ["slice", x8, [0], [8], 2]
+case("reshape of a strided slice to (2,2)", E5 + ":34-38", ["reshape", ds, [2, 2]], [[0.0, 2.0], [4.0, 6.0]])
+case("reshape of a strided slice to (1,4)", E5 + ":34-39", ["reshape", ds, [1, 4]], [[0.0, 2.0, 4.0, 6.0]])
+case("row 0 of the reshaped slice", E5 + ":56-59", ["slice", ["reshape", ds, [2, 2]], [0, 0], [1, 2], None],
+     [[0.0, 2.0]])
+case("row 1 of the reshaped slice", E5 + ":57-61", ["slice", ["reshape", ds, [2, 2]], [1, 0], [2, 2], None],
+     [[4.0, 6.0]])
+
+# examples/example-04-cross-boundary-fusion.scm: 7 windows of 8 samples,
+# hop 4, of x[n] = n by im2col, transposed and weighted by a rectangular window
+E4 = "examples/example-04-cross-boundary-fusion.scm"
+x32 = ["reshape", inp([float(v) for v in range(32)], [32]), [1, 1, 32]]
+win = ["transpose", ["im2col", x32, [1, 8], [1, 4], 0], None]
+case("windowed analysis window matrix", E4 + ":40-51", win, [[float(4 * k + j) for j in range(8)] for k in range(7)],
+     shape=[7, 8])
+case("windowed analysis rectangular window", E4 + ":64-82", ["mul", win, inp([1.0] * 8, [1, 8])],
+     [[float(4 * k + j) for j in range(8)] for k in range(7)], shape=[7, 8])
+
 out = Path(__file__).resolve().parent / "known_answers.json"
 out.write_text(json.dumps({"generator": "tests/golden/make_known_answers.py", "cases": cases}, indent=1))
 print(f"wrote {len(cases)} cases to {out}")
