@@ -312,6 +312,38 @@ case("windowed analysis window matrix", E4 + ":40-51", win, [[float(4 * k + j) f
 case("windowed analysis rectangular window", E4 + ":64-82", ["mul", win, inp([1.0] * 8, [1, 8])],
      [[float(4 * k + j) for j in range(8)] for k in range(7)], shape=[7, 8])
 
+# tests/test-col2im.scm groups 2-6: col2im(im2col(x)) scales each pixel by
+# the number of windows covering it (corners once, edges twice, the centre
+# of a 3x3 image four times with a 2x2 kernel, stride 1), the pattern the
+# tests state; shapes where they state only shapes
+cover33 = [[1, 2, 1], [2, 4, 2], [1, 2, 1]]
+imgA = [[1, 2, 3], [4, 5, 6], [7, 8, 9]]
+imgB = [[9, 8, 7], [6, 5, 4], [3, 2, 1]]
+times = lambda im: [[im[i][j] * cover33[i][j] for j in range(3)] for i in range(3)]
+case("col2im accumulates overlapping windows", C2 + ":90-112",
+     ["col2im", ["im2col", img33, [2, 2], 1, 0], [1, 3, 3], [2, 2], 1, 0], [times(imgA)], shape=[1, 3, 3])
+case("col2im single window of ones", C2 + ":114-129",
+     ["col2im", ["im2col", inp([[[1, 1], [1, 1]]], [1, 2, 2]), [2, 2], 1, 0], [1, 2, 2], [2, 2], 1, 0],
+     [[[1, 1], [1, 1]]])
+case("col2im with padding shape", C2 + ":134-146",
+     ["col2im", ["im2col", inp([[[1, 2], [3, 4]]], [1, 2, 2]), [2, 2], 1, 1], [1, 2, 2], [2, 2], 1, 1],
+     shape=[1, 2, 2])
+case("col2im batched matches per-image", C2 + ":211-244",
+     ["col2im", ["im2col", ["stack", [img33, img_b], 0], [2, 2], 1, 0], [2, 1, 3, 3], [2, 2], 1, 0],
+     [[times(imgA)], [times(imgB)]], shape=[2, 1, 3, 3])
+case("col2im batched shape", C2 + ":198-209",
+     ["col2im", ["im2col", inp([1.0] * 72, [2, 2, 6, 3]), [2, 2], 1, 0], [2, 2, 6, 3], [2, 2], 1, 0],
+     shape=[2, 2, 6, 3])
+case("col2im adjoint of ones", C2 + ":251-270", ["col2im", inp([1.0] * 32, [8, 4]), [2, 3, 3], [2, 2], 1, 0],
+     [cover33, cover33], shape=[2, 3, 3])
+case("col2im gradient of twos", C2 + ":272-290", ["col2im", inp([2.0] * 16, [4, 4]), [1, 3, 3], [2, 2], 1, 0],
+     [[[2 * c for c in row] for row in cover33]], shape=[1, 3, 3])
+case("col2im large kernel", C2 + ":305-314",
+     ["col2im", ["im2col", inp([1.0] * 25, [1, 5, 5]), [5, 5], 1, 0], [1, 5, 5], [5, 5], 1, 0], [[[1.0] * 5] * 5])
+case("col2im asymmetric kernel and stride shape", C2 + ":316-324",
+     ["col2im", ["im2col", inp([1.0] * 12, [1, 3, 4]), [2, 3], [1, 2], 0], [1, 3, 4], [2, 3], [1, 2], 0],
+     shape=[1, 3, 4])
+
 out = Path(__file__).resolve().parent / "known_answers.json"
 out.write_text(json.dumps({"generator": "tests/golden/make_known_answers.py", "cases": cases}, indent=1))
 print(f"wrote {len(cases)} cases to {out}")
