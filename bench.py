@@ -3,7 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl amcuda|reference]
                     [--workload filterbank|fused|linreg|attention|conv]
 
-Default workload: the polyphase filter bank realized
+Default workload: the polyphase filter bank (config 2 of the five) realized
 through the public API: 64 signals of 2^24 f32 samples per GPU, 64 branches x
 16 taps, the im2col -> reshape -> transpose -> product -> tap-sum tree.  One
 step = one realize of that tree on device-resident inputs.  Multi-GPU runs one
