@@ -915,8 +915,8 @@ static bool prog_int_only(const ReduceArgs& a) {
   return true;
 }
 
-constexpr int kStOT = 8;          // outputs per CTA
-constexpr int kStSC = 96;         // reduced positions per sub-chunk (static shared memory < 48 KB)
+constexpr int kStOT = 4;          // outputs per CTA (4 f64 = one 32-byte sector)
+constexpr int kStSC = 192;        // reduced positions per sub-chunk (static shared memory < 48 KB)
 constexpr int kStWorkers = 224;   // warps 1-7 copy and evaluate; warp 0 folds
 
 template <int MODE, int V>
