@@ -260,12 +260,117 @@ def cpu_other(wl: str, dtype: str):
     return None
 
 
+def _oracle_other_sample(job):
+    """One bounded unit of a non-default workload through the oracle port of
+    the reference's CPU path: the whole config-1 tree, 2^15 rows of one
+    linear-regression step, one (batch, head) attention block forward and
+    backward, or one conv image's three passes.  Returns (seconds, work) with
+    work in the GPU arm's unit (bytes or FLOPs)."""
+    wl, dtype = job
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import numpy as np
+    import oracle
+    from amcuda import morph as M
+    from amcuda import workloads as W
+    oracle.lib()
+    if wl == "fused":
+        xm, ym = W.c1_inputs_morph(dtype)
+        tree = W.c1_tree(xm, ym)
+        run, work = (lambda: oracle.realize(tree)), (2 * (1 << 19) + 1024) * (8 if dtype == "f64" else 4)
+    elif wl == "linreg":
+        rows, d = 1 << 15, 256
+        X, y, _ = W.c5_inputs(rows, d)
+        run, work = (lambda: oracle.linreg(X, y, np.zeros(d), 1, 0.1)), rows * (d + 1) * 8
+    elif wl == "attention":
+        n, dh = 2048, 64
+        q, k, v, do = (W.normal(W.seed_of(4, j), n * dh).astype(np.float32).reshape(1, n, dh) for j in range(4))
+        tree = M.attention_morphism(M.morph_from_numpy(q), M.morph_from_numpy(k), M.morph_from_numpy(v), 0.125)
+
+        def run():
+            oracle.realize(tree)
+            oracle.attention_bwd(q, k, v, do, 0.125)
+        work = 12.0 * n * n * dh
+    else:
+        x = W.normal(W.seed_of(3, 0), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
+        w = (W.normal(W.seed_of(3, 1), 64 * 64 * 9) * np.sqrt(2 / 576)).astype(np.float32).reshape(64, 64, 3, 3)
+        dy = W.normal(W.seed_of(3, 2), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
+
+        def run():
+            oracle.conv2d_fwd(x, w)
+            oracle.conv2d_dgrad(dy, w, x.shape)
+            oracle.conv2d_wgrad(x, dy, w.shape)
+        work = 3 * 2.0 * 64 * 64 * 9 * 56 * 56
+    t0 = time.perf_counter()
+    run()
+    return time.perf_counter() - t0, work
+
+
+_OTHER_ARM = {
+    "fused": ("GB/s", 1e9, "the whole config-1 tree ({dtype}) per process per step"),
+    "linreg": ("GB/s", 1e9, "2^15 of the 2^22 rows of one step per process per step"),
+    "attention": ("TFLOP/s", 1e12, "1 of the 256 (batch, head) blocks, forward and backward, per process per step"),
+    "conv": ("TFLOP/s", 1e12, "1 of the 64 images, three passes, per process per step"),
+}
+_OTHER_METRIC = {
+    "fused": "fused view+map+reduce realize GB/s ({dtype})",
+    "linreg": "linear-regression step (fused pass over X) GB/s",
+    "attention": "attention forward + backward TFLOP/s",
+    "conv": "conv2d forward + data gradient + weight gradient TFLOP/s",
+}
+
+
+def other_config(wl: str, args) -> dict:
+    """The `config` of a non-default workload's bench line (both arms)."""
+    if wl == "fused":
+        return {"workload": f"config 1: x,y 2^20 {args.dtype}, reshape 1024x1024, transpose, slice step 2, "
+                            f"sum(x^2+y) over axis 1", "l2": "256 MB flush between steps"}
+    if wl == "linreg":
+        return {"workload": f"config 5: X {args.rows} x 256 f64 per GPU, MSE gradient step, lr 0.1",
+                "l2": "X larger than L2"}
+    if wl == "attention":
+        return {"workload": f"config 4: Q,K,V,dO ({args.batch or 16},16,2048,64) f32, scale 1/8; O, dQ, dK, dV per step",
+                "flops": "algorithmic 12*B*H*S^2*D (6 GEMMs; the backward recomputes S and dP twice more)"}
+    return {"workload": f"config 3: x ({args.batch or 64},64,56,56) f32, w (64,64,3,3), stride 1 pad 1; "
+                        f"Y, dX and dW per step"}
+
+
+def reference_arm_other(args, cores):
+    """The reference arm of the non-default workloads: the oracle port on
+    every host core (one spawned process per core, each running the bounded
+    unit above), whole-job work over the wall time of each step."""
+    wl = args.workload
+    unit, scale, what = _OTHER_ARM[wl]
+    dtype = args.dtype if wl == "fused" else ("f64" if wl == "linreg" else "f32")
+    jobs = [(wl, args.dtype)] * cores
+    times, vals = [], []
+    with mp.get_context("spawn").Pool(cores) as pool:
+        for i in range(args.warmup + args.steps):
+            res = pool.map(_oracle_other_sample, jobs)
+            # the processes run their units side by side: the step takes the
+            # longest one (input generation and process start-up excluded)
+            dt = max(r[0] for r in res)
+            if i >= args.warmup:
+                times.append(dt)
+                vals.append(sum(r[1] for r in res) / dt / scale)
+    value = sum(vals) / len(vals)
+    sample = (what.format(dtype=args.dtype) + f", {cores} spawned processes running side by side, step time = the "
+              f"longest process, oracle port of the reference's CPU path")
+    print(json.dumps({
+        "impl": "reference", "metric": _OTHER_METRIC[wl].format(dtype=args.dtype), "value": value, "unit": unit,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
+        "config": other_config(wl, args),
+        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
 def reference_arm(args, ws, rank):
     if rank != 0:
         return
     cores = os.cpu_count() or 1
     if args.workload != "filterbank":
-        print(json.dumps({"impl": "reference", "unavailable": "reference arm is defined for the default workload"}))
+        reference_arm_other(args, cores)
         return
     length = 1 << 20
     signals = cores
@@ -494,8 +599,7 @@ def bench_other(args, ws, rank, local):
         unit, bound, metric = "GB/s", "hbm", f"fused view+map+reduce realize GB/s ({args.dtype})"
         flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
         pre = lambda: flush.fill_(1)
-        cfg = {"workload": f"config 1: x,y 2^20 {args.dtype}, reshape 1024x1024, transpose, slice step 2, "
-                           f"sum(x^2+y) over axis 1", "l2": "256 MB flush between steps"}
+        cfg = other_config(wl, args)
         launches = plan.stats()["launches"]
     elif wl == "linreg":
         n, d = args.rows, 256
@@ -517,8 +621,7 @@ def bench_other(args, ws, rank, local):
         work = n * d * 8 + n * 8
         unit, bound, metric = "GB/s", "hbm", "linear-regression step (fused pass over X) GB/s"
         pre = lambda: None
-        cfg = {"workload": f"config 5: X {n} x 256 f64 per GPU, MSE gradient step, lr 0.1",
-               "l2": "X larger than L2"}
+        cfg = other_config(wl, args)
         launches = 3
     elif wl == "attention":
         B, H, S, D = args.batch or 16, 16, 2048, 64
@@ -536,8 +639,7 @@ def bench_other(args, ws, rank, local):
         work = 12.0 * B * H * S * S * D
         unit, bound, metric = "TFLOP/s", "tensor", "attention forward + backward TFLOP/s"
         pre = lambda: None
-        cfg = {"workload": f"config 4: Q,K,V,dO ({B},16,2048,64) f32, scale 1/8; O, dQ, dK, dV per step",
-               "flops": "algorithmic 12*B*H*S^2*D (6 GEMMs; the backward recomputes S and dP twice more)"}
+        cfg = other_config(wl, args)
         launches = 6   # forward: V^T, K rounding, kernel; backward: pre-pass, dK/dV, dQ
     elif wl == "conv":
         N = args.batch or 64
@@ -558,7 +660,7 @@ def bench_other(args, ws, rank, local):
         work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
         unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward + data gradient + weight gradient TFLOP/s"
         pre = lambda: None
-        cfg = {"workload": f"config 3: x ({N},64,56,56) f32, w (64,64,3,3), stride 1 pad 1; Y, dX and dW per step"}
+        cfg = other_config(wl, args)
         launches = 6   # 2 x (weights, kernel) + weight-gradient kernel + reduce
     else:
         raise SystemExit(f"unknown workload {wl}")
