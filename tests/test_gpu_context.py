@@ -144,3 +144,19 @@ def test_example8_polyphase_allocations(amc):
     ctx2 = amc.make_morphism_context()
     r = amc.realize_ctx(ctx2, filt)
     assert stats(amc, ctx2)["allocations"] == 1 and float(r.values()) == 6.0
+
+
+def test_blas_in_context(amc):
+    """test-batch-ops.scm:387-445: matmul, a batched matmul with a shared
+    weight and matvec traced and replayed in a context, equal to realize."""
+    A = ml(amc, [[1, 2], [3, 4]], [2, 2])
+    B = ml(amc, [[5, 6], [7, 8]], [2, 2])
+    A3 = amc.stack_into_batch([ml(amc, [[1, 2], [3, 4]], [2, 2]), ml(amc, [[5, 6], [7, 8]], [2, 2])])
+    for tree in (amc.morph_matmul(A, B), amc.morph_batch_matmul(A3, ml(amc, [[1, 0], [0, 1]], [2, 2])),
+                 amc.morph_matvec(ml(amc, [[1, 2, 3], [4, 5, 6]], [2, 3]), ml(amc, [1, 2, 3], [3]))):
+        ctx = amc.make_morphism_context()
+        trace = np.asarray(amc.realize_ctx(ctx, tree).values())
+        assert np.array_equal(trace, np.asarray(oracle.values(tree)))
+        amc.finalize_context(ctx)
+        amc.reset_context(ctx)
+        assert np.array_equal(np.asarray(amc.realize_ctx(ctx, tree).values()), trace)
