@@ -368,7 +368,7 @@ def reference_arm_other(args, cores):
 def reference_arm(args, ws, rank):
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
+    cores = args.ref_procs or os.cpu_count() or 1
     if args.workload != "filterbank":
         reference_arm_other(args, cores)
         return
@@ -726,6 +726,8 @@ def main():
     ap.add_argument("--dtype", default="f64")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--ref-procs", type=int, default=None,
+                    help="processes of the reference arm (default: one per host core)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl != "reference" else args.warmup
     ws, rank, local = dist_setup(args)

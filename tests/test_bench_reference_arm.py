@@ -16,10 +16,10 @@ KEYS = {"impl", "metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_
 @pytest.mark.parametrize("workload", ["fused", "linreg"])
 def test_reference_arm_line(workload):
     out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--workload", workload, "--steps", "1",
-                          "--warmup", "1"], cwd=ROOT, capture_output=True, text=True, timeout=600)
+                          "--warmup", "1", "--ref-procs", "2"], cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stderr[-2000:]
     line = json.loads(out.stdout.strip().splitlines()[-1])
     assert KEYS <= set(line) and line["impl"] == "reference" and line["value"] > 0
-    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] == 2
     assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
     assert line["unit"] == "GB/s" and line["config"]["workload"].startswith("config")
