@@ -26,8 +26,8 @@ from .grad import (Var, accumulate_grad, backward, make_var, topo_sort, var_abs,
                    var_div, var_exp, var_grad, var_grad_fn, var_log, var_matmul, var_mean, var_mul, var_name,
                    var_negate, var_parents, var_pow, var_relu, var_requires_grad, var_reshape, var_sigmoid,
                    var_sin, var_sqrt, var_sub, var_sum, var_tanh, var_transpose, var_value, zero_grad)
-from .ssa import (morphism_to_ssa, ssa_constant_id, ssa_loss_binding_val, ssa_realize, ssa_realize_ctx,  # noqa: E402
-                  ssa_vjp)
+from .ssa import (morphism_to_ssa, ssa_constant_id, ssa_element_wise_fusion_pass, ssa_loss_binding_val,  # noqa: E402
+                  ssa_realize, ssa_realize_ctx, ssa_vjp)
 from .realize import DeviceBuffer, Plan, force_morphism, init, morph_to_list, realize, to_numpy  # noqa: E402
 from .context import (MorphismContext, context_stats, finalize_context, make_morphism_context, plan_ctx,  # noqa: E402
                       realize_ctx, reset_context)

@@ -30,7 +30,8 @@ from .morph import (Concrete, Expr, Morphism, morph_add, morph_cos, morph_div, m
 
 __all__ = [
     "ConstRef", "BindingRef", "SSABinding", "SSAProgram", "morphism_to_ssa", "ssa_constant_id",
-    "ssa_loss_binding_val", "ssa_vjp", "rebuild_morphism", "ssa_realize", "ssa_realize_ctx",
+    "ssa_loss_binding_val", "ssa_vjp", "ssa_element_wise_fusion_pass", "rebuild_morphism", "ssa_realize",
+    "ssa_realize_ctx",
 ]
 
 _ids = itertools.count()
@@ -322,6 +323,92 @@ def ssa_vjp(fwd: SSAProgram, param_vals: list, loss_val) -> SSAProgram:
     loss_out = emit("add", [loss_val, zero], loss_b.shape, loss_b.dtype, lambda v: morph_add(v[0], v[1]))
     grads = [param_grad[_vid(p)] for p in param_vals if _vid(p) in param_grad]
     return SSAProgram(fwd.constants, fwd.morph_to_val, fwd.bindings + bwd, [loss_out] + grads, len(param_vals))
+
+
+# ------------------------------------------------------------------ element-wise fusion pass
+
+class _Shape(Morphism):
+    """An operand stand-in with only shape and dtype: enough for a
+    constructor to give the node's program."""
+
+    def __init__(self, shape, dtype):
+        self.shape, self.dtype, self.batch_axis = tuple(shape), dtype, -1
+
+
+def _binding_program(b: SSABinding, sd: dict):
+    """The element-wise program of a binding (its constructor's `prog`), or
+    None for matmul, reductions and structural bindings."""
+    if b.op in ("matmul", "matvec", "dot", "reshape", "transpose", "slice") or isinstance(b.op, tuple):
+        return None
+    m = b.build([_Shape(*sd[_vid(v)]) for v in b.inputs])
+    return list(m.meta["prog"]) if isinstance(m, Expr) and "prog" in m.meta else None
+
+
+def _depth(prog) -> int:
+    """The deepest stack a postfix program reaches."""
+    from . import _abi as A
+    sp = depth = 0
+    for (op, _, _) in prog:
+        sp += 1 if op in (A.OP["LOAD"], A.OP["CONST"], A.OP["ICONST"]) else (-1 if op >= A.OP["ADD"] else 0)
+        depth = max(depth, sp)
+    return depth
+
+
+def ssa_element_wise_fusion_pass(prog: SSAProgram) -> SSAProgram:
+    """ssa-element-wise-fusion-pass (ssa.scm:372-426): a greedy scan that
+    merges a producer binding into the binding right after it when the
+    producer has one use, is that binding's first input, has its shape,
+    reads only operands of its own shape, and both are element-wise.  The
+    merged binding keeps the consumer's name and computes
+    consumer(producer(...), ...) in double with no rounding of the
+    intermediate (compose-flat-combiners), stored to the consumer's dtype.
+
+    ssa_vjp does not apply this pass: realize already fuses element-wise
+    nodes on the device and rounds each to its dtype, which equals the
+    unfused program; the pass's unrounded composition differs from it only
+    in f32 programs.  A merge is skipped when the result would exceed a map
+    node's 4 operands or program limits."""
+    from . import _abi as A
+    sd: dict = {}
+    for cid, m in prog.constants.items():
+        sd[cid] = (tuple(m.shape), m.dtype)
+    for b in prog.bindings:
+        sd[b.name] = (b.shape, b.dtype)
+    uses: dict = {b.name: 0 for b in prog.bindings}
+    for b in prog.bindings:
+        for v in b.inputs:
+            if isinstance(v, BindingRef) and v.id in uses:
+                uses[v.id] += 1
+    bs, out = list(prog.bindings), []
+    while bs:
+        p = bs.pop(0)
+        if bs:
+            c = bs[0]
+            pp, cp = _binding_program(p, sd), _binding_program(c, sd)
+            ok = (pp is not None and cp is not None and uses.get(p.name) == 1 and c.inputs
+                  and isinstance(c.inputs[0], BindingRef) and c.inputs[0].id == p.name and p.shape == c.shape
+                  and all(sd[_vid(v)][0] == p.shape for v in p.inputs)
+                  and len(p.inputs) + len(c.inputs) - 1 <= A.NODE_MAX_IN)
+            if ok:
+                n_p = len(p.inputs)
+                fused = []
+                for (op, a, imm) in cp:
+                    if op == A.OP["LOAD"] and a == 0:
+                        fused += pp
+                    elif op == A.OP["LOAD"]:
+                        fused.append((op, n_p + a - 1, imm))
+                    else:
+                        fused.append((op, a, imm))
+                if len(fused) <= A.PROG_MAX and _depth(fused) <= A.STACK_MAX:
+                    shape, dtype = c.shape, c.dtype
+                    build = (lambda xs, shape=shape, dtype=dtype, fused=fused:
+                             Expr("map", list(xs), shape, dtype, {"prog": list(fused)}))
+                    merged = SSABinding(c.name, c.op, p.inputs + c.inputs[1:], shape, dtype,
+                                        dict(c.meta, fused=True), build)
+                    bs[0] = merged            # the merged binding may absorb the next one too
+                    continue
+        out.append(p)
+    return SSAProgram(prog.constants, prog.morph_to_val, out, prog.outputs, prog.n_params)
 
 
 # ------------------------------------------------------------------ phase 3: realization

@@ -278,3 +278,41 @@ def test_each_vjp_rule_agrees_with_tree_autograd(name):
         ref = np.asarray(oracle.values(am.var_grad(p)))
         assert np.asarray(got.values()).shape == ref.shape
         np.testing.assert_allclose(np.asarray(got.values()), ref, rtol=1e-12, atol=1e-14, err_msg=name)
+
+
+# ------------------------------------------------------------------ E2: the element-wise fusion pass (test-ssa.scm:810-870)
+
+def test_fusion_pass_binding_counts_and_values():
+    a = ml([-3.0, 2.0], [2])
+    p0 = S.morphism_to_ssa(am.make_var(am.morph_negate(am.morph_abs(a))))
+    p1 = S.ssa_element_wise_fusion_pass(p0)
+    assert len(p0.bindings) - len(p1.bindings) == 1
+    assert flat(S.ssa_realize(p1, oracle.realize)[0]) == [-3.0, -2.0]
+    a = ml([1.0, 2.0], [2])
+    b = am.morph_abs(a)
+    p1 = S.ssa_element_wise_fusion_pass(S.morphism_to_ssa(am.make_var(am.morph_add(b, am.morph_negate(b)))))
+    assert len(p1.bindings) == 3                       # b has two consumers: nothing merges
+    c = am.morph_reduce("sum", am.morph_abs(ml([1.0, -2.0, 3.0, -4.0], [4])), [0])
+    assert len(S.ssa_element_wise_fusion_pass(S.morphism_to_ssa(am.make_var(c))).bindings) == 2
+    xv = am.make_var(ml([1.0, 2.0, 3.0], [3]), True)
+    joint = S.ssa_element_wise_fusion_pass(joint_of(am.var_sum(am.var_negate(xv)), [xv]))
+    assert close(flat(S.ssa_realize(joint, oracle.realize)[1]), [-1.0, -1.0, -1.0])
+
+
+@pytest.mark.parametrize("dt", ["f64", "f32"])
+def test_fusion_pass_composes_without_rounding_the_intermediate(dt):
+    """A merged chain equals the unfused program in f64; in f32 it equals
+    the double-precision composition stored once (compose-flat-combiners)."""
+    rng = np.random.default_rng(12)
+    xs, ys = rng.uniform(0.5, 2.0, 16), rng.uniform(0.5, 2.0, 16)
+    x, y = am.morph_from_numpy(xs, dt), am.morph_from_numpy(ys, dt)
+    tree = am.morph_mul(am.morph_sqrt(am.morph_add(am.morph_exp(x), y)), y)
+    p0 = S.morphism_to_ssa(am.make_var(tree))
+    p1 = S.ssa_element_wise_fusion_pass(p0)
+    assert len(p1.bindings) < len(p0.bindings)
+    got = np.asarray(S.ssa_realize(p1, oracle.realize)[0].values())
+    if dt == "f64":
+        np.testing.assert_array_equal(got, np.asarray(S.ssa_realize(p0, oracle.realize)[0].values()))
+    else:
+        x64, y64 = xs.astype(np.float32).astype(np.float64), ys.astype(np.float32).astype(np.float64)
+        np.testing.assert_allclose(got, (np.sqrt(np.exp(x64) + y64) * y64).astype(np.float32), rtol=2e-7)
