@@ -135,3 +135,19 @@ def test_edge_cases():
     assert final.op == "sqrt"
     np.testing.assert_allclose(oracle.values(final), np.sqrt([2.0, 5.0, 10.0]), rtol=1e-15)
     assert am.morph_mul(ml([[[1, 2]]], (1, 1, 2)), ml([3, 4], (2,))).shape == (1, 1, 2)
+
+
+# ------------------------------------------------------------------ activation forwards (test-ssa.scm:874-915)
+
+def test_activation_forward_values():
+    import math
+    vals = lambda m: list(np.asarray(oracle.values(m), dtype=np.float64))
+    assert vals(am.morph_relu(ml([1.0, 2.0, 3.0], (3,)))) == [1.0, 2.0, 3.0]
+    assert vals(am.morph_relu(ml([-1.0, -2.0, -3.0], (3,)))) == [0.0, 0.0, 0.0]
+    assert vals(am.morph_relu(ml([-1.0, 2.0, -3.0, 4.0], (4,)))) == [0.0, 2.0, 0.0, 4.0]
+    xs = [-2.0, -1.0, 0.0, 1.0, 2.0]
+    np.testing.assert_allclose(vals(am.morph_sigmoid(ml(xs, (5,)))), [1.0 / (1.0 + math.exp(-x)) for x in xs],
+                               rtol=0, atol=1e-9)
+    xs = [-1.0, 0.0, 1.0]
+    np.testing.assert_allclose(vals(am.morph_tanh(ml(xs, (3,)))),
+                               [(math.exp(2 * x) - 1) / (math.exp(2 * x) + 1) for x in xs], rtol=0, atol=1e-9)
