@@ -316,3 +316,23 @@ def test_fusion_pass_composes_without_rounding_the_intermediate(dt):
     else:
         x64, y64 = xs.astype(np.float32).astype(np.float64), ys.astype(np.float32).astype(np.float64)
         np.testing.assert_allclose(got, (np.sqrt(np.exp(x64) + y64) * y64).astype(np.float32), rtol=2e-7)
+
+
+def test_ssa_mse_step_matches_the_linear_regression_oracle():
+    """The C5 program through the SSA compiler: loss = mean((X w - y)^2) and
+    its gradient w.r.t. w (2/N X^T (X w - y)), one gradient-descent step of
+    which is what the fused linear-regression kernels replay.  The SSA
+    gradient and loss agree with the oracle's step to 1e-12."""
+    from amcuda import workloads as W
+    rows, d, lr = 256, 8, 0.1
+    X, y, _ = W.c5_inputs(rows, d)
+    w0 = np.random.default_rng(3).standard_normal(d) * 0.1
+    Xv = am.make_var(am.morph_from_numpy(X))
+    wv = am.make_var(am.morph_from_numpy(w0.reshape(d, 1)), True)
+    yv = am.make_var(am.morph_from_numpy(np.asarray(y).reshape(rows, 1)))
+    r = am.var_sub(am.var_matmul(Xv, wv), yv)
+    res = S.ssa_realize(joint_of(am.var_mean(am.var_mul(r, r)), [wv]), oracle.realize)
+    loss, dw = float(np.asarray(res[0].values()).reshape(-1)[0]), np.asarray(res[1].values()).reshape(-1)
+    w1, losses = oracle.linreg(X, y, w0, 1, lr)
+    np.testing.assert_allclose(loss, losses[0], rtol=1e-12)
+    np.testing.assert_allclose(w0 - lr * dw, w1, rtol=1e-12, atol=1e-15)
