@@ -2,13 +2,14 @@
 
 The lazy-morphism API of the reference (constructors in amcuda.morph,
 realize / realize_ctx) over libamcuda.so, the C-ABI library of hand-written
-sm_100a kernels.  Importing this package loads the library and fails loudly
-when it is missing; there is no CPU fallback.
+sm_100a kernels.  The library is loaded by the first call that needs the
+device (init, realize, a buffer or a workload entry point) and that call
+fails loudly when the library is missing; there is no CPU fallback.
+Building morphism trees needs no library, so host-only users (the oracle,
+the reference arm of the benchmark) never map it.
 """
 from . import _abi
 from ._abi import AmcError
-
-_abi.load()
 
 from .morph import (Concrete, Expr, Morphism, attention_morphism, broadcast_shapes, col2im_morph,  # noqa: E402
                     compute_strides, im2col_morph, infer_reduction_dtype, morph_abs, morph_add, morph_ceiling,

@@ -112,6 +112,7 @@ SIGNATURES = {
     "amc_conv2d_dgrad_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
     "amc_conv2d_wgrad_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
     "amc_tc_peak_tf32": [_I32, _I32, _I32, _I32, _P, _P],
+    "amc_probe_bounded_wait": [_I32, _I32, _P],
 }
 
 _lib = None

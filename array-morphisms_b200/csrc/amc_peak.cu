@@ -21,7 +21,22 @@ namespace {
 // the SM's shared memory so exactly one CTA runs per SM
 constexpr int kPeakSmem = 120 * 1024;
 __device__ int g_peak_error;
+__device__ int g_wait_probe_error;
 }  // namespace
+
+// The bounded mbarrier wait every TMA/tensor-core kernel uses, on its own:
+// one thread initialises a barrier that expects one arrival, arrives on it
+// only when `arrive` is set, and waits with the given poll limit.  With no
+// arrival the wait runs out, the thread records AMC_ERR_TIMEOUT in the flag
+// and the kernel returns, as the production kernels do on expiry.
+__global__ void k_wait_probe(int limit, int arrive) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  mbar_init(&bar, 1);
+  mbar_fence_init();
+  if (arrive) mbar_arrive(&bar);
+  if (!mbar_wait(&bar, 0, limit)) atomicExch(&g_wait_probe_error, AMC_ERR_TIMEOUT);
+}
 
 template <int N, bool ATMEM>
 __global__ void __launch_bounds__(128, 1) k_tc_peak(int iters, int warps) {
@@ -130,5 +145,22 @@ extern "C" int amc_tc_peak_tf32(int32_t n, int32_t warps, int32_t a_tmem, int32_
   }
   const double flops = 2.0 * 128.0 * n * 8.0 * (4.0 * iters + 1.0) * warps * num_sms();
   *tflops = ms > 0.f ? flops / (ms * 1e-3) / 1e12 : 0.0;
+  return AMC_OK;
+}
+
+extern "C" int amc_probe_bounded_wait(int32_t limit, int32_t arrive, void* stream) {
+  if (limit < 1 || limit > (1 << 22) || (arrive != 0 && arrive != 1))
+    return fail(AMC_ERR_INVALID, "amc_probe_bounded_wait: limit 1..2^22, arrive 0|1");
+  cudaStream_t s = pick_stream(stream);
+  k_wait_probe<<<1, 32, 0, s>>>(limit, arrive);
+  AMC_CUDA(cudaGetLastError());
+  AMC_CUDA(cudaStreamSynchronize(s));
+  int err = 0;
+  AMC_CUDA(cudaMemcpyFromSymbol(&err, g_wait_probe_error, sizeof(int)));
+  if (err) {
+    int z = 0;
+    AMC_CUDA(cudaMemcpyToSymbol(g_wait_probe_error, &z, sizeof(int)));
+    return fail(err, "amc_probe_bounded_wait: the wait gave up after " + std::to_string(limit) + " polls");
+  }
   return AMC_OK;
 }

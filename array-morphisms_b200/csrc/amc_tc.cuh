@@ -3,14 +3,24 @@
 // mbarriers, tensor-memory loads, 2-D tiled TMA loads (no multicast), and the
 // shared-memory / instruction descriptors.
 //
-// Shared-memory operand layouts are the canonical 128-byte-swizzled ones:
+// Shared-memory operand layouts are the canonical 128-byte-swizzled ones, in
+// two majornesses:
 //   K-major  : rows of 128 B (32 tf32 along K), 8-row groups 1024 B apart;
-//              a K extent of 64 is two such regions.  desc: SBO = 1024.
-// Every operand here is K-major: with the plain 128-byte swizzle, tf32
-// operands described as MN-major were measured to produce zeros (N=64) or
-// wrong values (N=32), so transposed operands are materialised K-major.
-// TMA writes exactly these layouts with CU_TENSOR_MAP_SWIZZLE_128B and a box
-// whose inner extent is 32 floats; tiles start on 1024-byte boundaries.
+//              a K extent of 64 is two such regions.  sdesc(): SBO = 1024,
+//              layout type 2 (SWIZZLE_128B).  TMA writes it with
+//              CU_TENSOR_MAP_SWIZZLE_128B and a box whose inner extent is 32
+//              floats.  Used by every operand whose contraction runs along
+//              the row of its row-major array (Q, K and the conv tiles).
+//   MN-major : rows of 128 B holding 32 consecutive M/N elements, one row per
+//              K index, 32-byte atoms swizzled within the row, 4-row K groups
+//              512 B apart.  sdesc_mn(): layout type 1
+//              (SWIZZLE_128B_BASE32B).  TMA writes it with
+//              CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.  Used where the
+//              contraction runs down the rows of a row-major array: V in P V,
+//              dO in dV += P^T dO, Q in dK += dS^T Q and K in dQ += dS K.
+// An MN-major tf32 operand described with the plain 128-byte swizzle (layout
+// type 2) reads as zeros (N=64) or wrong values (N=32); only layout type 1
+// works for it.  Tiles start on 1024-byte boundaries.
 #pragma once
 
 #include <cuda.h>

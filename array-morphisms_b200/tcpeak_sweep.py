@@ -1,6 +1,9 @@
 """Print the tcgen05 kind::tf32 issue-rate table of this GPU.
 
-    python -m amcuda.tcpeak        (with array-morphisms_b200 on sys.path)
+    python array-morphisms_b200/tcpeak_sweep.py
+
+A measurement script beside the package, not part of it: bench.py takes its
+TF32 denominator from the same probe entry point directly.
 
 Each row: M=128 x N x K=8 products issued back to back by 1, 2 or 4 threads
 per SM (amc_tc_peak_tf32), B read from shared memory and A from shared memory
@@ -9,6 +12,11 @@ The last column is the shared-memory operand bytes per product over the
 clocks it took: at about 128 B/clock the product is bound by the
 shared-memory read port, not by the pipe."""
 from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent))
 
 
 def main() -> None:

@@ -44,15 +44,6 @@ def peaks():
     return HBM_FALLBACK, 1590.0, "fallback"
 
 
-def profile_traffic(name: str):
-    """traffic bytes per launch recorded in profiles/<name>.md (from ncu)."""
-    f = ROOT / "profiles" / f"{name}.md"
-    if not f.exists():
-        return None
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
-    return float(m.group(1)) if m else None
-
-
 # ---------------------------------------------------------------------------- distributed plumbing
 def dist_setup(args):
     ws = int(os.environ.get("WORLD_SIZE", "1"))
@@ -359,7 +350,7 @@ def reference_arm_other(args, cores):
         "impl": "reference", "metric": _OTHER_METRIC[wl].format(dtype=args.dtype), "value": value, "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-        "config": other_config(wl, args),
+        "config": dict(other_config(wl, args), sample=sample),
         "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -392,7 +383,7 @@ def reference_arm(args, ws, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": CONFIG_FB,
+        "config": dict(CONFIG_FB, sample=sample),
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -467,7 +458,7 @@ def bench_filterbank(args, ws, rank, local):
     hbm, _, kind = peaks()
     mean_step = sum(step_ms) / len(step_ms)
     achieved = bytes_step / (mean_step / 1e3) / 1e9
-    traffic = profile_traffic("window_fir_filterbank")
+    traffic = None
 
     # ---- end to end: pinned host signals -> device -> realize -> host result.
     # Two buffer sets (two plans of the same public tree) and three streams:

@@ -358,6 +358,15 @@ int amc_conv2d_wgrad_f32(const float* X, const float* dY, float* dW, int32_t N, 
  * the stream. */
 int amc_tc_peak_tf32(int32_t n, int32_t warps, int32_t a_tmem, int32_t iters, double* tflops, void* stream);
 
+/* Bounded-wait probe (diagnostic; no reference counterpart): runs the bounded
+ * mbarrier wait of the TMA/tensor-core kernels alone on a tiny launch.  The
+ * barrier expects one arrival, which the kernel makes only when arrive = 1;
+ * the wait polls at most `limit` (1..2^22) times.  Returns AMC_OK when the
+ * barrier completed and AMC_ERR_TIMEOUT when the wait ran out, after the
+ * kernel recorded the timeout and returned (the context stays usable).
+ * Synchronizes the stream. */
+int amc_probe_bounded_wait(int32_t limit, int32_t arrive, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
