@@ -24,7 +24,7 @@ OP = dict(LOAD=1, CONST=2, ICONST=3, CVT=4, NEG=10, ABS=11, FLOOR=12, CEIL=13, S
 RED = dict(sum=0, mean=1, prod=2, max=3, min=4)
 PAD = dict(constant=0, edge=1, reflect=2)
 NODE = dict(LEAF=1, RESHAPE=2, TRANSPOSE=3, SLICE=4, MAP=5, REDUCE=6, PAD=7, IM2COL=8, COL2IM=9, STACK=10,
-            CONCAT=11, MATMUL=12, MATVEC=13, DOT=14, ATTENTION=15, SCAN=16)
+            CONCAT=11, MATMUL=12, MATVEC=13, DOT=14, ATTENTION=15, SCAN=16, OUTPUTS=17)
 PROG_MAX = 64
 STACK_MAX = 16
 NODE_MAX_IN = 4
@@ -72,12 +72,15 @@ SIGNATURES = {
     "amc_buf_download": [_U64, _P, _I64, _I64],
     "amc_buf_upload_async": [_U64, _P, _I64, _I64, _P],
     "amc_buf_download_async": [_U64, _P, _I64, _I64, _P],
+    "amc_buf_copy_async": [_U64, _I64, _U64, _I64, _I64, _P],
     "amc_buf_devptr": [_U64, C.POINTER(_P)],
     "amc_buf_info": [_U64, _PI32, _PI64],
     "amc_buf_free": [_U64],
     "amc_plan_create": [C.POINTER(Node), _I32, _PU64],
     "amc_plan_execute": [_U64, _P],
     "amc_plan_result": [_U64, C.POINTER(View)],
+    "amc_plan_result_count": [_U64, _PI32],
+    "amc_plan_result_at": [_U64, _I32, C.POINTER(View)],
     "amc_plan_stats": [_U64, _PI32, _PI32, _PI64],
     "amc_plan_capture_graph": [_U64, _P],
     "amc_plan_destroy": [_U64],
@@ -86,6 +89,7 @@ SIGNATURES = {
     "amc_ctx_pin_output": [_U64, _U64],
     "amc_ctx_finalize": [_U64],
     "amc_ctx_reset": [_U64],
+    "amc_ctx_replay": [_U64, _U64, _P],
     "amc_ctx_stats": [_U64, _PI32, _PI32, _PI64, _PI32],
     "amc_ctx_destroy": [_U64],
     "amc_colour": [_I32, _PI32, _PI64, _PI32, _PI32, _PI32, _PI32, _PI32],

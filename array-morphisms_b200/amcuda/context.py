@@ -49,6 +49,24 @@ def realize_ctx(ctx: MorphismContext, m: Morphism, pin_output: bool = False) -> 
     return p.result(keep_device=False)
 
 
+def realize_ctx_many(ctx: MorphismContext, ms: list, pin_output: bool = False) -> tuple:
+    """The lazy morphisms of `ms` realized together through the context in
+    one plan (each shared node once); pin_output pins every result while
+    tracing.  Returns (plan, results)."""
+    p = Plan(ms, ctx)
+    p.execute()
+    if pin_output:
+        A.call("amc_ctx_pin_output", ctx.handle, p.handle)
+    return p, p.results(keep_device=False)
+
+
+def replay_plan(ctx: MorphismContext, plan: Plan, stream: int | None = None) -> None:
+    """Run a plan created in the context's replay mode again on its arena
+    buffers, without re-planning (amc_ctx_replay; execute-replay-plan,
+    ssa.scm:1519-1654)."""
+    A.call("amc_ctx_replay", ctx.handle, plan.handle, C.c_void_p(stream or 0))
+
+
 def plan_ctx(ctx: MorphismContext, m: Morphism) -> Plan:
     """A replayable plan bound to the context (for repeated execution or
     CUDA-graph capture without re-planning)."""

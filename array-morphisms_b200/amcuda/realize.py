@@ -131,7 +131,10 @@ _MAP_OPS = {"add", "sub", "mul", "div", "pow", "gt", "lt", "eq", "ge", "le", "ma
             "cos", "tan", "negate", "abs", "floor", "ceiling", "relu", "sigmoid", "tanh"}
 
 
-def serialize(root: Morphism) -> Serialized:
+def serialize(root) -> Serialized:
+    """amc_node records of one tree, or of several roots (a list) realized
+    together: then a final OUTPUTS node lists the roots, and a node shared
+    between them is serialized, planned and computed once."""
     S = Serialized()
 
     def visit(m: Morphism) -> int:
@@ -229,16 +232,32 @@ def serialize(root: Morphism) -> Serialized:
         S.keep.append(m)  # keep the morphism (and its buffers) alive
         return idx
 
-    visit(root)
+    if isinstance(root, (list, tuple)):
+        idx = [visit(r) for r in root]
+        nd = A.Node()
+        nd.kind = A.NODE["OUTPUTS"]
+        nd.n_in = len(idx)
+        if len(idx) <= A.NODE_MAX_IN:
+            for k, i in enumerate(idx):
+                nd.in_[k] = i
+        else:
+            ext = (C.c_int32 * len(idx))(*idx)
+            S.keep.append(ext)
+            nd.in_ext = C.cast(ext, C.POINTER(C.c_int32))
+        S.nodes.append(nd)
+    else:
+        visit(root)
     return S
 
 
 class Plan:
-    """A created device plan for one tree (amc_plan_*)."""
+    """A created device plan (amc_plan_*) for one tree, or for a list of
+    roots realized together (their results in order: results())."""
 
-    def __init__(self, root: Morphism, ctx=None):
+    def __init__(self, root, ctx=None):
         _ensure_init()
-        self.root = root
+        self.roots = list(root) if isinstance(root, (list, tuple)) else [root]
+        self.root = self.roots[0]
         self.S = serialize(root)
         arr = self.S.array()
         h = C.c_uint64(0)
@@ -260,14 +279,21 @@ class Plan:
         A.call("amc_plan_stats", self.handle, C.byref(l), C.byref(b), C.byref(by))
         return {"launches": l.value, "buffers": b.value, "bytes": by.value}
 
-    def result(self, keep_device: bool = True) -> Concrete:
+    def result(self, keep_device: bool = True, index: int = 0, arena: bool = False) -> Concrete:
+        """Result `index` as a Concrete.  Its device buffer is kept (read on
+        the host only when .data is first used) for plans outside a context;
+        a context plan's result is downloaded now, since the next replay
+        writes the same arena memory, unless `arena` asks for the arena
+        buffer itself (valid until the context's next replay writes it, as
+        the reference's pool vectors are)."""
         v = A.View()
-        A.call("amc_plan_result", self.handle, C.byref(v))
+        A.call("amc_plan_result_at", self.handle, index, C.byref(v))
         shape = tuple(v.shape[i] for i in range(v.rank))
         strides = tuple(v.strides[i] for i in range(v.rank))
-        dtype = self.root.dtype
+        root = self.roots[index]
+        dtype = root.dtype
         owner = self.S.leaf_owner.get(v.buf)
-        ba = getattr(self.root, "batch_axis", -1)
+        ba = getattr(root, "batch_axis", -1)
         if owner is not None:
             # zero-copy view of a leaf (create-view): shares the leaf's vector
             A._lib.amc_buf_free(v.buf)
@@ -276,10 +302,13 @@ class Plan:
         nel = C.c_int64()
         A.call("amc_buf_info", v.buf, None, C.byref(nel))
         buf = DeviceBuffer(v.buf, dtype, nel.value)
-        if keep_device and self.ctx is None:
+        if keep_device and (self.ctx is None or arena):
             return Concrete(None, shape, strides, v.offset, dtype, ba, dev=buf)
         data = buf.download()
         return Concrete(data, shape, strides, v.offset, dtype, ba)
+
+    def results(self, keep_device: bool = True, arena: bool = False) -> list:
+        return [self.result(keep_device, i, arena) for i in range(len(self.roots))]
 
     def __del__(self):
         try:
@@ -297,6 +326,18 @@ def realize(m: Morphism) -> Concrete:
     p = Plan(m)
     p.execute()
     return p.result()
+
+
+def realize_many(ms: list) -> list:
+    """The morphisms of `ms` realized together in one plan: a node shared
+    between them is computed once (concrete arrays are returned as-is)."""
+    lazy = [m for m in ms if not isinstance(m, Concrete)]
+    if not lazy:
+        return list(ms)
+    p = Plan(lazy)
+    p.execute()
+    it = iter(p.results())
+    return [m if isinstance(m, Concrete) else next(it) for m in ms]
 
 
 def force_morphism(m: Morphism) -> Concrete:

@@ -12,10 +12,11 @@ element-wise bindings that the reference's psi-composition pass
 since every fused map node is still rounded to its dtype.
 
 Names, program structure and rules follow ssa.scm (file:line on each
-function).  The replay plan of ssa-realize/ctx (ssa.scm:1390-1654) is the
-context's own replay here: realize_ctx in trace mode records the
-allocations, finalize_context colours them into one arena, and later runs
-replay into it.
+function).  The outputs of a program are planned together, so each
+binding runs once.  ssa-realize/ctx traces the program through the context
+(allocations recorded, finalize_context colours them into one arena), then
+compiles the replay plan once against the arena and re-runs it each step
+without re-planning (ssa.scm:1390-1654).
 """
 from __future__ import annotations
 
@@ -435,21 +436,71 @@ def _output_trees(prog: SSAProgram) -> list:
 
 
 def ssa_realize(prog: SSAProgram, realize: Optional[Callable[[Morphism], Concrete]] = None) -> list:
-    """ssa-realize (ssa.scm:1130-1156): the outputs as concrete arrays.  The
-    bindings become one lazy tree per output, realized on the device (or by
-    the `realize` given, e.g. the oracle's)."""
+    """ssa-realize (ssa.scm:1130-1156): the outputs as concrete arrays.  On
+    the device the outputs' trees are planned and run together, so every
+    binding is computed once, as the reference's binding loop computes it
+    (the loss and the gradients share the forward bindings).  A `realize`
+    given (e.g. the oracle's) is applied to each output tree in turn."""
+    trees = _output_trees(prog)
     if realize is None:
-        from .realize import realize
-    return [o if isinstance(o, Concrete) else realize(o) for o in _output_trees(prog)]
+        from .realize import realize_many
+        return realize_many(trees)
+    return [o if isinstance(o, Concrete) else realize(o) for o in trees]
 
 
-def ssa_realize_ctx(ctx, prog: SSAProgram) -> list:
-    """ssa-realize/ctx (ssa.scm:1661-1749): the outputs realized through the
-    morphism context, each output pinned while tracing (context-pin-output!
-    applies in trace mode only, ssa.scm:1716-1717).  In trace mode the
-    context records the allocations; after finalize_context and
-    reset_context, the same call replays into the coloured arena without
-    allocating."""
-    from .context import context_stats, realize_ctx
-    pin = context_stats(ctx)["mode"] == "trace"     # pinning applies while tracing only
-    return [o if isinstance(o, Concrete) else realize_ctx(ctx, o, pin_output=pin) for o in _output_trees(prog)]
+def _const_devs(prog: SSAProgram) -> tuple:
+    """Identity of each constant's device copy: a constant whose host vector
+    was rewritten (host_changed) gets a new device copy, and a replay plan
+    compiled over the old one is stale."""
+    return tuple(id(m._dev) for m in prog.constants.values())
+
+
+def ssa_realize_ctx(ctx, prog: SSAProgram, stream=None) -> list:
+    """ssa-realize/ctx (ssa.scm:1661-1749).
+
+    Trace mode: the outputs are realized together through the context (each
+    binding once), every output pinned (context-pin-output! applies while
+    tracing only, ssa.scm:1716-1717), and returned on the host.
+
+    Replay mode (after finalize_context and reset_context): the first call
+    compiles the replay plan, i.e. plans the program once against the
+    context's arena (compile-replay-plan, ssa.scm:1390-1512); this and every
+    later call runs it without re-planning or allocating
+    (execute-replay-plan, ssa.scm:1519-1654).  The outputs are returned as
+    the arena buffers themselves, as the reference returns its pool vectors:
+    read them before the next replay overwrites them.  A constant rewritten
+    through host_changed() makes the next call compile the plan again.
+    `stream` (a CUDA stream pointer) orders the replay's launches."""
+    from .context import context_stats, realize_ctx_many, replay_plan
+    from .realize import Plan
+    trace = context_stats(ctx)["mode"] == "trace"
+    if trace:
+        trees = _output_trees(prog)
+        lazy = [o for o in trees if not isinstance(o, Concrete)]
+        if not lazy:
+            return trees
+        _, res = realize_ctx_many(ctx, lazy, pin_output=True)
+        it = iter(res)
+        return [o if isinstance(o, Concrete) else next(it) for o in trees]
+    cache = prog.__dict__.setdefault("_replay", {})
+    key = ctx.handle
+    entry = cache.get(key)
+    if entry is not None and entry[2] != _const_devs(prog):
+        entry = None
+    if entry is None:
+        trees = _output_trees(prog)
+        lazy = [o for o in trees if not isinstance(o, Concrete)]
+        plan = Plan(lazy, ctx) if lazy else None
+        if plan is not None:
+            plan.execute(stream)
+        entry = (plan, trees, _const_devs(prog))
+        cache[key] = entry
+    else:
+        plan = entry[0]
+        if plan is not None:
+            replay_plan(ctx, plan, stream)
+    plan, trees = entry[0], entry[1]
+    if plan is None:
+        return list(trees)
+    it = iter(plan.results(arena=True))
+    return [o if isinstance(o, Concrete) else next(it) for o in trees]

@@ -290,3 +290,101 @@ def tc_peak_tf32(iters: int = 4000, n: int = 256, warps: int = 1, a_tmem: bool =
     out = C.c_double(0.0)
     A.call("amc_tc_peak_tf32", n, warps, int(bool(a_tmem)), iters, C.byref(out), _stream(stream))
     return out.value
+
+
+# ---------------------------------------------------------------------------- C5 through the public SSA path
+class LinregSSA:
+    """Config 5 as a user writes it: the MSE loss of a linear model built
+    from variables (grad.scm's var-* constructors), compiled to a joint
+    forward + reverse-mode SSA program (morphism-to-ssa, ssa-vjp) and run by
+    ssa-realize/ctx with buffer reuse: one traced step, finalize, then each
+    step replays the compiled plan in the context's arena and updates the
+    parameter in place, w <- w - lr * dw (the plain gradient step of
+    example-09, realized as a morphism over the gradient's arena buffer).
+
+    X (rows, d) and y (rows, 1) are concrete arrays (host or device
+    resident); w0 is (d,).  On the device the planner runs the program's
+    forward GEMV and gradient GEMV as one pass over X (the GEMV pair of the
+    row-pass kernels).  `grad_hook(dw_concrete)` runs between the replay and
+    the update (a multi-GPU caller sums the gradient over the row shards
+    there).  At most `max_steps` steps are recorded."""
+
+    def __init__(self, X, y, w0, lr: float, stream=None, max_steps: int = 4096, grad_hook=None):
+        from .grad import make_var, var_matmul, var_mean, var_mul, var_sub
+        from .morph import Concrete, morph_from_numpy
+        from .ssa import morphism_to_ssa, ssa_constant_id, ssa_loss_binding_val, ssa_vjp
+        self.X = X if isinstance(X, Concrete) else morph_from_numpy(np.asarray(X, dtype=np.float64))
+        rows, d = self.X.shape
+        self.y = y if isinstance(y, Concrete) else morph_from_numpy(np.asarray(y, dtype=np.float64).reshape(rows, 1))
+        self.rows, self.d, self.lr = rows, d, float(lr)
+        self.w = morph_from_numpy(np.asarray(w0, dtype=np.float64).reshape(d, 1))
+        wv = make_var(self.w, True)
+        r = var_sub(var_matmul(make_var(self.X), wv), make_var(self.y))
+        fwd = morphism_to_ssa(var_mean(var_mul(r, r)))
+        self.prog = ssa_vjp(fwd, [ssa_constant_id(fwd, self.w)], ssa_loss_binding_val(fwd))
+        self.ctx = None
+        self.stream = stream
+        self.max_steps = max_steps
+        self.grad_hook = grad_hook
+        self.steps = 0
+        self._update = None
+        self._losses = None
+        self.trace_stats = None
+
+    def _apply(self, dw, loss) -> None:
+        """w <- w - lr * dw on the device, into w's own buffer, and the
+        step's loss copied into the device-side loss record."""
+        from .morph import morph_from_numpy, morph_mul, morph_sub
+        from .realize import Plan, device_buffer_of
+        if self.steps >= self.max_steps:
+            raise ValueError(f"LinregSSA: more than max_steps={self.max_steps} steps")
+        if self.grad_hook is not None:
+            self.grad_hook(dw)
+        wbuf = device_buffer_of(self.w)
+        if self._update is None:
+            # planned once over the arena buffer of dw, which every replay rewrites
+            self._update = Plan(morph_sub(self.w, morph_mul(morph_from_numpy(np.array([self.lr])), dw)))
+            self._update_out = self._update.result()._dev
+        self._update.execute(self.stream)
+        st = C.c_void_p(self.stream or 0)     # the replay's stream (0: the library's stream)
+        A.call("amc_buf_copy_async", wbuf.handle, 0, self._update_out.handle, 0, 8 * self.d, st)
+        A.call("amc_buf_copy_async", self._losses.handle, 8 * self.steps, loss._dev.handle, 8 * loss.offset, 8, st)
+        self.w._data = None        # the host copy is stale; .data downloads the device value
+        self.steps += 1
+
+    def trace(self) -> None:
+        """The first step: ssa-realize/ctx in trace mode (allocations
+        recorded, outputs pinned), the update, then finalize-context!."""
+        from .context import context_stats, finalize_context, make_morphism_context
+        from .realize import DeviceBuffer, device_buffer_of
+        from .ssa import ssa_realize_ctx
+        self.ctx = make_morphism_context()
+        loss, dw = ssa_realize_ctx(self.ctx, self.prog)
+        if self.grad_hook is not None:
+            self.grad_hook(dw)
+        w_new = np.ascontiguousarray(self.w.values().reshape(-1) - self.lr * np.asarray(dw.values()).reshape(-1))
+        wbuf = device_buffer_of(self.w)
+        A.call("amc_buf_upload", wbuf.handle, w_new.ctypes.data_as(C.c_void_p), w_new.nbytes, 0)
+        self.w._data = None
+        self._losses = DeviceBuffer.create("f64", self.max_steps)
+        l0 = np.asarray(loss.values(), dtype=np.float64).reshape(-1)[:1].copy()
+        A.call("amc_buf_upload", self._losses.handle, l0.ctypes.data_as(C.c_void_p), 8, 0)
+        self.trace_stats = context_stats(self.ctx)
+        finalize_context(self.ctx)
+        self.steps = 1
+
+    def step(self) -> None:
+        """One replayed step: reset-context!, the compiled SSA plan, the
+        in-place update.  Allocates nothing after the first replay."""
+        from .context import reset_context
+        from .ssa import ssa_realize_ctx
+        reset_context(self.ctx)
+        loss, dw = ssa_realize_ctx(self.ctx, self.prog, stream=self.stream)
+        self._apply(dw, loss)
+
+    def losses(self) -> np.ndarray:
+        """The loss of every step so far (the traced step first)."""
+        return self._losses.download()[: self.steps].copy() if self._losses is not None else np.zeros(0)
+
+    def weights(self) -> np.ndarray:
+        return np.asarray(self.w.values()).reshape(-1)

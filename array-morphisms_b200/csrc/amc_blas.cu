@@ -2,9 +2,11 @@
 // the normalized kernel interface on host vectors, so a Scheme adapter can
 // register libamcuda exactly as chicken-blas-backend.scm registers the CBLAS
 // egg.  Operands are staged through stream-ordered device memory; the
-// arithmetic is the double-accumulating kernel used by the planner, so f64
-// results match the reference's Scheme fallback loops bit for bit when the
-// accumulation order agrees, and f32 results are rounded once from double.
+// arithmetic is the planner's: the double-accumulating k_gemm, whose f64
+// results match the reference's Scheme fallback loops bit for bit and whose
+// f32 results are rounded once from double, and for large matrix-vector
+// shapes and dot products the row passes of amc_rowpass.cu (double
+// accumulation in a fixed parallel order).
 #include <cstring>
 
 #include "amc_internal.h"
@@ -80,7 +82,10 @@ int gemm_host(int dtype, int32_t M, int32_t N, int32_t K, double alpha, const vo
   g.B = dB; g.b_dtype = dtype; g.sb0 = tb ? 1 : ldb; g.sb1 = tb ? ldb : 1;
   g.C = dC; g.c_dtype = dtype;
   g.alpha = alpha; g.beta = beta;
-  int rc = launch_gemm(g, st.s);
+  void* scratch = nullptr;
+  if (size_t sb = gemm_scratch_bytes(g)) scratch = st.up(nullptr, sb);
+  if (st.rc) return st.finish();
+  int rc = launch_gemm_scratch(g, scratch, st.s);
   if (rc) { st.rc = rc; return st.finish(); }
   st.down(C, dC, (size_t)M * N * es);
   return st.finish();
@@ -101,7 +106,10 @@ int gemv_host(int dtype, int32_t M, int32_t N, double alpha, const void* A, cons
   g.B = dx; g.b_dtype = dtype; g.sb0 = 1; g.sb1 = 0;
   g.C = dy; g.c_dtype = dtype;
   g.alpha = alpha; g.beta = beta;
-  int rc = launch_gemm(g, st.s);
+  void* scratch = nullptr;
+  if (size_t sb = gemm_scratch_bytes(g)) scratch = st.up(nullptr, sb);
+  if (st.rc) return st.finish();
+  int rc = launch_gemm_scratch(g, scratch, st.s);
   if (rc) { st.rc = rc; return st.finish(); }
   st.down(y, dy, (size_t)M * es);
   return st.finish();
@@ -122,7 +130,10 @@ int dot_host(int dtype, int32_t N, const void* x, const void* y, void* out) {
   g.B = dy; g.b_dtype = dtype; g.sb0 = 1; g.sb1 = 0;
   g.C = dr; g.c_dtype = dtype;
   g.alpha = 1.0; g.beta = 0.0;
-  int rc = launch_gemm(g, st.s);
+  void* scratch = nullptr;
+  if (size_t sb = gemm_scratch_bytes(g)) scratch = st.up(nullptr, sb);
+  if (st.rc) return st.finish();
+  int rc = launch_gemm_scratch(g, scratch, st.s);
   if (rc) { st.rc = rc; return st.finish(); }
   st.down(out, dr, es);
   return st.finish();

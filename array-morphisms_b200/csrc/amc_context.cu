@@ -135,6 +135,9 @@ int ctx_alloc(void* cp, int32_t dtype, int64_t n, const std::vector<uint64_t>& r
   return AMC_OK;
 }
 
+int ctx_mode(void* cp) { return ((Ctx*)cp)->mode; }
+int32_t ctx_counter(void* cp) { return ((Ctx*)cp)->counter; }
+
 }  // namespace amc
 
 using namespace amc;
@@ -162,9 +165,30 @@ int amc_ctx_pin_output(uint64_t ch, uint64_t ph) {
   Plan* p = plan_get(ph);
   if (!c || !p) return fail(AMC_ERR_INVALID, "amc_ctx_pin_output: unknown context or plan");
   if (c->mode != 0) return fail(AMC_ERR_STATE, "amc_ctx_pin_output: context is not in trace mode");
-  auto it = c->id_of.find(p->result.buf);
-  if (it == c->id_of.end()) return AMC_OK;  // zero-copy result: nothing recorded
-  c->recs[it->second].pinned = true;
+  for (const amc_view& r : p->results) {
+    auto it = c->id_of.find(r.buf);
+    if (it != c->id_of.end()) c->recs[it->second].pinned = true;   // a zero-copy result records nothing
+  }
+  return AMC_OK;
+}
+
+// The replay-plan executor (execute-replay-plan, ssa.scm:1519-1654): a plan
+// created in replay mode runs again with the arena buffers it was bound to,
+// without re-planning.  It must stand where it was created in the replay
+// sequence (the counter at its first allocation id); the counter then moves
+// past its allocations, as re-creating it would.
+int amc_ctx_replay(uint64_t ch, uint64_t ph, void* stream) {
+  Ctx* c = ctx_get(ch);
+  Plan* p = plan_get(ph);
+  if (!c || !p) return fail(AMC_ERR_INVALID, "amc_ctx_replay: unknown context or plan");
+  if (p->ctx != (void*)c || !p->ctx_replay) return fail(AMC_ERR_STATE, "amc_ctx_replay: the plan was not created in this context's replay mode");
+  if (c->mode != 1) return fail(AMC_ERR_STATE, "amc_ctx_replay: context is not in replay mode");
+  if (c->counter != p->ctx_first_id)
+    return fail(AMC_ERR_STATE, "amc_ctx_replay: the plan's allocations start at " + std::to_string(p->ctx_first_id) +
+                                   " but the context counter is at " + std::to_string(c->counter) + " (reset-context! first)");
+  int rc = plan_execute(p, pick_stream(stream));
+  if (rc) return rc;
+  c->counter += p->ctx_ids;
   return AMC_OK;
 }
 

@@ -198,6 +198,44 @@ struct GemmEpiArgs {
 int launch_gemm(const GemmArgs& a, cudaStream_t s);
 int launch_gemm_epi(const GemmEpiArgs& a, cudaStream_t s);
 
+// Row passes over a row-major X (rows x d, unit stride along d); see
+// amc_rowpass.cu.  fwd: p_i = X[i,:] . w stored (alpha/beta, rounded) at
+// r[i*sr]; acc: out[k] = sum_i X[i,k] e_i, with e_i = prog(leaves at row i)
+// whose leaf e_rleaf is the stored p_i (fwd) or e_i = b[i*sb] (no fwd);
+// dot: out = sum_i X[i*ldx] b[i*sb].  Leaf strides[0] is the stride along
+// the row index.  partials: scratch of rowpass_scratch_bytes().
+struct RowPassArgs {
+  int64_t rows;
+  int32_t d, x_dtype;
+  const void* X; int64_t ldx;
+  int32_t fwd, acc, dot, e_rleaf;
+  const void* w; int32_t w_dtype; int32_t _p0; int64_t sw;
+  void* r; int32_t r_dtype; int32_t _p1; int64_t sr;
+  const void* b; int32_t b_dtype; int32_t _p2; int64_t sb;
+  int32_t nleaf; int32_t _p3;
+  DLeaf leaf[kMaxLeaves];
+  DProg prog;
+  void* out; int32_t out_dtype; int32_t _p4; int64_t sout;
+  double alpha, beta;
+  double* partials;
+};
+constexpr int kRowPassMaxD = 1024;
+// Contractions at least this large leave k_gemm's sequential order for the
+// row passes (elements of A; rows of a transposed GEMV; dot length).
+constexpr int64_t kRowPassMinElems = (int64_t)1 << 20;
+constexpr int64_t kRowPassMinRows = (int64_t)1 << 14;
+constexpr int64_t kRowPassMinDot = (int64_t)1 << 16;
+int rowpass_grid(int64_t rows);
+size_t rowpass_scratch_bytes(const RowPassArgs& a);
+int rowpass_launches(const RowPassArgs& a);
+int launch_rowpass(const RowPassArgs& a, cudaStream_t s);
+// GEMM dispatch with the row passes: scratch of gemm_scratch_bytes(g)
+// (0: none needed), launches per execute.
+bool gemm_as_rowpass(const GemmArgs& g, RowPassArgs& r);
+size_t gemm_scratch_bytes(const GemmArgs& g);
+int gemm_launches(const GemmArgs& g);
+int launch_gemm_scratch(const GemmArgs& g, void* scratch, cudaStream_t s);
+
 struct AttnArgs {
   int64_t blocks;
   int32_t n, dk, dv, dtype;

@@ -169,7 +169,8 @@ Plan::~Plan() {
   for (uint64_t h : slots) buf_release(h);
   for (uint64_t h : held) buf_release(h);
   for (void* p : dev_small) cudaFree(p);
-  if (result.buf && result_owned) buf_release(result.buf);
+  for (auto& r : results)
+    if (r.buf) buf_release(r.buf);
 }
 
 struct Builder {
@@ -178,6 +179,11 @@ struct Builder {
   Plan* plan;
   std::vector<std::optional<Val>> memo;
   std::vector<int> uses;   // operand references to each node (+1 for the root)
+  std::vector<char> active; // nodes whose build is in progress
+  // While the GEMV pair builds its row program: a slot whose producer reads
+  // this buffer would run before the buffer is written (watch_hit).
+  uint64_t watch_buf = 0;
+  bool watch_hit = false;
   // The most recent GEMM step, while its result may still take an epilogue.
   struct {
     size_t step = 0;
@@ -241,6 +247,9 @@ struct Builder {
 
   // A contiguous output slot of the given dtype/shape.
   int new_slot(int32_t dtype, int32_t rank, const int64_t* shape, const std::vector<uint64_t>& reads, View& v) {
+    if (watch_buf)
+      for (uint64_t r : reads)
+        if (r == watch_buf) watch_hit = true;
     uint64_t h = 0;
     int rc = plan->add_slot(dtype, numel(rank, shape), reads, &h);
     if (rc) return rc;
@@ -1053,7 +1062,208 @@ struct Builder {
     return AMC_OK;
   }
 
-  int node_gemm(const amc_node& nd, Val& out) {
+  // ----------------------------------------------------------- the GEMV pair
+  // X w over a row-major X (rows x d), and X^T e where e is an element-wise
+  // function of X w's rows: the forward and gradient products of a linear
+  // model (ssa-vjp's matmul rule, ssa.scm:922-940, on the MSE program).
+  // Both run in one read of X (amc_rowpass.cu).
+
+  // The X operand node of a GEMV (rows x d) . (d x 1 | d), else -1.
+  int fwd_gemv_x(int i) const {
+    const amc_node& nd = nodes[i];
+    if ((nd.kind != AMC_N_MATMUL && nd.kind != AMC_N_MATVEC) || nd.n_in != 2) return -1;
+    const amc_node& a = nodes[nd.in[0]];
+    const amc_node& b = nodes[nd.in[1]];
+    if (a.rank != 2) return -1;
+    if (nd.kind == AMC_N_MATMUL && !(b.rank == 2 && b.shape[1] == 1)) return -1;
+    if (nd.kind == AMC_N_MATVEC && b.rank != 1) return -1;
+    return nd.in[0];
+  }
+
+  // The X of a transposed GEMV transpose(X) . (rows x 1 | rows), else -1;
+  // *bnode receives the vector operand.
+  int bwd_gemv_x(int j, int* bnode) const {
+    const amc_node& nd = nodes[j];
+    if ((nd.kind != AMC_N_MATMUL && nd.kind != AMC_N_MATVEC) || nd.n_in != 2) return -1;
+    const amc_node& t = nodes[nd.in[0]];
+    const amc_node& b = nodes[nd.in[1]];
+    if (t.kind != AMC_N_TRANSPOSE || t.rank != 2 || t.n_in != 1 || t.iparam[0] != 1 || t.iparam[1] != 0) return -1;
+    if (nd.kind == AMC_N_MATMUL && !(b.rank == 2 && b.shape[1] == 1)) return -1;
+    if (nd.kind == AMC_N_MATVEC && b.rank != 1) return -1;
+    *bnode = nd.in[1];
+    return t.in[0];
+  }
+
+  // 0: v does not depend on node i; 1: it does, through element-wise nodes
+  // of `rows` elements only (maps, and reshapes that keep the row order);
+  // -1: through anything else.
+  int ew_dep(int v, int i, int64_t rows, std::vector<int8_t>& seen) const {
+    if (v == i) return 1;
+    if (v < i) return 0;   // operands precede their nodes
+    if (seen[v] != 2) return seen[v];
+    const amc_node& nd = nodes[v];
+    int r = 0;
+    if (nd.kind != AMC_N_LEAF) {
+      const int32_t* in = nd.n_in > AMC_NODE_MAX_IN ? nd.in_ext : nd.in;
+      for (int k = 0; k < nd.n_in && r >= 0; ++k) {
+        int d = ew_dep(in[k], i, rows, seen);
+        if (d < 0) r = -1;
+        else if (d > 0) r = 1;
+      }
+      if (r > 0 && !((nd.kind == AMC_N_MAP || nd.kind == AMC_N_RESHAPE) && numel(nd.rank, nd.shape) == rows)) r = -1;
+    }
+    seen[v] = (int8_t)r;
+    return r;
+  }
+
+  // `self` is the node being built (active by definition).
+  bool pair_candidate(int i, int j, int bnode, int self) {
+    if (memo[i] || memo[j] || (i != self && active[i]) || (j != self && active[j])) return false;
+    const amc_node& xa = nodes[nodes[i].in[0]];
+    const int64_t rows = xa.shape[0], d = xa.shape[1];
+    if (d < 1 || d > kRowPassMaxD || rows * d < kRowPassMinElems) return false;
+    if (!dtype_float(nodes[i].dtype) || !dtype_float(nodes[j].dtype)) return false;
+    std::vector<int8_t> seen(n, 2);
+    return ew_dep(bnode, i, rows, seen) == 1;
+  }
+
+  int try_gemv_pair(int idx, Val& out, bool& done) {
+    done = false;
+    int xi = fwd_gemv_x(idx);
+    if (xi >= 0) {
+      for (int j = idx + 1; j < n; ++j) {
+        int b = -1;
+        if (bwd_gemv_x(j, &b) == xi && pair_candidate(idx, j, b, idx)) {
+          int rc = build_gemv_pair(idx, j, b);
+          if (rc) return rc;
+          if (memo[idx]) {
+            out = *memo[idx];
+            done = true;
+          }
+          return AMC_OK;
+        }
+      }
+      return AMC_OK;
+    }
+    int b = -1;
+    int xj = bwd_gemv_x(idx, &b);
+    if (xj < 0) return AMC_OK;
+    for (int i = 0; i < idx; ++i)
+      if (fwd_gemv_x(i) == xj && pair_candidate(i, idx, b, idx)) {
+        int rc = build_gemv_pair(i, idx, b);
+        if (rc) return rc;
+        if (memo[idx]) {
+          out = *memo[idx];
+          done = true;
+        }
+        return AMC_OK;
+      }
+    return AMC_OK;
+  }
+
+  // Forward product i = X w, gradient product j = X^T e(b).  Sets memo[i];
+  // sets memo[j] unless the row program cannot run inside the pass, in which
+  // case the forward product alone is placed before its readers and j is
+  // built as an ordinary product.
+  int build_gemv_pair(int i, int j, int bnode) {
+    const amc_node& fi = nodes[i];
+    const amc_node& fj = nodes[j];
+    View X, w, XT;
+    int rc = concrete(fi.in[0], X);
+    if (!rc) rc = concrete(fi.in[1], w);
+    if (!rc) rc = concrete(fj.in[0], XT);
+    if (rc) return rc;
+    const int64_t rows = X.shape[0], d = X.shape[1];
+    const bool x_ok = X.rank == 2 && dtype_float(X.dtype) && dtype_float(w.dtype) && X.strides[1] == 1 &&
+                      X.strides[0] >= d && w.shape[0] == d && XT.buf == X.buf && XT.offset == X.offset &&
+                      XT.rank == 2 && XT.strides[0] == X.strides[1] && XT.strides[1] == X.strides[0];
+    if (!x_ok) return AMC_OK;   // not a pair after all: both build as ordinary products
+    View r0;
+    rc = new_slot(fi.dtype, fi.rank, fi.shape, {X.buf, w.buf}, r0);
+    if (rc) return rc;
+    GemmArgs g;
+    memset(&g, 0, sizeof g);
+    g.M = rows; g.N = 1; g.K = d; g.alpha = 1.0; g.beta = 0.0;
+    g.A = (const char*)ptr_of(X.buf) + X.offset * (int64_t)dtype_size(X.dtype);
+    g.a_dtype = X.dtype; g.sa0 = X.strides[0]; g.sa1 = 1;
+    g.B = (const char*)ptr_of(w.buf) + w.offset * (int64_t)dtype_size(w.dtype);
+    g.b_dtype = w.dtype; g.sb0 = w.strides[0]; g.sb1 = 0;
+    g.C = ptr_of(r0.buf); g.c_dtype = fi.dtype;
+    memo[i] = Val();
+    memo[i]->view = r0;
+    // the row program: built with X w standing as r0
+    const size_t s0 = plan->steps.size();
+    watch_buf = r0.buf;
+    watch_hit = false;
+    Val ev;
+    rc = get(bnode, ev);
+    watch_buf = 0;
+    if (rc) return rc;
+    Val e = as_expr(ev);
+    if (ev.expr) e.prog.push_back(ins(AMC_OP_CVT, ev.dtype));   // the GEMM reads b's stored value
+    int rleaf = -1;
+    bool ok = !watch_hit && numel(e.rank, e.shape) == rows && (e.rank == 1 || (e.rank == 2 && e.shape[1] == 1)) &&
+              (int)e.leaves.size() <= kMaxLeaves && e.prog.size() <= (size_t)AMC_PROG_MAX;
+    for (size_t l = 0; ok && l < e.leaves.size(); ++l) {
+      const View& L = e.leaves[l];
+      if (!dtype_float(L.dtype)) ok = false;
+      if (L.buf == r0.buf) {
+        if (rleaf >= 0 || L.offset != 0 || (rows > 1 && L.strides[0] != 1)) ok = false;
+        rleaf = (int)l;
+      }
+    }
+    for (auto& I : e.prog)
+      if (I.op == AMC_OP_ICONST || (I.op == AMC_OP_CVT && !dtype_float(I.a))) ok = false;
+    if (!ok || rleaf < 0) {
+      // the forward product alone, ahead of the steps that read r0
+      plan->steps.insert(plan->steps.begin() + (long)s0, [g](cudaStream_t s) { return launch_gemm_scratch(g, nullptr, s); });
+      plan->launches += 1;
+      tail.cbuf = 0;
+      return AMC_OK;
+    }
+    RowPassArgs a;
+    memset(&a, 0, sizeof a);
+    a.fwd = 1; a.acc = 1;
+    a.rows = rows; a.d = (int32_t)d;
+    a.X = g.A; a.x_dtype = X.dtype; a.ldx = X.strides[0];
+    a.w = g.B; a.w_dtype = w.dtype; a.sw = w.strides[0];
+    a.r = g.C; a.r_dtype = fi.dtype; a.sr = 1;
+    a.alpha = 1.0; a.beta = 0.0;
+    a.nleaf = (int32_t)e.leaves.size();
+    a.e_rleaf = rleaf;
+    for (size_t l = 0; l < e.leaves.size(); ++l) {
+      a.leaf[l] = dleaf(e.leaves[l]);
+      for (int k = 1; k < AMC_MAX_RANK; ++k) a.leaf[l].strides[k] = 0;
+      if (rows == 1) a.leaf[l].strides[0] = 0;
+    }
+    fill_prog(a.prog, e.prog, e.leaves);
+    std::vector<uint64_t> reads = reads_of(e.leaves);
+    reads.push_back(X.buf);
+    reads.push_back(w.buf);
+    View part;
+    int64_t psz[1] = {(int64_t)((rowpass_scratch_bytes(a) + 7) / 8)};
+    rc = new_slot(AMC_F64, 1, psz, reads, part);
+    if (rc) return rc;
+    reads.push_back(part.buf);
+    View dw;
+    rc = new_slot(fj.dtype, fj.rank, fj.shape, reads, dw);
+    if (rc) return rc;
+    a.partials = (double*)ptr_of(part.buf);
+    a.out = ptr_of(dw.buf); a.out_dtype = fj.dtype; a.sout = 1;
+    plan->steps.push_back([a](cudaStream_t s) { return launch_rowpass(a, s); });
+    plan->launches += rowpass_launches(a);
+    memo[j] = Val();
+    memo[j]->view = dw;
+    return AMC_OK;
+  }
+
+  int node_gemm(int idx, Val& out) {
+    const amc_node& nd = nodes[idx];
+    {
+      bool done = false;
+      int rc = try_gemv_pair(idx, out, done);
+      if (rc || done) return rc;
+    }
     if (nd.n_in != 2) return err(AMC_ERR_INVALID, "matmul/matvec/dot need two operands");
     View A, B;
     int rc = concrete(nd.in[0], A);
@@ -1089,6 +1299,28 @@ struct Builder {
     if (rc) return rc;
     if (numel(nd.rank, nd.shape) != g.M * g.N) return err(AMC_ERR_INVALID, "matmul result shape mismatch");
     g.C = ptr_of(o.buf);
+    const size_t sbytes = gemm_scratch_bytes(g);
+    if (sbytes) {
+      // a row-pass product (large matrix-vector shapes): no epilogue fusion
+      View sv;
+      int64_t sh[1] = {(int64_t)((sbytes + 7) / 8)};
+      rc = new_slot(AMC_F64, 1, sh, {A.buf, B.buf}, sv);
+      if (rc) return rc;
+      void* scratch = ptr_of(sv.buf);
+      plan->steps.push_back([g, scratch](cudaStream_t s) { return launch_gemm_scratch(g, scratch, s); });
+      plan->launches += gemm_launches(g);
+      out = Val();
+      out.view = o;
+      return AMC_OK;
+    }
+    RowPassArgs rp;
+    if (gemm_as_rowpass(g, rp)) {
+      plan->steps.push_back([g](cudaStream_t s) { return launch_gemm_scratch(g, nullptr, s); });
+      plan->launches += 1;
+      out = Val();
+      out.view = o;
+      return AMC_OK;
+    }
     plan->steps.push_back([g](cudaStream_t s) { return launch_gemm(g, s); });
     plan->launches += 1;
     tail.step = plan->steps.size() - 1;
@@ -1171,6 +1403,7 @@ struct Builder {
     }
     Val v;
     int rc = AMC_OK;
+    active[i] = 1;
     switch (nd.kind) {
       case AMC_N_LEAF: rc = leaf_view(nd, v.view); break;
       case AMC_N_RESHAPE: rc = node_reshape(nd, v); break;
@@ -1185,11 +1418,13 @@ struct Builder {
       case AMC_N_CONCAT: rc = node_route(nd, v); break;
       case AMC_N_MATMUL:
       case AMC_N_MATVEC:
-      case AMC_N_DOT: rc = node_gemm(nd, v); break;
+      case AMC_N_DOT: rc = node_gemm(i, v); break;
       case AMC_N_ATTENTION: rc = node_attention(nd, v); break;
       case AMC_N_SCAN: rc = node_scan(nd, v); break;
-      default: return err(AMC_ERR_INVALID, "unknown node kind");
+      case AMC_N_OUTPUTS: rc = err(AMC_ERR_INVALID, "an OUTPUTS node must be the last node and no operand"); break;
+      default: rc = err(AMC_ERR_INVALID, "unknown node kind"); break;
     }
+    active[i] = 0;
     if (rc) return rc;
     if (nd.kind != AMC_N_MAP && nd.kind != AMC_N_MATMUL && nd.kind != AMC_N_MATVEC && nd.kind != AMC_N_DOT)
       v.fuse_buf = 0;
@@ -1214,27 +1449,58 @@ int plan_create(void* ctx, const amc_node* nodes, int32_t n, uint64_t* out) {
   if (fault_injected("plan")) return fail(AMC_ERR_INJECTED, "plan: injected failure (AMC_FAULT=plan)");
   Plan* p = new Plan();
   p->ctx = ctx;
+  if (ctx && ctx_mode(ctx) == 1) {
+    p->ctx_replay = true;
+    p->ctx_first_id = ctx_counter(ctx);
+  }
   Builder b{nodes, n, p, std::vector<std::optional<Val>>(n)};
   b.count_uses();
-  Val root;
-  int rc = b.get(n - 1, root);
-  if (!rc) {
-    View res;
-    if (root.expr) rc = b.materialize(root, res, b.uses[n - 1] == 1);
-    else res = root.view;
-    if (!rc) {
-      amc_view& r = p->result;
-      r.buf = res.buf;
-      r.dtype = res.dtype;
-      r.rank = res.rank;
-      for (int d = 0; d < res.rank; ++d) { r.shape[d] = res.shape[d]; r.strides[d] = res.strides[d]; }
-      r.offset = res.offset;
-      buf_retain(res.buf);
-      p->result_owned = true;
-      // hold leaf buffers for the plan's lifetime
-      for (int i = 0; i < n; ++i)
-        if (nodes[i].kind == AMC_N_LEAF) { buf_retain(nodes[i].leaf.buf); p->held.push_back(nodes[i].leaf.buf); }
+  b.active.assign(n, 0);
+  // roots: the last node, or every operand of a final OUTPUTS node (the
+  // outputs of one program realized together, each shared node once)
+  std::vector<int> roots;
+  int rc = AMC_OK;
+  if (nodes[n - 1].kind == AMC_N_OUTPUTS) {
+    const amc_node& on = nodes[n - 1];
+    const int32_t* in = on.n_in > AMC_NODE_MAX_IN ? on.in_ext : on.in;
+    if (on.n_in < 1 || !in) rc = fail(AMC_ERR_INVALID, "plan: OUTPUTS needs at least one operand");
+    for (int k = 0; !rc && k < on.n_in; ++k) {
+      if (in[k] < 0 || in[k] >= n - 1) rc = fail(AMC_ERR_INVALID, "plan: OUTPUTS operand out of range");
+      else roots.push_back(in[k]);
     }
+  } else {
+    roots.push_back(n - 1);
+  }
+  for (size_t k = 0; !rc && k < roots.size(); ++k) {
+    Val root;
+    rc = b.get(roots[k], root);
+    if (rc) break;
+    View res;
+    if (root.expr) {
+      rc = b.materialize(root, res, b.uses[roots[k]] == 1);
+      if (rc) break;
+      b.memo[roots[k]] = Val();
+      b.memo[roots[k]]->view = res;   // a root listed twice is one buffer
+    } else {
+      res = root.view;
+    }
+    amc_view r;
+    memset(&r, 0, sizeof r);
+    r.buf = res.buf;
+    r.dtype = res.dtype;
+    r.rank = res.rank;
+    for (int d = 0; d < res.rank; ++d) { r.shape[d] = res.shape[d]; r.strides[d] = res.strides[d]; }
+    r.offset = res.offset;
+    buf_retain(res.buf);
+    p->results.push_back(r);
+  }
+  if (!rc) {
+    if (p->ctx_replay) p->ctx_ids = ctx_counter(ctx) - p->ctx_first_id;
+    p->result = p->results[0];
+    p->result_owned = true;
+    // hold leaf buffers for the plan's lifetime
+    for (int i = 0; i < n; ++i)
+      if (nodes[i].kind == AMC_N_LEAF) { buf_retain(nodes[i].leaf.buf); p->held.push_back(nodes[i].leaf.buf); }
   }
   if (rc) {
     delete p;
@@ -1277,6 +1543,22 @@ int amc_plan_result(uint64_t h, amc_view* out) {
   if (!p || !out) return fail(AMC_ERR_INVALID, "amc_plan_result: unknown plan");
   *out = p->result;
   buf_retain(p->result.buf);  // the caller owns one reference
+  return AMC_OK;
+}
+
+int amc_plan_result_count(uint64_t h, int32_t* n) {
+  Plan* p = plan_get(h);
+  if (!p || !n) return fail(AMC_ERR_INVALID, "amc_plan_result_count: unknown plan");
+  *n = (int32_t)p->results.size();
+  return AMC_OK;
+}
+
+int amc_plan_result_at(uint64_t h, int32_t i, amc_view* out) {
+  Plan* p = plan_get(h);
+  if (!p || !out) return fail(AMC_ERR_INVALID, "amc_plan_result_at: unknown plan");
+  if (i < 0 || i >= (int32_t)p->results.size()) return fail(AMC_ERR_INVALID, "amc_plan_result_at: index out of range");
+  *out = p->results[i];
+  buf_retain(out->buf);  // the caller owns one reference
   return AMC_OK;
 }
 

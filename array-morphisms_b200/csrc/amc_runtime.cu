@@ -285,6 +285,18 @@ int amc_buf_download_async(uint64_t h, void* host, int64_t bytes, int64_t off, v
   return AMC_OK;
 }
 
+int amc_buf_copy_async(uint64_t dst, int64_t dst_off, uint64_t src, int64_t src_off, int64_t bytes, void* stream) {
+  Buffer* d = buf_get(dst);
+  Buffer* s = buf_get(src);
+  int rc = check_range(d, bytes, dst_off);
+  if (!rc) rc = check_range(s, bytes, src_off);
+  if (rc) return rc;
+  if (!bytes) return AMC_OK;
+  AMC_CUDA(cudaMemcpyAsync((char*)d->ptr + dst_off, (const char*)s->ptr + src_off, (size_t)bytes,
+                           cudaMemcpyDeviceToDevice, pick_stream(stream)));
+  return AMC_OK;
+}
+
 int amc_buf_devptr(uint64_t h, void** out) {
   Buffer* b = buf_get(h);
   if (!b || !out) return fail(AMC_ERR_INVALID, "amc_buf_devptr: unknown buffer");

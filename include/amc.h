@@ -153,6 +153,9 @@ typedef struct amc_insn {
  *              (batch-scan, result (n, E...)), 0 the last (batch-fold, result E); the
  *              accumulator is rounded to the init dtype after each step, as the per-element
  *              tree of batch-ops.scm:278-322 stores it.  Replaces that tree of n map nodes.
+ *   OUTPUTS    the last node only: its operands are the roots of one program realized
+ *              together, every shared node once (the outputs of ssa-realize, ssa.scm:1130-1156
+ *              and :1661-1749); amc_plan_result_at gives each.
  * The planner recognises reshape(matmul(W, im2col(X))) on one f32 (C, H, W)
  * image as a convolution (detect-conv2d-pattern, realization.scm:136-164) and
  * runs amc_conv2d_fwd_f32 on it; an ATTENTION node of contiguous f32 operands
@@ -173,6 +176,7 @@ typedef struct amc_insn {
 #define AMC_N_DOT      14
 #define AMC_N_ATTENTION 15
 #define AMC_N_SCAN     16
+#define AMC_N_OUTPUTS  17
 
 #define AMC_NODE_MAX_IN 4
 
@@ -208,6 +212,11 @@ int amc_buf_upload(uint64_t h, const void* host, int64_t bytes, int64_t byte_off
 int amc_buf_download(uint64_t h, void* host, int64_t bytes, int64_t byte_offset);
 int amc_buf_upload_async(uint64_t h, const void* host, int64_t bytes, int64_t byte_offset, void* stream);
 int amc_buf_download_async(uint64_t h, void* host, int64_t bytes, int64_t byte_offset, void* stream);
+/* Device-to-device copy between buffers, stream-ordered (the in-place
+ * update of a vector, e.g. a parameter after an optimizer step,
+ * f64vector-set! over a whole vector; core.scm:649-658). */
+int amc_buf_copy_async(uint64_t dst, int64_t dst_byte_offset, uint64_t src, int64_t src_byte_offset, int64_t bytes,
+                       void* stream);
 int amc_buf_devptr(uint64_t h, void** out);
 int amc_buf_info(uint64_t h, int32_t* dtype, int64_t* nelem);
 int amc_buf_free(uint64_t h);
@@ -221,6 +230,10 @@ int amc_plan_execute(uint64_t plan, void* stream);
 /* The root's result: a view of a plan-owned (or context-owned) buffer, or of
  * a leaf buffer when the root is a zero-copy view (realization.scm:649-717). */
 int amc_plan_result(uint64_t plan, amc_view* out);
+/* The results of a plan whose last node is OUTPUTS (one per operand, in
+ * order; a single-root plan has one).  The caller owns one reference. */
+int amc_plan_result_count(uint64_t plan, int32_t* n);
+int amc_plan_result_at(uint64_t plan, int32_t i, amc_view* out);
 /* Number of kernel launches one execute issues, and allocations it made. */
 int amc_plan_stats(uint64_t plan, int32_t* launches, int32_t* buffers, int64_t* bytes);
 /* Capture the plan's launches into a CUDA graph; later executes replay it. */
@@ -238,6 +251,12 @@ int amc_plan_create_ctx(uint64_t ctx, const amc_node* nodes, int32_t n, uint64_t
 int amc_ctx_pin_output(uint64_t ctx, uint64_t plan);       /* context.scm:190-200 */
 int amc_ctx_finalize(uint64_t ctx);                         /* context.scm:133-154 */
 int amc_ctx_reset(uint64_t ctx);                            /* context.scm:156-161 */
+/* Run again a plan created in this context's replay mode, on its arena
+ * buffers, without re-planning (execute-replay-plan, ssa.scm:1519-1654).  The
+ * context counter must be at the plan's first allocation (after
+ * amc_ctx_reset, or after the plans created before it), and moves past the
+ * plan's allocations. */
+int amc_ctx_replay(uint64_t ctx, uint64_t plan, void* stream);
 /* stats: allocations recorded, buffers after colouring, arena bytes, mode (0 trace, 1 replay) */
 int amc_ctx_stats(uint64_t ctx, int32_t* allocations, int32_t* buffers, int64_t* arena_bytes, int32_t* mode);
 int amc_ctx_destroy(uint64_t ctx);
