@@ -78,13 +78,13 @@ def _torch_splitmix(seed: int, start: int, n: int, device):
     return z
 
 
-def normal_torch(seed: int, n: int, device="cuda", chunk: int = 1 << 26):
-    """Same bits as normal(); generated on the device in chunks."""
+def normal_torch(seed: int, n: int, device="cuda", chunk: int = 1 << 26, start: int = 0):
+    """Same bits as normal(seed, n, start); generated on the device in chunks."""
     import torch
     out = torch.empty(n, dtype=torch.float64, device=device)
     for s in range(0, n, chunk):
         m = min(chunk, n - s)
-        z = _torch_splitmix(seed, 2 * s, 2 * m, device)
+        z = _torch_splitmix(seed, 2 * (start + s), 2 * m, device)
         u = (((z >> 11) & ((1 << 53) - 1)).to(torch.float64)) * (2.0 ** -53)
         u1, u2 = u[0::2], u[1::2]
         out[s:s + m] = torch.sqrt(-2.0 * torch.log1p(-u1)) * torch.cos(2.0 * math.pi * u2)
@@ -194,6 +194,16 @@ def c5_inputs_torch(n: int, d: int = 256, device="cuda"):
     wt = torch.from_numpy(normal(seed_of(5, 1), d)).to(device)
     y = X @ wt + 0.01 * normal_torch(seed_of(5, 2), n, device)
     return X, y, wt
+
+
+def c5_shard_torch(n: int, d: int = 256, shard: int = 0, device="cuda"):
+    """Rows [shard*n, (shard+1)*n) of the config-5 data on the device: X
+    (n, d) and y (n, 1), y = X w_true + 0.01 noise with the shared w_true."""
+    import torch
+    X = normal_torch(seed_of(5, 0), n * d, device, start=shard * n * d).view(n, d)
+    wt = torch.from_numpy(normal(seed_of(5, 1), d)).to(device)
+    y = X @ wt + 0.01 * normal_torch(seed_of(5, 2), n, device, start=shard * n)
+    return X, y.view(n, 1)
 
 
 # ---------------------------------------------------------------------------- device entry points (torch tensors)
@@ -381,6 +391,13 @@ class LinregSSA:
         reset_context(self.ctx)
         loss, dw = ssa_realize_ctx(self.ctx, self.prog, stream=self.stream)
         self._apply(dw, loss)
+
+    def replay_launches(self) -> int:
+        """Kernel launches of one replayed step: the compiled SSA plan and the
+        update (the copies are not kernels)."""
+        plan = self.prog.__dict__.get("_replay", {}).get(self.ctx.handle, (None,))[0]
+        n = plan.stats()["launches"] if plan is not None else 0
+        return n + (self._update.stats()["launches"] if self._update is not None else 0)
 
     def losses(self) -> np.ndarray:
         """The loss of every step so far (the traced step first)."""

@@ -215,6 +215,12 @@ struct RowPassArgs {
   int32_t nleaf; int32_t _p3;
   DLeaf leaf[kMaxLeaves];
   DProg prog;
+  // The row program in closed form when it is the residual form
+  // k * ((c1 * c2) * (p - y)) (k 1 or 2; c1, c2 and y a leaf or a constant,
+  // c2 possibly absent; each operation rounded as the program rounds it):
+  // set by rowpass_prepare.
+  int32_t closed, ck, c_leaf, c2_leaf, y_leaf, c2_used;   // *_leaf -1: the constant
+  double c_const, c2_const, y_const;
   void* out; int32_t out_dtype; int32_t _p4; int64_t sout;
   double alpha, beta;
   double* partials;
@@ -229,6 +235,8 @@ int rowpass_grid(int64_t rows);
 size_t rowpass_scratch_bytes(const RowPassArgs& a);
 int rowpass_launches(const RowPassArgs& a);
 int launch_rowpass(const RowPassArgs& a, cudaStream_t s);
+// Once per planned launch: finds a closed form of the row program.
+void rowpass_prepare(RowPassArgs& a);
 // GEMM dispatch with the row passes: scratch of gemm_scratch_bytes(g)
 // (0: none needed), launches per execute.
 bool gemm_as_rowpass(const GemmArgs& g, RowPassArgs& r);
@@ -271,6 +279,7 @@ int fir_check_error();   // reads and clears the device-side wait-timeout flag
 int attention_check_error();
 int attention_bwd_check_error();
 int conv_check_error();
+int rowpass_check_error();
 int device_check_errors();  // all kernels' bounded-wait flags
 
 }  // namespace amc

@@ -389,6 +389,10 @@ __device__ __forceinline__ void leaf_offsets(const ReduceArgs& a, long long o, l
     for (int l = 0; l < a.nleaf; ++l) off[l] = o * a.leaf_o[l].strides[0] + r * a.leaf_r[l][0];
     return;
   }
+  if (a.orank == 0 && a.rrank == 1) {   // a full reduction of one axis
+    for (int l = 0; l < a.nleaf; ++l) off[l] = r * a.leaf_r[l][0];
+    return;
+  }
   for (int l = 0; l < a.nleaf; ++l) off[l] = 0;
   long long rem = o;
   for (int d = a.orank - 1; d >= 0; --d) {
@@ -482,6 +486,9 @@ __device__ __forceinline__ double small_unary(int op, int cvt, double x) {
   return un_f(op, x);
 }
 
+__device__ __forceinline__ void eval_small_vals(const DProg& P, const double (&l0)[kSmallV], const double (&l1)[kSmallV],
+                                                double (&out)[kSmallV]);
+
 __device__ __forceinline__ void eval_small(const ReduceArgs& a, const long long (&o)[kSmallV],
                                            const long long (&r)[kSmallV], double (&out)[kSmallV]) {
   double l0[kSmallV], l1[kSmallV];
@@ -492,12 +499,18 @@ __device__ __forceinline__ void eval_small(const ReduceArgs& a, const long long 
                 ? load_f(a.leaf_o[1].ptr, a.leaf_o[1].dtype, o[v] * a.leaf_o[1].strides[0] + r[v] * a.leaf_r[1][0])
                 : 0.0;
   }
+  eval_small_vals(a.prog, l0, l1, out);
+}
+
+// The small program on gathered leaf values (l0: leaf 0, l1: leaf 1).
+__device__ __forceinline__ void eval_small_vals(const DProg& P, const double (&l0)[kSmallV], const double (&l1)[kSmallV],
+                                                double (&out)[kSmallV]) {
 #pragma unroll
   for (int v = 0; v < kSmallV; ++v) {
     double s0 = 0.0, s1 = 0.0, s2 = 0.0;
     int sp = 0;
-    for (int pc = 0; pc < a.prog.n; ++pc) {
-      const amc_insn I = a.prog.code[pc];
+    for (int pc = 0; pc < P.n; ++pc) {
+      const amc_insn I = P.code[pc];
       if (I.op == AMC_OP_LOAD || I.op == AMC_OP_CONST) {
         const double t = I.op == AMC_OP_CONST ? I.imm : (I.a == 0 ? l0[v] : l1[v]);
         if (sp == 0) s0 = t;
@@ -1068,7 +1081,27 @@ __global__ void __launch_bounds__(256) k_reduce_tree1(const __grid_constant__ Re
   long long chunk = (a.R + G - 1) / G, r_begin = g * chunk, r_end = r_begin + chunk < a.R ? r_begin + chunk : a.R;
   double f = a.op == AMC_RED_PROD ? 1.0 : a.op == AMC_RED_MAX ? -INFINITY : a.op == AMC_RED_MIN ? INFINITY : 0.0;
   long long i = a.op == AMC_RED_PROD ? 1 : 0;
-  for (long long r = r_begin + threadIdx.x; r < r_end; r += blockDim.x) {
+  long long r = r_begin + threadIdx.x;
+  if (a.prog.all_float && a.prog.max_depth <= 3 && a.nleaf <= 2) {
+    // small float programs: the leaves of kSmallV elements gathered together
+    // (one memory latency per kSmallV elements), the program on registers;
+    // each thread still combines its elements in ascending r
+    const long long step = (long long)blockDim.x;
+    for (; r + (kSmallV - 1) * step < r_end; r += kSmallV * step) {
+      double l0[kSmallV], l1[kSmallV], v[kSmallV];
+#pragma unroll
+      for (int k = 0; k < kSmallV; ++k) {
+        long long off[kMaxLeaves];
+        leaf_offsets(a, o, r + k * step, off);
+        l0[k] = load_f(a.leaf_o[0].ptr, a.leaf_o[0].dtype, off[0]);
+        l1[k] = a.nleaf > 1 ? load_f(a.leaf_o[1].ptr, a.leaf_o[1].dtype, off[1]) : 0.0;
+      }
+      eval_small_vals(a.prog, l0, l1, v);
+#pragma unroll
+      for (int k = 0; k < kSmallV; ++k) tree_combine(a.op, false, f, i, v[k], 0);
+    }
+  }
+  for (; r < r_end; r += blockDim.x) {
     double vf; long long vi;
     eval_src(a, o, r, vf, vi);
     tree_combine(a.op, exact, f, i, vf, vi);
@@ -1090,13 +1123,31 @@ __global__ void __launch_bounds__(256) k_reduce_tree1(const __grid_constant__ Re
   if (threadIdx.x == 0) { pf[o * G + g] = sf[0]; pi[o * G + g] = si[0]; }
 }
 
-__global__ void k_reduce_tree2(const __grid_constant__ ReduceArgs a, const double* pf, const long long* pi, int G) {
-  long long o = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (o >= a.O) return;
+// Pass 2: one CTA per output; thread t folds partials t, t+128, ... in
+// ascending order, then the 128 folds combine in a fixed tree.
+__global__ void __launch_bounds__(128) k_reduce_tree2(const __grid_constant__ ReduceArgs a, const double* pf,
+                                                      const long long* pi, int G) {
+  const long long o = blockIdx.x;
   const bool exact = !dtype_is_float_d(a.src_dtype);
   double f = a.op == AMC_RED_PROD ? 1.0 : a.op == AMC_RED_MAX ? -INFINITY : a.op == AMC_RED_MIN ? INFINITY : 0.0;
   long long i = a.op == AMC_RED_PROD ? 1 : 0;
-  for (int g = 0; g < G; ++g) tree_combine(a.op, exact, f, i, pf[o * G + g], pi[o * G + g]);
+  for (int g = threadIdx.x; g < G; g += blockDim.x) tree_combine(a.op, exact, f, i, pf[o * G + g], pi[o * G + g]);
+  __shared__ double sf[128];
+  __shared__ long long si[128];
+  sf[threadIdx.x] = f;
+  si[threadIdx.x] = i;
+  __syncthreads();
+  for (int w = blockDim.x / 2; w > 0; w >>= 1) {
+    if (threadIdx.x < w) {
+      double f1 = sf[threadIdx.x]; long long i1 = si[threadIdx.x];
+      tree_combine(a.op, exact, f1, i1, sf[threadIdx.x + w], si[threadIdx.x + w]);
+      sf[threadIdx.x] = f1; si[threadIdx.x] = i1;
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x != 0) return;
+  f = sf[0];
+  i = si[0];
   if (dtype_is_float_d(a.out_dtype)) {
     double v = exact ? (double)i : f;
     if (a.op == AMC_RED_MEAN) v = v / (double)a.R;
@@ -1130,7 +1181,7 @@ int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scr
     dim3 g1((unsigned)G, (unsigned)a.O);
     k_reduce_tree1<<<g1, 256, 0, s>>>(a, pf, pi, G);
     AMC_CUDA(cudaGetLastError());
-    k_reduce_tree2<<<(unsigned)((a.O + 127) / 128), 128, 0, s>>>(a, pf, pi, G);
+    k_reduce_tree2<<<(unsigned)a.O, 128, 0, s>>>(a, pf, pi, G);
     AMC_CUDA(cudaGetLastError());
     return AMC_OK;
   }

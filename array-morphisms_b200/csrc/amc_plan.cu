@@ -708,8 +708,15 @@ struct Builder {
     a.src_dtype = e.dtype;
     a.nleaf = (int32_t)e.leaves.size();
     int ko = 0, kr = 0;
+    int n_red_big = 0;
+    for (int d = 0; d < e.rank; ++d)
+      if ((mask & (1LL << d)) && e.shape[d] != 1) ++n_red_big;
     for (int d = 0; d < e.rank; ++d) {
       if (mask & (1LL << d)) {
+        // a reduced axis of extent 1 adds nothing to the index (kept when
+        // every reduced axis has extent 1, so one remains)
+        if (e.shape[d] == 1 && n_red_big > 0) continue;
+        if (e.shape[d] == 1 && n_red_big == 0 && kr > 0) continue;
         a.rshape[kr] = e.shape[d];
         for (int l = 0; l < a.nleaf; ++l) a.leaf_r[l][kr] = e.leaves[l].strides[d];
         ++kr;
@@ -1250,6 +1257,7 @@ struct Builder {
     if (rc) return rc;
     a.partials = (double*)ptr_of(part.buf);
     a.out = ptr_of(dw.buf); a.out_dtype = fj.dtype; a.sout = 1;
+    rowpass_prepare(a);
     plan->steps.push_back([a](cudaStream_t s) { return launch_rowpass(a, s); });
     plan->launches += rowpass_launches(a);
     memo[j] = Val();

@@ -1,28 +1,40 @@
 """Benchmark of the realize hot path on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl amcuda|reference]
-                    [--workload filterbank|fused|linreg|attention|conv]
+                    [--workload all|filterbank|fused|linreg|attention|conv]
 
-Default workload: the polyphase filter bank (config 2 of the five) realized
-through the public API: 64 signals of 2^24 f32 samples per GPU, 64 branches x
-16 taps, the im2col -> reshape -> transpose -> product -> tap-sum tree.  One
-step = one realize of that tree on device-resident inputs.  Multi-GPU runs one
-process per GPU (torchrun); each rank realizes its own 64 signals (weak
-scaling, no data-path collective); time is the max over ranks.
-
-Prints ONE JSON line (rank 0).  `value` is algorithmic HBM GB/s of the whole
-job; `e2e` is the same metric with the host->device upload of every step's
+Default (`all`): ONE JSON line whose headline is the polyphase filter bank
+(config 2 of the five) realized through the public API: 64 signals of 2^24
+f32 samples per GPU, 64 branches x 16 taps, the im2col -> reshape ->
+transpose -> product -> tap-sum tree; one step = one realize of that tree on
+device-resident inputs.  `value` is algorithmic HBM GB/s of the whole job;
+`e2e` is the same metric with the host->device upload of every step's
 signals from pinned memory and the device->host read of its result inside
 the timed region.
+
+The same line carries `per_config`: the other configs, each with its own
+value, step time, roofline, CPU baseline, e2e and clocks:
+  fused_f64, fused_s32  config 1 (view + map + reduce tree, realize)
+  conv                  config 3 (Y, dX, dW through the conv entry points)
+  attention             config 4 (O, dQ, dK, dV through the attention entries)
+  linreg                config 5 (the MSE program through morphism-to-ssa,
+                        ssa-vjp and ssa-realize/ctx replay, 2^22 x 256 f64)
+`--workload X` prints the line of config X alone.
+
+Multi-GPU runs one process per GPU (torchrun); per-GPU work is fixed (weak
+scaling): signals, conv images, attention batch entries and regression rows
+are sharded, config 1 runs as replicas.  The conv weight gradient and the
+regression gradient cross the shards and are summed over ranks in a fixed
+order.  Time is the max over ranks of CUDA-event time.
 """
 from __future__ import annotations
 
 import argparse
+import gc
 import json
 import math
 import multiprocessing as mp
 import os
-import re
 import subprocess
 import sys
 import tempfile
@@ -33,7 +45,11 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "array-morphisms_b200"))
 
 HBM_FALLBACK = 6650.0
-TF32_NOMINAL = 1125.0  # dense TF32 TFLOP/s (half the dense bf16 nominal), used when no measurement exists
+
+# DRAM bytes per launch of the dominant kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum), with what was captured.
+# None where no capture of the current kernel exists.
+NCU_TRAFFIC: dict = {}
 
 
 def peaks():
@@ -42,6 +58,11 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d.get("hbm_gbs", HBM_FALLBACK)), float(d.get("bf16_tflops", 1590.0)), "measured"
     return HBM_FALLBACK, 1590.0, "fallback"
+
+
+def traffic_of(name: str):
+    t = NCU_TRAFFIC.get(name)
+    return (t["bytes_per_launch"], t["source"]) if t else (None, None)
 
 
 # ---------------------------------------------------------------------------- distributed plumbing
@@ -75,8 +96,8 @@ def max_over_ranks(ws, v: float) -> float:
 
 
 class Clocks:
-    """SM clock and clock-event (throttle) reasons sampled during the timed
-    region: NVML every 2 ms on a thread (short regions get samples too), or
+    """SM clock and clock-event (throttle) reasons sampled while the GPU
+    runs the measured work: NVML on a thread (as fast as NVML answers), or
     nvidia-smi -lms 200 when NVML is unavailable.  Only reads settings."""
 
     REASONS = (("hw_slowdown", 0x8), ("sw_power_cap", 0x4), ("sw_thermal_slowdown", 0x20),
@@ -96,6 +117,8 @@ class Clocks:
                 self.h = pynvml.nvmlDeviceGetHandleByIndex(gpu)
             self.mx = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
             self.run = True
+            self._old_si = sys.getswitchinterval()
+            sys.setswitchinterval(0.0002)   # let the sampler in while the main thread works
             self.t = threading.Thread(target=self._loop, daemon=True)
             self.t.start()
         except Exception:
@@ -110,7 +133,11 @@ class Clocks:
                 self.mask |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.h))
             except Exception:
                 pass
-            time.sleep(0.002)
+            time.sleep(0.0005)
+
+    def mark(self):
+        """Number of samples so far (to count those inside the timed region)."""
+        return len(self.samples)
 
     def _start_smi(self, gpu):
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
@@ -123,14 +150,18 @@ class Clocks:
         except Exception:
             self.p = None
 
-    def stop(self):
+    def stop(self, timed_span=None):
         if self.h is not None:
             self.run = False
             self.t.join(timeout=2)
+            sys.setswitchinterval(self._old_si)
             sm = sorted(self.samples)
             reasons = sorted(n for n, bit in self.REASONS if self.mask & bit)
-            return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": self.mx, "reasons": reasons,
-                    "samples": len(sm), "source": "nvml"}
+            out = {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": self.mx, "reasons": reasons,
+                   "samples": len(sm), "source": "nvml"}
+            if timed_span is not None:
+                out["samples_in_timed_region"] = timed_span[1] - timed_span[0]
+            return out
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         time.sleep(0.25)
@@ -158,12 +189,13 @@ class Clocks:
 
 
 # ---------------------------------------------------------------------------- reference arm / CPU baseline
+# Host-only: these build the workload trees (amcuda.morph / amcuda.workloads
+# need no library) and run the oracle port of the reference's CPU path.
 def _oracle_filterbank_sample(args):
     """One oracle realize of the filter-bank tree on a signal sample; returns
     (seconds, algorithmic bytes)."""
     sig, length = args
     sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
     import oracle
     from amcuda import morph as M
     from amcuda import workloads as W
@@ -178,18 +210,10 @@ def _oracle_filterbank_sample(args):
     return dt, length * 4 + F * 64 * 4 + 4096
 
 
-def cpu_filterbank(n_procs: int, length: int, signals: int):
-    """Oracle on `signals` signal samples over n_procs spawned processes."""
-    jobs = [(s, length) for s in range(signals)]
-    t0 = time.perf_counter()
-    if n_procs == 1:
-        res = [_oracle_filterbank_sample(j) for j in jobs]
-    else:
-        with mp.get_context("spawn").Pool(n_procs) as pool:
-            res = pool.map(_oracle_filterbank_sample, jobs)
-    wall = time.perf_counter() - t0
-    by = sum(r[1] for r in res)
-    return by / wall / 1e9, wall
+def cpu_filterbank(length: int):
+    """The oracle on one signal sample, one thread: (GB/s, seconds)."""
+    dt, by = _oracle_filterbank_sample((0, length))
+    return by / dt / 1e9, dt
 
 
 def _timed(fn, min_s: float = 1.0):
@@ -204,60 +228,9 @@ def _timed(fn, min_s: float = 1.0):
             return dt / n
 
 
-def cpu_other(wl: str, dtype: str):
-    """The oracle port of the reference's CPU path, timed on a bounded sample
-    of the workload on one host thread: (value, unit, sample)."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import numpy as np
-    import oracle
-    from amcuda import morph as M
-    from amcuda import workloads as W
-    if wl == "fused":
-        xm, ym = W.c1_inputs_morph(dtype)
-        tree = W.c1_tree(xm, ym)
-        esz = 8 if dtype == "f64" else 4
-        t = _timed(lambda: oracle.realize(tree))
-        return ((2 * (1 << 19) + 1024) * esz / t / 1e9, "GB/s",
-                f"the whole config-1 tree ({dtype}), per-node realize with materialised map and add nodes, 1 thread")
-    if wl == "linreg":
-        rows, d = 1 << 15, 256
-        X, y, _ = W.c5_inputs(rows, d)
-        t = _timed(lambda: oracle.linreg(X, y, np.zeros(d), 1, 0.1))
-        return (rows * (d + 1) * 8 / t / 1e9, "GB/s",
-                f"{rows} of the 2^22 rows, one step of the SSA replay (GEMV, residual, strided GEMM), 1 thread")
-    if wl == "attention":
-        n, dh = 2048, 64
-        q, k, v, do = (W.normal(W.seed_of(4, j), n * dh).astype(np.float32).reshape(1, n, dh) for j in range(4))
-        tree = M.attention_morphism(M.morph_from_numpy(q), M.morph_from_numpy(k), M.morph_from_numpy(v), 0.125)
-
-        def run():
-            oracle.realize(tree)
-            oracle.attention_bwd(q, k, v, do, 0.125)
-        t = _timed(run)
-        return (12.0 * n * n * dh / t / 1e12, "TFLOP/s",
-                "1 of the 256 (batch, head) blocks: the %attn-2d! restatement forward and a double-precision VJP, 1 thread")
-    if wl == "conv":
-        x = W.normal(W.seed_of(3, 0), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
-        w = (W.normal(W.seed_of(3, 1), 64 * 64 * 9) * np.sqrt(2 / 576)).astype(np.float32).reshape(64, 64, 3, 3)
-        dy = W.normal(W.seed_of(3, 2), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
-
-        def run():
-            oracle.conv2d_fwd(x, w)
-            oracle.conv2d_dgrad(dy, w, x.shape)
-            oracle.conv2d_wgrad(x, dy, w.shape)
-        t = _timed(run)
-        return (3 * 2.0 * 64 * 64 * 9 * 56 * 56 / t / 1e12, "TFLOP/s",
-                "1 of the 64 images: im2col + double-accumulating GEMM forward, col2im data gradient, weight gradient, 1 thread")
-    return None
-
-
-def _oracle_other_sample(job):
-    """One bounded unit of a non-default workload through the oracle port of
-    the reference's CPU path: the whole config-1 tree, 2^15 rows of one
-    linear-regression step, one (batch, head) attention block forward and
-    backward, or one conv image's three passes.  Returns (seconds, work) with
-    work in the GPU arm's unit (bytes or FLOPs)."""
-    wl, dtype = job
+def _oracle_unit(wl: str, dtype: str):
+    """One bounded unit of a workload for the oracle port of the reference's
+    CPU path: (run, work in the GPU arm's unit, unit, scale, sample text)."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import numpy as np
     import oracle
@@ -267,12 +240,15 @@ def _oracle_other_sample(job):
     if wl == "fused":
         xm, ym = W.c1_inputs_morph(dtype)
         tree = W.c1_tree(xm, ym)
-        run, work = (lambda: oracle.realize(tree)), (2 * (1 << 19) + 1024) * (8 if dtype == "f64" else 4)
-    elif wl == "linreg":
+        esz = 8 if dtype == "f64" else 4
+        return ((lambda: oracle.realize(tree)), (2 * (1 << 19) + 1024) * esz, "GB/s", 1e9,
+                f"the whole config-1 tree ({dtype}), per-node realize with materialised map and add nodes")
+    if wl == "linreg":
         rows, d = 1 << 15, 256
         X, y, _ = W.c5_inputs(rows, d)
-        run, work = (lambda: oracle.linreg(X, y, np.zeros(d), 1, 0.1)), rows * (d + 1) * 8
-    elif wl == "attention":
+        return ((lambda: oracle.linreg(X, y, np.zeros(d), 1, 0.1)), rows * (d + 1) * 8, "GB/s", 1e9,
+                f"{rows} of the 2^22 rows, one step of the SSA replay (GEMV, residual, mean, strided GEMM)")
+    if wl == "attention":
         n, dh = 2048, 64
         q, k, v, do = (W.normal(W.seed_of(4, j), n * dh).astype(np.float32).reshape(1, n, dh) for j in range(4))
         tree = M.attention_morphism(M.morph_from_numpy(q), M.morph_from_numpy(k), M.morph_from_numpy(v), 0.125)
@@ -280,17 +256,31 @@ def _oracle_other_sample(job):
         def run():
             oracle.realize(tree)
             oracle.attention_bwd(q, k, v, do, 0.125)
-        work = 12.0 * n * n * dh
-    else:
-        x = W.normal(W.seed_of(3, 0), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
-        w = (W.normal(W.seed_of(3, 1), 64 * 64 * 9) * np.sqrt(2 / 576)).astype(np.float32).reshape(64, 64, 3, 3)
-        dy = W.normal(W.seed_of(3, 2), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
+        return (run, 12.0 * n * n * dh, "TFLOP/s", 1e12,
+                "1 of the 256 (batch, head) blocks: the %attn-2d! restatement forward and a double-precision VJP")
+    x = W.normal(W.seed_of(3, 0), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
+    w = (W.normal(W.seed_of(3, 1), 64 * 64 * 9) * np.sqrt(2 / 576)).astype(np.float32).reshape(64, 64, 3, 3)
+    dy = W.normal(W.seed_of(3, 2), 64 * 56 * 56).astype(np.float32).reshape(1, 64, 56, 56)
 
-        def run():
-            oracle.conv2d_fwd(x, w)
-            oracle.conv2d_dgrad(dy, w, x.shape)
-            oracle.conv2d_wgrad(x, dy, w.shape)
-        work = 3 * 2.0 * 64 * 64 * 9 * 56 * 56
+    def run():
+        oracle.conv2d_fwd(x, w)
+        oracle.conv2d_dgrad(dy, w, x.shape)
+        oracle.conv2d_wgrad(x, dy, w.shape)
+    return (run, 3 * 2.0 * 64 * 64 * 9 * 56 * 56, "TFLOP/s", 1e12,
+            "1 of the 64 images: im2col + double-accumulating GEMM forward, col2im data gradient, weight gradient")
+
+
+def cpu_other(wl: str, dtype: str) -> dict:
+    """The oracle port timed on a bounded sample of the workload, 1 thread."""
+    run, work, unit, scale, what = _oracle_unit(wl, dtype)
+    t = _timed(run)
+    return {"value": work / t / scale, "unit": unit, "cores": 1, "kind": "port", "sample": what + ", 1 thread"}
+
+
+def _oracle_other_sample(job):
+    """One bounded unit (see _oracle_unit) timed once: (seconds, work)."""
+    wl, dtype = job
+    run, work, _, _, _ = _oracle_unit(wl, dtype)
     t0 = time.perf_counter()
     run()
     return time.perf_counter() - t0, work
@@ -302,91 +292,103 @@ _OTHER_ARM = {
     "attention": ("TFLOP/s", 1e12, "1 of the 256 (batch, head) blocks, forward and backward, per process per step"),
     "conv": ("TFLOP/s", 1e12, "1 of the 64 images, three passes, per process per step"),
 }
-_OTHER_METRIC = {
+_METRIC = {
     "fused": "fused view+map+reduce realize GB/s ({dtype})",
-    "linreg": "linear-regression step (fused pass over X) GB/s",
+    "linreg": "linear-regression SSA training step GB/s (ssa-realize/ctx replay, one pass over X)",
     "attention": "attention forward + backward TFLOP/s",
     "conv": "conv2d forward + data gradient + weight gradient TFLOP/s",
 }
 
 
-def other_config(wl: str, args) -> dict:
-    """The `config` of a non-default workload's bench line (both arms)."""
+def other_config(wl: str, args, dtype: str | None = None) -> dict:
+    """The `config` of a non-headline workload (both arms)."""
+    dtype = dtype or args.dtype
     if wl == "fused":
-        return {"workload": f"config 1: x,y 2^20 {args.dtype}, reshape 1024x1024, transpose, slice step 2, "
-                            f"sum(x^2+y) over axis 1", "l2": "256 MB flush between steps"}
+        return {"workload": f"config 1: x,y 2^20 {dtype}, reshape 1024x1024, transpose, slice step 2, "
+                            f"sum(x^2+y) over axis 1", "l2": "256 MB flush between steps", "parallelism": "replicas"}
     if wl == "linreg":
-        return {"workload": f"config 5: X {args.rows} x 256 f64 per GPU, MSE gradient step, lr 0.1",
-                "l2": "X larger than L2"}
+        return {"workload": f"config 5: X {args.rows} x 256 f64 per GPU, loss mean((X w - y)^2), gradient by "
+                            f"reverse-mode SSA, plain gradient step lr 0.1, ssa-realize/ctx replay",
+                "l2": "X (8 GiB) larger than L2", "parallelism": "rows sharded, gradient summed over ranks"}
     if wl == "attention":
         return {"workload": f"config 4: Q,K,V,dO ({args.batch or 16},16,2048,64) f32, scale 1/8; O, dQ, dK, dV per step",
-                "flops": "algorithmic 12*B*H*S^2*D (6 GEMMs; the backward recomputes S and dP twice more)"}
+                "flops": "algorithmic 12*B*H*S^2*D (6 GEMMs; the backward recomputes S and dP twice more)",
+                "l2": "operands (0.54 GB) larger than L2", "parallelism": "batch sharded"}
     return {"workload": f"config 3: x ({args.batch or 64},64,56,56) f32, w (64,64,3,3), stride 1 pad 1; "
-                        f"Y, dX and dW per step"}
+                        f"Y, dX and dW per step", "l2": "x, dY, Y, dX (205 MB) larger than L2",
+            "parallelism": "batch sharded, dW summed over ranks"}
 
 
-def reference_arm_other(args, cores):
-    """The reference arm of the non-default workloads: the oracle port on
-    every host core (one spawned process per core, each running the bounded
-    unit above), whole-job work over the wall time of each step."""
-    wl = args.workload
-    unit, scale, what = _OTHER_ARM[wl]
-    dtype = args.dtype if wl == "fused" else ("f64" if wl == "linreg" else "f32")
-    jobs = [(wl, args.dtype)] * cores
+def _ref_pool_steps(pool, jobs, args, steps=None):
     times, vals = [], []
-    with mp.get_context("spawn").Pool(cores) as pool:
-        for i in range(args.warmup + args.steps):
-            res = pool.map(_oracle_other_sample, jobs)
-            # the processes run their units side by side: the step takes the
-            # longest one (input generation and process start-up excluded)
-            dt = max(r[0] for r in res)
-            if i >= args.warmup:
-                times.append(dt)
-                vals.append(sum(r[1] for r in res) / dt / scale)
-    value = sum(vals) / len(vals)
-    sample = (what.format(dtype=args.dtype) + f", {cores} spawned processes running side by side, step time = the "
+    steps = args.steps if steps is None else steps
+    for i in range(args.warmup + steps):
+        res = pool.map(_oracle_other_sample, jobs)
+        # the processes run their units side by side: the step takes the
+        # longest one (input generation and process start-up excluded)
+        dt = max(r[0] for r in res)
+        if i >= args.warmup:
+            times.append(dt)
+            vals.append(sum(r[1] for r in res) / dt)
+    return times, vals
+
+
+def reference_line_other(args, cores, wl, dtype, pool, steps=None) -> dict:
+    """The reference arm of a non-headline workload: the oracle port on every
+    host core (one spawned process per core, each running one bounded unit),
+    whole-job work over the wall time of each step."""
+    unit, scale, what = _OTHER_ARM[wl]
+    times, vals = _ref_pool_steps(pool, [(wl, dtype)] * cores, args, steps)
+    value = sum(vals) / len(vals) / scale
+    sample = (what.format(dtype=dtype) + f", {cores} spawned processes running side by side, step time = the "
               f"longest process, oracle port of the reference's CPU path")
-    print(json.dumps({
-        "impl": "reference", "metric": _OTHER_METRIC[wl].format(dtype=args.dtype), "value": value, "unit": unit,
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": dtype, "data": "synthetic",
-        "config": dict(other_config(wl, args), sample=sample),
-        "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+    return {"impl": "reference", "metric": _METRIC[wl].format(dtype=dtype), "value": value, "unit": unit,
+            "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+            "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": dtype if wl in ("fused", "linreg") else "f32", "data": "synthetic",
+            "config": dict(other_config(wl, args, dtype), sample=sample),
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+PER_CONFIG = [("fused_f64", "fused", "f64"), ("fused_s32", "fused", "s32"), ("conv", "conv", "f32"),
+              ("attention", "attention", "f32"), ("linreg", "linreg", "f64")]
 
 
 def reference_arm(args, ws, rank):
     if rank != 0:
         return
     cores = args.ref_procs or os.cpu_count() or 1
-    if args.workload != "filterbank":
-        reference_arm_other(args, cores)
-        return
-    length = 1 << 20
-    signals = cores
-    # warm-up (spawn + oracle build) then timed steps
-    times, vals = [], []
     with mp.get_context("spawn").Pool(cores) as pool:
-        pool.map(_oracle_filterbank_sample, [(s, 1 << 14) for s in range(cores)])
+        if args.workload not in ("all", "filterbank"):
+            print(json.dumps(reference_line_other(args, cores, args.workload, args.dtype, pool)))
+            return
+        length = 1 << 20
+        pool.map(_oracle_filterbank_sample, [(s, 1 << 14) for s in range(cores)])  # spawn + oracle build
+        times, vals = [], []
         for i in range(args.warmup + args.steps):
             t0 = time.perf_counter()
-            res = pool.map(_oracle_filterbank_sample, [(s, length) for s in range(signals)])
+            res = pool.map(_oracle_filterbank_sample, [(s, length) for s in range(cores)])
             dt = time.perf_counter() - t0
             if i >= args.warmup:
                 times.append(dt)
                 vals.append(sum(r[1] for r in res) / dt / 1e9)
-    value = sum(vals) / len(vals)
-    sample = (f"{signals} signals x 2^20 samples per step (of the 64 x 2^24 workload), oracle port of the "
-              f"reference's per-node realize, one spawned process per host core")
-    print(json.dumps({
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": dict(CONFIG_FB, sample=sample),
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
-        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }))
+        value = sum(vals) / len(vals)
+        sample = (f"{cores} signals x 2^20 samples per step (of the 64 x 2^24 workload), oracle port of the "
+                  f"reference's per-node realize, one spawned process per host core")
+        out = {
+            "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(CONFIG_FB, sample=sample),
+            "cpu_baseline": {"value": value, "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        if args.workload == "all" and not args.no_per_config:
+            # one timed step of each (a few seconds of host work apiece)
+            out["per_config"] = {name: reference_line_other(args, cores, wl, dt, pool, steps=1)
+                                 for name, wl, dt in PER_CONFIG}
+        print(json.dumps(out))
 
 
 METRIC = "fused realize() HBM GB/s (polyphase filter bank)"
@@ -396,69 +398,154 @@ CONFIG_FB = {"workload": "polyphase filter bank: 64 signals x 2^24 f32 per GPU, 
              "l2": "inputs (4 GiB per GPU) larger than L2; no flush needed", "parallelism": "batch-sharded, weak"}
 
 
-# ---------------------------------------------------------------------------- GPU arm: filter bank
+# ---------------------------------------------------------------------------- device helpers
+def _cudart():
+    import ctypes as C
+    import torch  # noqa: F401  (loads the CUDA runtime)
+    for name in ("libcudart.so.12", "libcudart.so"):
+        try:
+            return C.CDLL(name)
+        except OSError:
+            continue
+    import glob
+    for p in glob.glob(os.path.join(os.path.dirname(__import__("torch").__file__), "lib", "libcudart*.so*")):
+        return C.CDLL(p)
+    raise RuntimeError("libcudart not found")
+
+
+def cudart_copy(dst: int, src: int, nbytes: int, kind: int = 3):
+    """cudaMemcpy (kind 3: device to device, 2: device to host)."""
+    import ctypes as C
+    rt = _cudart()
+    rt.cudaMemcpy.restype = C.c_int
+    rc = rt.cudaMemcpy(C.c_void_p(dst), C.c_void_p(src), C.c_size_t(nbytes), kind)
+    if rc:
+        raise RuntimeError(f"cudaMemcpy failed {rc}")
+
+
+def device_buffer_from(t, dtype: str):
+    """A library buffer holding a copy of the torch CUDA tensor t."""
+    import amcuda as am
+    b = am.DeviceBuffer.create(dtype, t.numel())
+    cudart_copy(b.devptr(), t.data_ptr(), t.numel() * t.element_size())
+    return b
+
+
+class CudaView:
+    """A device pointer presented to torch (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, n: int, typestr: str = "<f8"):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
+
+
+def _release():
+    import torch
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+
+
+def time_steps(run, steps, warmup, stream, local, ws, pre=None, min_region_s: float = 0.0, max_steps: int = 20000):
+    """Warm up, then time `steps` steps (more when one step is so short that
+    the region would be under min_region_s) with CUDA events on `stream`,
+    each step bracketed by its own events; clocks sampled meanwhile.
+    Returns (per-step ms list, steps, clocks)."""
+    import torch
+    for _ in range(warmup):
+        if pre:
+            pre()
+        run()
+    torch.cuda.synchronize()
+    if min_region_s > 0:
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        run()
+        b.record(stream)
+        torch.cuda.synchronize()
+        est = max(a.elapsed_time(b) / 1e3, 1e-6)
+        steps = max(steps, min(max_steps, int(math.ceil(min_region_s / est))))
+    barrier(ws)
+    clk = Clocks(local)
+    time.sleep(0.01)
+    evs = []
+    m0 = clk.mark()
+    for _ in range(steps):
+        if pre:
+            pre()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        run()
+        b.record(stream)
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    m1 = clk.mark()
+    clocks = clk.stop((m0, m1))
+    return [a.elapsed_time(b) for a, b in evs], steps, clocks
+
+
+def time_e2e(step, steps, stream):
+    """Wall of `steps` end-to-end steps on `stream` by CUDA events (ms)."""
+    import torch
+    step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b)
+
+
+_TC_PEAK = {}
+
+
+def tf32_peak():
+    if "v" not in _TC_PEAK:
+        from amcuda import workloads as W
+        _TC_PEAK["v"] = W.tc_peak_tf32(4000)
+    return _TC_PEAK["v"]
+
+
+def entry(metric, value, unit, ms, steps, dtype, cfg, roofline, cpu, e2e, launches, clocks, **extra):
+    d = {"metric": metric, "value": value, "unit": unit, "ms_per_step": ms, "steps": steps, "dtype": dtype,
+         "config": cfg, "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
+         "clocks": clocks}
+    d.update(extra)
+    return d
+
+
+# ---------------------------------------------------------------------------- GPU arm: filter bank (headline)
 def bench_filterbank(args, ws, rank, local):
-    import numpy as np
+    import ctypes as C
     import torch
     import amcuda as am
+    from amcuda import _abi as A
     from amcuda import workloads as W
-    from amcuda.dist import allreduce_fixed_order
     am.init(local)
     torch.cuda.set_device(local)
     B, L = args.signals, args.samples
     F = W.c2_frames(L)
     x_t = W.c2_signals_torch(B, L, device="cuda", first=rank * B)
     h_t = torch.from_numpy(W.c2_prototype()).cuda()
-    # leaves wrap the device tensors (no copy); the tree is the public API's
-    xb = am.DeviceBuffer.create("f32", B * L)
-    hb = am.DeviceBuffer.create("f32", h_t.numel())
-    torch.cuda.synchronize()
-    import ctypes as C
-    from amcuda import _abi as A
-    A.call("amc_buf_upload", hb.handle, C.c_void_p(h_t.cpu().numpy().ctypes.data), 4 * h_t.numel(), 0)
-    # copy the generated signals into the library's buffer (device to device)
-    xptr = xb.devptr()
-    cudart_copy(xptr, x_t.data_ptr(), 4 * B * L)
+    xb = device_buffer_from(x_t, "f32")
+    hb = device_buffer_from(h_t, "f32")
     del x_t
-    torch.cuda.empty_cache()
+    _release()
     xm = am.Concrete(None, (B, L), dtype="f32", dev=xb)
     hm = am.Concrete(None, (W.PROTO,), dtype="f32", dev=hb)
     plan = am.Plan(W.c2_tree(xm, hm))
     st = plan.stats()
-    torch.cuda.synchronize()
     stream = torch.cuda.Stream()  # an explicit stream: events and launches share it
     torch.cuda.set_stream(stream)
     sptr = stream.cuda_stream
-    for _ in range(args.warmup):
-        plan.execute(sptr)
-    torch.cuda.synchronize()
-    barrier(ws)
-    clk = Clocks(local)
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    per = []
-    torch.cuda.synchronize()
-    t_all0 = torch.cuda.Event(enable_timing=True)
-    t_all1 = torch.cuda.Event(enable_timing=True)
-    t_all0.record(stream)
-    for _ in range(args.steps):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        plan.execute(sptr)
-        b.record(stream)
-        per.append((a, b))
-    t_all1.record(stream)
-    torch.cuda.synchronize()
-    clocks = clk.stop()
-    barrier(ws)
-    total_ms = t_all0.elapsed_time(t_all1)
-    step_ms = [a.elapsed_time(b) for a, b in per]
-    total_ms = max_over_ranks(ws, total_ms)
+    step_ms, steps, clocks = time_steps(lambda: plan.execute(sptr), args.steps, args.warmup, stream, local, ws)
+    total_ms = max_over_ranks(ws, sum(step_ms))
     bytes_step = B * L * 4 + B * F * 64 * 4 + 4 * W.PROTO
-    value = ws * bytes_step * args.steps / (total_ms / 1e3) / 1e9
+    value = ws * bytes_step * steps / (total_ms / 1e3) / 1e9
     hbm, _, kind = peaks()
-    mean_step = sum(step_ms) / len(step_ms)
-    achieved = bytes_step / (mean_step / 1e3) / 1e9
-    traffic = None
+    achieved = bytes_step / (sum(step_ms) / len(step_ms) / 1e3) / 1e9
+    traffic, tsrc = traffic_of("filterbank")
 
     # ---- end to end: pinned host signals -> device -> realize -> host result.
     # Two buffer sets (two plans of the same public tree) and three streams:
@@ -469,7 +556,7 @@ def bench_filterbank(args, ws, rank, local):
     if not args.no_e2e:
         x_host = torch.empty((B, L), dtype=torch.float32, pin_memory=True)
         out_host = torch.empty((B, F, 64), dtype=torch.float32, pin_memory=True)
-        cudart_copy_d2h(x_host.data_ptr(), xptr, 4 * B * L)
+        cudart_copy(x_host.data_ptr(), xb.devptr(), 4 * B * L, 2)
         xb2 = am.DeviceBuffer.create("f32", B * L)
         plan2 = am.Plan(W.c2_tree(am.Concrete(None, (B, L), dtype="f32", dev=xb2), hm))
         sets = [(xb, plan, plan.result()._dev), (xb2, plan2, plan2.result()._dev)]
@@ -513,193 +600,301 @@ def bench_filterbank(args, ws, rank, local):
                "path": "two Plans of the public realize tree over two device buffer sets; per step "
                        "amc_buf_upload_async of the signals from pinned memory, execute, amc_buf_download_async of "
                        "the (B,F,64) result, on three streams so consecutive steps' copies and realize overlap"}
-        del plan2, xb2
+        del plan2, xb2, sets, x_host, out_host
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        v, wall = cpu_filterbank(1, 1 << 22, 1)
+        v, wall = cpu_filterbank(1 << 22)
         cpu = {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
                "sample": f"1 signal x 2^22 samples through the oracle port of the reference's per-node realize "
                          f"(im2col, product and tap reduction materialised), 1 thread, {wall:.1f} s"}
-    if rank == 0:
-        out = {
-            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG_FB,
-            "roofline": {"bound": "hbm", "kernel": "k_fir_tma (+ k_fir_tail)", "achieved": achieved, "peak": hbm,
-                         "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
-                         "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind,
-                         "algorithmic_bytes_per_launch": bytes_step},
-            "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": st["launches"] * args.steps, "clocks": clocks,
-        }
-        print(json.dumps(out))
+    out = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": ws, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": total_ms / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": CONFIG_FB,
+        "roofline": {"bound": "hbm", "kernel": "k_fir_tma (+ k_fir_tail)", "achieved": achieved, "peak": hbm,
+                     "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic, "traffic_source": tsrc,
+                     "peak_source": f"{kind} (MEASURED_PEAKS.json hbm_gbs)" if kind == "measured" else kind,
+                     "algorithmic_bytes_per_launch": bytes_step},
+        "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": st["launches"] * steps, "clocks": clocks,
+    }
+    del plan, xm, hm, xb, hb
+    _release()
+    return out
 
 
-def _cudart():
+# ---------------------------------------------------------------------------- GPU arm: the other configs
+def pc_fused(args, ws, rank, local, dtype):
+    """Config 1 through realize: the view + map + reduce tree on device leaves."""
     import ctypes as C
-    import torch  # noqa: F401  (loads the CUDA runtime)
-    for name in ("libcudart.so.12", "libcudart.so"):
-        try:
-            return C.CDLL(name)
-        except OSError:
-            continue
-    import glob
-    for p in glob.glob(os.path.join(os.path.dirname(__import__("torch").__file__), "lib", "libcudart*.so*")):
-        return C.CDLL(p)
-    raise RuntimeError("libcudart not found")
+    import torch
+    import amcuda as am
+    from amcuda import _abi as A
+    from amcuda import workloads as W
+    stream = torch.cuda.current_stream()
+    sptr = stream.cuda_stream
+    x, y = W.c1_inputs(dtype)
+    xm, ym = am.morph_from_numpy(x, dtype), am.morph_from_numpy(y, dtype)
+    plan = am.Plan(W.c1_tree(xm, ym))
+    esz = 8 if dtype == "f64" else 4
+    work = 2 * (1 << 19) * esz + 1024 * esz
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    ms, steps, clocks = time_steps(lambda: plan.execute(sptr), args.steps, args.warmup, stream, local, ws,
+                                   pre=lambda: flush.fill_(1), min_region_s=0.3, max_steps=4000)
+    t = max_over_ranks(ws, sum(ms))
+    hbm, _, kind = peaks()
+    per = work / (sum(ms) / len(ms) / 1e3) / 1e9
+    e2e = None
+    if not args.no_e2e:
+        from amcuda.realize import device_buffer_of
+        xh = torch.from_numpy(x).pin_memory()
+        yh = torch.from_numpy(y).pin_memory()
+        out_dev = plan.result()._dev
+        oh = torch.empty(1024 * esz, dtype=torch.uint8, pin_memory=True)
+        xbuf, ybuf = device_buffer_of(xm), device_buffer_of(ym)
+        sp = C.c_void_p(sptr)
+
+        def step():
+            A.call("amc_buf_upload_async", xbuf.handle, C.c_void_p(xh.data_ptr()), x.nbytes, 0, sp)
+            A.call("amc_buf_upload_async", ybuf.handle, C.c_void_p(yh.data_ptr()), y.nbytes, 0, sp)
+            plan.execute(sptr)
+            A.call("amc_buf_download_async", out_dev.handle, C.c_void_p(oh.data_ptr()), 1024 * esz, 0, sp)
+        n_e = 50
+        e_ms = max_over_ranks(ws, time_e2e(step, n_e, stream))
+        e2e = {"value": ws * work * n_e / (e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": x.nbytes + y.nbytes,
+               "d2h_bytes_per_step": 1024 * esz, "steps": n_e,
+               "path": "amc_buf_upload_async of x and y from pinned memory into the plan's leaves, the realize "
+                       "plan, amc_buf_download_async of the 1024 sums, one stream"}
+    cpu = cpu_other("fused", dtype) if rank == 0 and ws == 1 and not args.no_cpu else None
+    traffic, tsrc = traffic_of(f"fused_{dtype}")
+    launches = plan.stats()["launches"]
+    return entry(_METRIC["fused"].format(dtype=dtype), ws * work * steps / (t / 1e3) / 1e9, "GB/s", t / steps, steps,
+                 dtype, other_config("fused", args, dtype),
+                 {"bound": "hbm", "kernel": "k_reduce_staged", "achieved": per, "peak": hbm, "unit": "GB/s",
+                  "frac": per / hbm, "traffic": traffic, "traffic_source": tsrc, "peak_source": kind + " hbm_gbs",
+                  "algorithmic_bytes_per_launch": work},
+                 cpu, e2e, launches * steps, clocks, scaling="replicas")
 
 
-def cudart_copy(dst: int, src: int, nbytes: int):
+def pc_conv(args, ws, rank, local):
+    """Config 3 through the conv entry points (the plugin seam of
+    execute-conv2d-blas): Y, dX and dW per step."""
+    import numpy as np
+    import torch
+    from amcuda import workloads as W
+    from amcuda.dist import allreduce_fixed_order
+    stream = torch.cuda.current_stream()
+    N = args.batch or 64
+    gen = lambda j, n: W.normal(W.seed_of(3, j), n, start=rank * n if j != 1 else 0)
+    x = torch.from_numpy(gen(0, N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
+    wt = torch.from_numpy((gen(1, 64 * 64 * 9) * math.sqrt(2 / 576)).astype(np.float32)).cuda().view(64, 64, 3, 3)
+    dy = torch.from_numpy(gen(2, N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
+    yy, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(wt)
+
+    def run():
+        W.conv2d_fwd(x, wt, yy)
+        W.conv2d_dgrad(dy, wt, dx)
+        W.conv2d_wgrad(x, dy, dw)
+        if ws > 1:
+            allreduce_fixed_order(dw)   # dW sums over the batch shards
+    work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
+    ms, steps, clocks = time_steps(run, args.steps, args.warmup, stream, local, ws, min_region_s=0.3, max_steps=4000)
+    t = max_over_ranks(ws, sum(ms))
+    peak = tf32_peak()
+    per = work / (sum(ms) / len(ms) / 1e3) / 1e12
+    e2e = None
+    if not args.no_e2e:
+        xh, dyh = x.cpu().pin_memory(), dy.cpu().pin_memory()
+        yh, dxh, dwh = (torch.empty(t_.shape, dtype=torch.float32, pin_memory=True) for t_ in (yy, dx, dw))
+
+        def step():
+            x.copy_(xh, non_blocking=True)
+            dy.copy_(dyh, non_blocking=True)
+            run()
+            yh.copy_(yy, non_blocking=True)
+            dxh.copy_(dx, non_blocking=True)
+            dwh.copy_(dw, non_blocking=True)
+        n_e = 10
+        e_ms = max_over_ranks(ws, time_e2e(step, n_e, stream))
+        e2e = {"value": ws * work * n_e / (e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": 2 * x.numel() * 4, "d2h_bytes_per_step": 2 * x.numel() * 4 + dw.numel() * 4,
+               "steps": n_e, "path": "x and dY copied from pinned memory, amc_conv2d_fwd/dgrad/wgrad_f32, Y, dX and "
+                                     "dW copied back, one stream"}
+    cpu = cpu_other("conv", "f32") if rank == 0 and ws == 1 and not args.no_cpu else None
+    traffic, tsrc = traffic_of("conv")
+    return entry(_METRIC["conv"], ws * work * steps / (t / 1e3) / 1e12, "TFLOP/s", t / steps, steps, "f32",
+                 other_config("conv", args),
+                 {"bound": "tensor", "kernel": "k_conv3x3_tc, k_conv_wgrad_tc", "achieved": per, "peak": peak,
+                  "unit": "TFLOP/s", "frac": per / peak, "traffic": traffic, "traffic_source": tsrc,
+                  "peak_source": "dense TF32 rate of a tcgen05 kind::tf32 M=128 N=256 issue loop on this GPU "
+                                 "(amc_tc_peak_tf32), measured in this run",
+                  "algorithmic_flops_per_step": work},
+                 cpu, e2e, 6 * steps, clocks, scaling="weak")
+
+
+def pc_attention(args, ws, rank, local):
+    """Config 4 through the attention entry points: O, dQ, dK, dV per step."""
+    import numpy as np
+    import torch
+    from amcuda import workloads as W
+    stream = torch.cuda.current_stream()
+    B, H, S, D = args.batch or 16, 16, 2048, 64
+    n = B * H * S * D
+    q, k, v, do = (torch.from_numpy(W.normal(W.seed_of(4, j), n, start=rank * n).astype(np.float32)).cuda()
+                   .view(B, H, S, D) for j in range(4))
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, S), dtype=torch.float32, device="cuda")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def run():
+        W.attention_fwd(q, k, v, o, lse, 1.0 / 8.0)
+        W.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, 1.0 / 8.0)
+    work = 12.0 * B * H * S * S * D
+    ms, steps, clocks = time_steps(run, args.steps, args.warmup, stream, local, ws, min_region_s=0.3, max_steps=2000)
+    t = max_over_ranks(ws, sum(ms))
+    peak = tf32_peak()
+    per = work / (sum(ms) / len(ms) / 1e3) / 1e12
+    e2e = None
+    if not args.no_e2e:
+        hs = [a.cpu().pin_memory() for a in (q, k, v, do)]
+        outs = [torch.empty(a.shape, dtype=torch.float32, pin_memory=True) for a in (o, dq, dk, dv)]
+
+        def step():
+            for dev_t, h in zip((q, k, v, do), hs):
+                dev_t.copy_(h, non_blocking=True)
+            run()
+            for h, dev_t in zip(outs, (o, dq, dk, dv)):
+                h.copy_(dev_t, non_blocking=True)
+        n_e = 6
+        e_ms = max_over_ranks(ws, time_e2e(step, n_e, stream))
+        e2e = {"value": ws * work * n_e / (e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": 4 * n * 4,
+               "d2h_bytes_per_step": 4 * n * 4, "steps": n_e,
+               "path": "Q, K, V, dO copied from pinned memory, amc_attention_fwd_f32 + amc_attention_bwd_f32, O, dQ, "
+                       "dK, dV copied back, one stream"}
+    cpu = cpu_other("attention", "f32") if rank == 0 and ws == 1 and not args.no_cpu else None
+    traffic, tsrc = traffic_of("attention")
+    return entry(_METRIC["attention"], ws * work * steps / (t / 1e3) / 1e12, "TFLOP/s", t / steps, steps, "f32",
+                 other_config("attention", args),
+                 {"bound": "tensor", "kernel": "k_attn_fwd_tc3, k_attn_bwd_dkv_tc, k_attn_bwd_dq_tc", "achieved": per,
+                  "peak": peak, "unit": "TFLOP/s", "frac": per / peak, "traffic": traffic, "traffic_source": tsrc,
+                  "peak_source": "dense TF32 rate of a tcgen05 kind::tf32 M=128 N=256 issue loop on this GPU "
+                                 "(amc_tc_peak_tf32), measured in this run",
+                  "algorithmic_flops_per_step": work},
+                 cpu, e2e, 6 * steps, clocks, scaling="weak")
+
+
+def pc_linreg(args, ws, rank, local):
+    """Config 5 through the public SSA path (workloads.LinregSSA): the MSE
+    program compiled by morphism-to-ssa / ssa-vjp, one traced step, then
+    ssa-realize/ctx replays with an in-place gradient step.  Rows are
+    sharded; at N > 1 each replay's gradient is summed over the ranks in rank
+    order before the step (lr / N: the mean over all rows)."""
     import ctypes as C
-    rt = _cudart()
-    rt.cudaMemcpy.restype = C.c_int
-    rc = rt.cudaMemcpy(C.c_void_p(dst), C.c_void_p(src), C.c_size_t(nbytes), 3)  # device to device
-    if rc:
-        raise RuntimeError(f"cudaMemcpy failed {rc}")
-
-
-def cudart_copy_d2h(dst: int, src: int, nbytes: int):
-    import ctypes as C
-    rt = _cudart()
-    rt.cudaMemcpy.restype = C.c_int
-    rc = rt.cudaMemcpy(C.c_void_p(dst), C.c_void_p(src), C.c_size_t(nbytes), 2)
-    if rc:
-        raise RuntimeError(f"cudaMemcpy failed {rc}")
-
-
-# ---------------------------------------------------------------------------- other workloads (per-config measurement)
-def bench_other(args, ws, rank, local):
     import numpy as np
     import torch
     import amcuda as am
+    from amcuda import _abi as A
     from amcuda import workloads as W
     from amcuda.dist import allreduce_fixed_order
-    am.init(local)
-    torch.cuda.set_device(local)
-    stream = torch.cuda.Stream()
-    torch.cuda.set_stream(stream)
+    stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
-    hbm, bf16, kind = peaks()
-    wl = args.workload
-    if wl == "fused":
-        xm, ym = W.c1_inputs_morph(args.dtype)
-        plan = am.Plan(W.c1_tree(xm, ym))
-        run = lambda: plan.execute(sptr)
-        esz = 8 if args.dtype == "f64" else 4
-        work = 2 * (1 << 19) * esz + 1024 * esz
-        unit, bound, metric = "GB/s", "hbm", f"fused view+map+reduce realize GB/s ({args.dtype})"
-        flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-        pre = lambda: flush.fill_(1)
-        cfg = other_config(wl, args)
-        launches = plan.stats()["launches"]
-    elif wl == "linreg":
-        n, d = args.rows, 256
-        X, y, _ = W.c5_inputs_torch(n, d)
-        w = torch.zeros(d, dtype=torch.float64, device="cuda")
+    n, d = args.rows, 256
+    X_t, y_t = W.c5_shard_torch(n, d, rank)
+    xb, yb = device_buffer_from(X_t, "f64"), device_buffer_from(y_t, "f64")
+    del X_t, y_t
+    _release()
+    Xm = am.Concrete(None, (n, d), dtype="f64", dev=xb)
+    ym = am.Concrete(None, (n, 1), dtype="f64", dev=yb)
+    hook = None
+    if ws > 1:
+        def hook(dw):
+            t_ = torch.as_tensor(CudaView(dw._dev.devptr() + 8 * dw.offset, d), device="cuda")
+            allreduce_fixed_order(t_)
+    steps_total = args.warmup + max(args.steps, 64) + 64
+    tr = W.LinregSSA(Xm, ym, np.zeros(d), 0.1 / ws, stream=sptr, max_steps=steps_total + 16, grad_hook=hook)
+    tr.trace()
+    tr.step()     # compiles the replay plan
+    work = n * d * 8 + n * 8
+    ms, steps, clocks = time_steps(tr.step, args.steps, args.warmup, stream, local, ws, min_region_s=0.08,
+                                   max_steps=64)
+    t = max_over_ranks(ws, sum(ms))
+    hbm, _, kind = peaks()
+    per = work / (sum(ms) / len(ms) / 1e3) / 1e9
+    replay_launches = tr.replay_launches()
+    # the hand-fused kernels of the same step on the same data (amc_linreg_step), for comparison
+    direct = None
+    if ws == 1:
+        w_ = torch.zeros(d, dtype=torch.float64, device="cuda")
         npart = W.linreg_partials_count(n, d)
         part = torch.empty(npart * (d + 1), dtype=torch.float64, device="cuda")
         gl = torch.empty(d + 1, dtype=torch.float64, device="cuda")
         loss = torch.empty(1, dtype=torch.float64, device="cuda")
-        N_total = n * ws
+        lib = A.load()
 
-        def run():
-            W.linreg_partials(X, y, w, part, N_total)
-            W.linreg_reduce(part, npart, d, gl)
-            if ws > 1:
-                # the grad+loss row crosses the row shards: rank-ordered all-reduce
-                allreduce_fixed_order(gl)
-            W.linreg_update(w, gl, N_total, 0.1, loss)
-        work = n * d * 8 + n * 8
-        unit, bound, metric = "GB/s", "hbm", "linear-regression step (fused pass over X) GB/s"
-        pre = lambda: None
-        cfg = other_config(wl, args)
-        launches = 3
-    elif wl == "attention":
-        B, H, S, D = args.batch or 16, 16, 2048, 64
-        q, k, v = (torch.from_numpy(W.normal(W.seed_of(4, j), B * H * S * D).astype(np.float32)).cuda().view(B, H, S, D)
-                   for j in range(3))
-        do = torch.from_numpy(W.normal(W.seed_of(4, 3), B * H * S * D).astype(np.float32)).cuda().view(B, H, S, D)
-        o = torch.empty_like(q)
-        lse = torch.empty((B, H, S), dtype=torch.float32, device="cuda")
-        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        def direct_step():
+            A.check(lib.amc_linreg_step(C.c_void_p(xb.devptr()), C.c_void_p(yb.devptr()), C.c_void_p(w_.data_ptr()),
+                                        n, d, C.c_double(0.1), C.c_void_p(part.data_ptr()),
+                                        C.c_void_p(gl.data_ptr()), C.c_void_p(loss.data_ptr()), C.c_void_p(sptr)))
+        dms, dsteps, _ = time_steps(direct_step, args.steps, args.warmup, stream, local, 1)
+        direct = {"value": work / (sum(dms) / len(dms) / 1e3) / 1e9, "unit": "GB/s",
+                  "ms_per_step": sum(dms) / len(dms), "steps": dsteps,
+                  "path": "amc_linreg_step: the hand-fused partials, reduce and update kernels on the same X, y"}
+        del part
+    e2e = None
+    if not args.no_e2e:
+        Xh = torch.empty(n * d, dtype=torch.float64, pin_memory=True)
+        yh = torch.empty(n, dtype=torch.float64, pin_memory=True)
+        cudart_copy(Xh.data_ptr(), xb.devptr(), 8 * n * d, 2)
+        cudart_copy(yh.data_ptr(), yb.devptr(), 8 * n, 2)
+        wh = torch.empty(d, dtype=torch.float64, pin_memory=True)
+        lh = torch.empty(1, dtype=torch.float64, pin_memory=True)
+        from amcuda.realize import device_buffer_of
+        wbuf = device_buffer_of(tr.w)
+        sp = C.c_void_p(sptr)
 
-        def run():
-            W.attention_fwd(q, k, v, o, lse, 1.0 / 8.0)
-            W.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, 1.0 / 8.0)
-        # algorithmic: forward 2 GEMMs (Q K^T, P V), backward 4 (dV, dP, dQ, dK)
-        work = 12.0 * B * H * S * S * D
-        unit, bound, metric = "TFLOP/s", "tensor", "attention forward + backward TFLOP/s"
-        pre = lambda: None
-        cfg = other_config(wl, args)
-        launches = 6   # forward: V^T, K rounding, kernel; backward: pre-pass, dK/dV, dQ
-    elif wl == "conv":
-        N = args.batch or 64
-        x = torch.from_numpy(W.normal(W.seed_of(3, 0), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
-        wt = torch.from_numpy((W.normal(W.seed_of(3, 1), 64 * 64 * 9) * math.sqrt(2 / 576)).astype(np.float32)).cuda().view(64, 64, 3, 3)
-        dy = torch.from_numpy(W.normal(W.seed_of(3, 2), N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
-        yy, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(wt)
+        def step():
+            A.call("amc_buf_upload_async", xb.handle, C.c_void_p(Xh.data_ptr()), 8 * n * d, 0, sp)
+            A.call("amc_buf_upload_async", yb.handle, C.c_void_p(yh.data_ptr()), 8 * n, 0, sp)
+            tr.step()
+            A.call("amc_buf_download_async", wbuf.handle, C.c_void_p(wh.data_ptr()), 8 * d, 0, sp)
+            A.call("amc_buf_download_async", tr._losses.handle, C.c_void_p(lh.data_ptr()), 8, 8 * (tr.steps - 1), sp)
+        n_e = 4
+        e_ms = max_over_ranks(ws, time_e2e(step, n_e, stream))
+        e2e = {"value": ws * work * n_e / (e_ms / 1e3) / 1e9, "unit": "GB/s", "h2d_bytes_per_step": 8 * n * d + 8 * n,
+               "d2h_bytes_per_step": 8 * d + 8, "steps": n_e,
+               "path": "X and y uploaded from pinned memory into the program's constants (amc_buf_upload_async), "
+                       "one ssa-realize/ctx replay + gradient step, w and the loss read back, one stream"}
+        del Xh, yh
+    losses = tr.losses()
+    cpu = cpu_other("linreg", "f64") if rank == 0 and ws == 1 and not args.no_cpu else None
+    traffic, tsrc = traffic_of("linreg")
+    out = entry(_METRIC["linreg"], ws * work * steps / (t / 1e3) / 1e9, "GB/s", t / steps, steps, "f64",
+                other_config("linreg", args),
+                {"bound": "hbm", "kernel": "k_rowpass<double,8,FWD,ACC> (the GEMV pair) + its partial sum",
+                 "achieved": per, "peak": hbm, "unit": "GB/s", "frac": per / hbm, "traffic": traffic,
+                 "traffic_source": tsrc, "peak_source": kind + " hbm_gbs (a copy: read + write)",
+                 "algorithmic_bytes_per_step": work},
+                cpu, e2e, replay_launches * steps, clocks, scaling="weak",
+                direct_kernel=direct, loss_first=float(losses[0]), loss_last=float(losses[-1]),
+                steps_trained=int(tr.steps))
+    del tr, Xm, ym, xb, yb
+    _release()
+    return out
 
-        def run():
-            W.conv2d_fwd(x, wt, yy)
-            W.conv2d_dgrad(dy, wt, dx)
-            W.conv2d_wgrad(x, dy, dw)
-            if ws > 1:
-                # dW sums over the batch shards: fixed-order all-reduce.  It is
-                # not overlapped with the next pass: NCCL's kernel would hold SMs
-                # that the one-CTA-per-SM conv kernels wait for (measured slower).
-                allreduce_fixed_order(dw)
-        work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
-        unit, bound, metric = "TFLOP/s", "tensor", "conv2d forward + data gradient + weight gradient TFLOP/s"
-        pre = lambda: None
-        cfg = other_config(wl, args)
-        launches = 6   # 2 x (weights, kernel) + weight-gradient kernel + reduce
-    else:
-        raise SystemExit(f"unknown workload {wl}")
-    for _ in range(args.warmup):
-        pre()
-        run()
-    torch.cuda.synchronize()
-    barrier(ws)
-    clk = Clocks(local)
-    # Steps are enqueued back to back; each step's events bracket its own work
-    # on the stream.  The L2 flush (where there is one) runs between them, so
-    # the host's launch latency overlaps device work instead of being timed.
-    evs = []
-    for _ in range(args.steps):
-        pre()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        run()
-        b.record(stream)
-        evs.append((a, b))
-    torch.cuda.synchronize()
-    ms = [a.elapsed_time(b) for a, b in evs]
-    clocks = clk.stop()
-    t = max_over_ranks(ws, sum(ms))
-    per = work / (sum(ms) / len(ms) / 1e3)
-    cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu:
-        r = cpu_other(wl, args.dtype)
-        if r:
-            cpu = {"value": r[0], "unit": r[1], "cores": 1, "kind": "port", "sample": r[2]}
-    scale = 1e9 if unit == "GB/s" else 1e12
-    if bound == "hbm":
-        peak, peak_source = hbm, kind + " hbm_gbs"
-    else:
-        # TF32 denominator measured now, on this GPU, by the library's tcgen05 probe
-        peak = W.tc_peak_tf32(4000)
-        peak_source = (f"tcgen05 kind::tf32 M=128 N=256 issue loop on this GPU (amc_tc_peak_tf32); "
-                       f"{kind} bf16/2 = {bf16 / 2.0:.1f} for context")
-    if rank == 0:
-        print(json.dumps({
-            "metric": metric, "value": ws * work * args.steps / (t / 1e3) / scale, "unit": unit, "n_gpus": ws,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": args.dtype if wl == "fused" else ("f64" if wl == "linreg" else "f32"),
-            "data": "synthetic", "config": cfg,
-            "roofline": {"bound": bound, "achieved": per / scale, "peak": peak, "unit": unit, "frac": per / scale / peak,
-                         "traffic": None,
-                         "peak_source": peak_source},
-            "cpu_baseline": cpu, "gpu_launches": launches * args.steps, "clocks": clocks}))
+
+PC_FUNCS = {"fused": pc_fused, "conv": pc_conv, "attention": pc_attention, "linreg": pc_linreg}
+
+
+def bench_one(args, ws, rank, local, wl, dtype):
+    import amcuda as am
+    import torch
+    am.init(local)
+    torch.cuda.set_device(local)
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
+    if wl == "fused":
+        return pc_fused(args, ws, rank, local, dtype)
+    return PC_FUNCS[wl](args, ws, rank, local)
 
 
 def main():
@@ -708,15 +903,16 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="amcuda", choices=["amcuda", "reference"])
-    ap.add_argument("--workload", default="filterbank", choices=["filterbank", "fused", "linreg", "attention", "conv"])
+    ap.add_argument("--workload", default="all", choices=["all", "filterbank", "fused", "linreg", "attention", "conv"])
     ap.add_argument("--signals", type=int, default=64)
     ap.add_argument("--samples", type=int, default=1 << 24)
     ap.add_argument("--rows", type=int, default=1 << 22)
     ap.add_argument("--batch", type=int, default=None,
                     help="per-GPU batch: default 16 (attention, config 4) or 64 (conv, config 3)")
-    ap.add_argument("--dtype", default="f64")
+    ap.add_argument("--dtype", default="f64", help="config 1's dtype with --workload fused")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true", help="the headline alone")
     ap.add_argument("--ref-procs", type=int, default=None,
                     help="processes of the reference arm (default: one per host core)")
     args = ap.parse_args()
@@ -725,10 +921,26 @@ def main():
     try:
         if args.impl == "reference":
             reference_arm(args, ws, rank)
-        elif args.workload == "filterbank":
-            bench_filterbank(args, ws, rank, local)
+        elif args.workload in ("all", "filterbank"):
+            out = bench_filterbank(args, ws, rank, local)
+            if args.workload == "all" and not args.no_per_config:
+                import torch
+                stream = torch.cuda.Stream()
+                torch.cuda.set_stream(stream)
+                per = {}
+                for name, wl, dt in PER_CONFIG:
+                    per[name] = pc_fused(args, ws, rank, local, dt) if wl == "fused" else PC_FUNCS[wl](args, ws, rank,
+                                                                                                     local)
+                    _release()
+                out["per_config"] = per
+            if rank == 0:
+                print(json.dumps(out))
         else:
-            bench_other(args, ws, rank, local)
+            e = bench_one(args, ws, rank, local, args.workload, args.dtype)
+            if rank == 0:
+                e.update({"n_gpus": ws, "warmup": args.warmup, "higher_is_better": True, "vs_baseline": None,
+                          "data": "synthetic"})
+                print(json.dumps(e))
     finally:
         if ws > 1 and args.impl != "reference":
             import torch.distributed as dist
