@@ -470,7 +470,9 @@ def ssa_realize_ctx(ctx, prog: SSAProgram, stream=None) -> list:
     the arena buffers themselves, as the reference returns its pool vectors:
     read them before the next replay overwrites them.  A constant rewritten
     through host_changed() makes the next call compile the plan again.
-    `stream` (a CUDA stream pointer) orders the replay's launches."""
+    The compiling call also captures the plan's launches into a CUDA graph,
+    which every later replay launches as one.  `stream` (a CUDA stream pointer) orders the replay's
+    launches."""
     from .context import context_stats, realize_ctx_many, replay_plan
     from .realize import Plan
     trace = context_stats(ctx)["mode"] == "trace"
@@ -493,6 +495,8 @@ def ssa_realize_ctx(ctx, prog: SSAProgram, stream=None) -> list:
         plan = Plan(lazy, ctx) if lazy else None
         if plan is not None:
             plan.execute(stream)
+            if plan.stats()["launches"] > 1:
+                plan.capture_graph(stream)   # later replays launch one graph (captured, not run, here)
         entry = (plan, trees, _const_devs(prog))
         cache[key] = entry
     else:

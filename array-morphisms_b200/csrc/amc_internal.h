@@ -221,6 +221,11 @@ struct RowPassArgs {
   // set by rowpass_prepare.
   int32_t closed, ck, c_leaf, c2_leaf, y_leaf, c2_used;   // *_leaf -1: the constant
   double c_const, c2_const, y_const;
+  // A full sum of (p - y2)^2 over the rows taken in the same pass (the MSE
+  // loss's reduction; closed form only): each CTA adds its rows' values into
+  // partials[grid * d + CTA]; rsum_y_leaf -1: the constant rsum_y_const.
+  int32_t rsum, rsum_y_leaf;
+  double rsum_y_const;
   void* out; int32_t out_dtype; int32_t _p4; int64_t sout;
   double alpha, beta;
   double* partials;
@@ -233,6 +238,13 @@ constexpr int64_t kRowPassMinRows = (int64_t)1 << 14;
 constexpr int64_t kRowPassMinDot = (int64_t)1 << 16;
 int rowpass_grid(int64_t rows);
 size_t rowpass_scratch_bytes(const RowPassArgs& a);
+// The row sum's second pass: out = sum of the n partials (fixed order),
+// divided by `div` when div != 0 (a mean), stored as out_dtype.
+int launch_rowsum_finish(const double* partials, int n, void* out, int out_dtype, double div, cudaStream_t s);
+// The number of CTAs that write partial rows for `a`.
+int rowpass_ctas(const RowPassArgs& a);
+// Whether the GEMV pair `a` runs the TMA pipeline (contiguous rows).
+bool rowpass_pair_tma(const RowPassArgs& a);
 int rowpass_launches(const RowPassArgs& a);
 int launch_rowpass(const RowPassArgs& a, cudaStream_t s);
 // Once per planned launch: finds a closed form of the row program.

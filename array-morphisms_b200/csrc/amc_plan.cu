@@ -184,6 +184,12 @@ struct Builder {
   // this buffer would run before the buffer is written (watch_hit).
   uint64_t watch_buf = 0;
   bool watch_hit = false;
+  // The GEMV pair planned last: its launch arguments (shared with its step,
+  // which reads them at launch), the buffer of X w and the partial sums.
+  struct {
+    std::shared_ptr<RowPassArgs> args;
+    uint64_t r0 = 0, part = 0;
+  } pair;
   // The most recent GEMM step, while its result may still take an epilogue.
   struct {
     size_t step = 0;
@@ -738,9 +744,16 @@ struct Builder {
     a.R = numel(kr, a.rshape);
     fill_prog(a.prog, e.prog, e.leaves);
     View o;
-    rc = new_slot(nd.dtype, nd.rank, nd.shape, reads_of(e.leaves), o);
+    std::vector<uint64_t> reads = reads_of(e.leaves);
+    if (pair.args) reads.push_back(pair.part);   // a folded row sum reads the pair's partials
+    rc = new_slot(nd.dtype, nd.rank, nd.shape, reads, o);
     if (rc) return rc;
     a.out = ptr_of(o.buf);
+    if (try_fold_row_sum(a, e, o, op)) {
+      out = Val();
+      out.view = o;
+      return AMC_OK;
+    }
     if (try_fir(a, e)) {
       out = Val();
       out.view = o;
@@ -1258,11 +1271,67 @@ struct Builder {
     a.partials = (double*)ptr_of(part.buf);
     a.out = ptr_of(dw.buf); a.out_dtype = fj.dtype; a.sout = 1;
     rowpass_prepare(a);
-    plan->steps.push_back([a](cudaStream_t s) { return launch_rowpass(a, s); });
+    auto ap = std::make_shared<RowPassArgs>(a);
+    plan->steps.push_back([ap](cudaStream_t s) { return launch_rowpass(*ap, s); });
     plan->launches += rowpass_launches(a);
+    pair.args = ap;
+    pair.r0 = r0.buf;
+    pair.part = part.buf;
     memo[j] = Val();
     memo[j]->view = dw;
     return AMC_OK;
+  }
+
+  // A full sum or mean of (X w - y)^2 over the rows of the GEMV pair planned
+  // last (the MSE loss): the pair's pass accumulates it as well, and this
+  // node only adds the pair's per-CTA partials.  The program must be the
+  // square of one residual whose first operand is X w read row by row.
+  bool try_fold_row_sum(const ReduceArgs& r, const Val& e, const View& out, int op) {
+    if (!pair.args || !pair.args->closed || !rowpass_pair_tma(*pair.args) || (op != AMC_RED_SUM && op != AMC_RED_MEAN))
+      return false;
+    RowPassArgs& a = *pair.args;
+    if (a.rsum || r.O != 1 || r.R != a.rows || r.rrank != 1 || out.dtype != AMC_F64 || r.src_dtype != AMC_F64 ||
+        !r.prog.all_float)
+      return false;
+    // program: MUL(S, S), S = SUB(LOAD rl, v) (CVT f64 already dropped)
+    const DProg& P = r.prog;
+    if (P.n != 7 || P.code[2].op != AMC_OP_SUB || P.code[5].op != AMC_OP_SUB || P.code[6].op != AMC_OP_MUL) return false;
+    for (int k = 0; k < 3; ++k)
+      if (P.code[k].op != P.code[3 + k].op || P.code[k].a != P.code[3 + k].a ||
+          (P.code[k].op == AMC_OP_CONST && P.code[k].imm != P.code[3 + k].imm))
+        return false;
+    if (P.code[0].op != AMC_OP_LOAD) return false;
+    const int rl = P.code[0].a;
+    if (e.leaves[rl].buf != pair.r0 || e.leaves[rl].offset != 0 || (a.rows > 1 && r.leaf_r[rl][0] != 1)) return false;
+    int yl = -1;
+    double yc = 0.0;
+    if (P.code[1].op == AMC_OP_CONST) {
+      yc = P.code[1].imm;
+    } else if (P.code[1].op == AMC_OP_LOAD && P.code[1].a != rl) {
+      // the y leaf joins the pair's row leaves (strides[0]: along the rows)
+      DLeaf L = r.leaf_o[P.code[1].a];
+      L.strides[0] = r.leaf_r[P.code[1].a][0];
+      for (int k = 1; k < AMC_MAX_RANK; ++k) L.strides[k] = 0;
+      for (int l = 0; l < a.nleaf; ++l)
+        if (a.leaf[l].ptr == L.ptr && a.leaf[l].dtype == L.dtype && a.leaf[l].strides[0] == L.strides[0]) yl = l;
+      if (yl < 0) {
+        if (a.nleaf >= kMaxLeaves) return false;
+        yl = a.nleaf;
+        a.leaf[a.nleaf++] = L;
+      }
+    } else {
+      return false;
+    }
+    a.rsum = 1;
+    a.rsum_y_leaf = yl;
+    a.rsum_y_const = yc;
+    const double* partials = (const double*)ptr_of(pair.part) + (size_t)rowpass_ctas(a) * a.d;
+    const int n = rowpass_ctas(a);
+    void* o = ptr_of(out.buf);
+    const double div = op == AMC_RED_MEAN ? (double)r.R : 0.0;
+    plan->steps.push_back([partials, n, o, div](cudaStream_t s) { return launch_rowsum_finish(partials, n, o, AMC_F64, div, s); });
+    plan->launches += 1;
+    return true;
   }
 
   int node_gemm(int idx, Val& out) {

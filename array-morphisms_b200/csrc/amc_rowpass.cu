@@ -591,6 +591,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) k_gemv_pair_tma(const __grid_
   if (warp == kPairCompute) {
     // ---------------------------------------------------------------- producer
     if (lane != 0) return;
+    const uint64_t policy = tc::l2_policy_evict_first();   // X is read once
     long long issued = 0;
     for (long long s = 0; s < nt && !*abort_flag; ++s) {
       const int st = (int)(s % ns);
@@ -609,7 +610,8 @@ __global__ void __launch_bounds__(kPairThreads, 1) k_gemv_pair_tma(const __grid_
         }
         const uint32_t bytes = (uint32_t)((long long)cr * D * sizeof(T));
         tc::mbar_expect_tx(bar, bytes);
-        tc::bulk_load_1d(xs + (size_t)st * TILE + (size_t)c * CROWS * D, src + (size_t)c * CROWS * D, bytes, bar);
+        tc::bulk_load_1d_hint(xs + (size_t)st * TILE + (size_t)c * CROWS * D, src + (size_t)c * CROWS * D, bytes, bar,
+                              policy);
       }
       ++issued;
     }
@@ -632,6 +634,7 @@ __global__ void __launch_bounds__(kPairThreads, 1) k_gemv_pair_tma(const __grid_
   const bool owner = (lane & 7) == 0;
   double lv[kMaxLeaves];
   if (owner && nt > 0 && row0 + q_own < rows_of(0)) load_row_leaves(a, rb + row0 + q_own, lv);
+  double rsum = 0.0;    // the row sum of this owner lane's rows, in row order
   bool ok = true;
   for (long long s = 0; s < nt && !*abort_flag; ++s) {
     const int st = (int)(s % ns);
@@ -662,6 +665,10 @@ __global__ void __launch_bounds__(kPairThreads, 1) k_gemv_pair_tma(const __grid_
     if (owner && row0 + q_own < nr) {
       const double pr = fwd_store(a, r, sum);
       ev = row_value<true, EV>(a, r, pr, lv);
+      if (EV == 3 && a.rsum) {
+        const double t = __dsub_rn(pr, a.rsum_y_leaf < 0 ? a.rsum_y_const : leaf_sel(lv, a.rsum_y_leaf));
+        rsum = __dadd_rn(rsum, __dmul_rn(t, t));
+      }
     }
     // the next tile's leaves, while this tile's rows accumulate
     if (owner && s + 1 < nt && row0 + q_own < rows_of(s + 1)) load_row_leaves(a, r + kPairRows, lv);
@@ -678,15 +685,27 @@ __global__ void __launch_bounds__(kPairThreads, 1) k_gemv_pair_tma(const __grid_
   // warp waited for every tile's copy)
   asm volatile("bar.sync 1, %0;" ::"r"(kPairCompute * 32) : "memory");
   if (!*abort_flag) {
-    double* red = (double*)pair_sm;   // [kPairCompute][D]
+    double* red = (double*)pair_sm;   // [kPairCompute][D], then [kPairCompute] row sums
 #pragma unroll
     for (int j = 0; j < KPL; ++j) red[warp * D + lane + 32 * j] = acc[j];
+    if (EV == 3 && a.rsum) {
+      // the 4 owner lanes' sums in row order (lanes 0, 8, 16, 24), then the warps in order
+      const double r8 = __shfl_sync(kFull, rsum, 8), r16 = __shfl_sync(kFull, rsum, 16),
+                   r24 = __shfl_sync(kFull, rsum, 24);
+      if (lane == 0) red[kPairCompute * D + warp] = ((rsum + r8) + r16) + r24;
+    }
     asm volatile("bar.sync 1, %0;" ::"r"(kPairCompute * 32) : "memory");
     for (int k = threadIdx.x; k < D; k += kPairCompute * 32) {
       double t = red[k];
 #pragma unroll
       for (int w = 1; w < kPairCompute; ++w) t += red[w * D + k];
       a.partials[(long long)blockIdx.x * D + k] = t;
+    }
+    if (EV == 3 && a.rsum && threadIdx.x == 0) {
+      double t = red[kPairCompute * D];
+#pragma unroll
+      for (int w = 1; w < kPairCompute; ++w) t += red[kPairCompute * D + w];
+      a.partials[(long long)gridDim.x * D + blockIdx.x] = t;
     }
   }
 }
@@ -761,7 +780,8 @@ __global__ void __launch_bounds__(kRowBlock) k_dot_partials(const TA* __restrict
 // columns and 8 groups of rows; group g adds rows g, g+8, ... ascending, then
 // the 8 group sums are added pairwise in index order.  alpha/beta as k_gemm.
 __global__ void __launch_bounds__(256) k_rowpass_reduce(const double* __restrict__ partials, int n, int d, void* out,
-                                                        int out_dtype, long long sout, double alpha, double beta) {
+                                                        int out_dtype, long long sout, double alpha, double beta,
+                                                        double div = 0.0) {
   __shared__ double red[8][33];
   const int l = threadIdx.x & 31, g = threadIdx.x >> 5;
   const int k = blockIdx.x * 32 + l;
@@ -774,6 +794,7 @@ __global__ void __launch_bounds__(256) k_rowpass_reduce(const double* __restrict
     double v = ((red[0][l] + red[1][l]) + (red[2][l] + red[3][l])) + ((red[4][l] + red[5][l]) + (red[6][l] + red[7][l]));
     if (alpha != 1.0) v = __dmul_rn(alpha, v);
     if (beta != 0.0) v = __dadd_rn(v, __dmul_rn(beta, ld_any(out, out_dtype, k * sout)));
+    if (div != 0.0) v = __ddiv_rn(v, div);
     store_to(out, out_dtype, k * sout, v);
   }
 }
@@ -813,7 +834,7 @@ int launch_pair_tma(const RowPassArgs& a, int grid, cudaStream_t s) {
   // the stages also hold the final warp reduction (kPairCompute x d doubles),
   // which is at most a quarter of the 8 stages a 32-column f32 tile gets
   const size_t stages = (size_t)ns * stage;
-  static_assert(kPairCompute * 32 * sizeof(double) <= 8 * kPairRows * 32 * sizeof(float), "reduction fits the stages");
+  static_assert(kPairCompute * 33 * sizeof(double) <= 8 * kPairRows * 32 * sizeof(float), "reduction fits the stages");
   const size_t smem = stages + (kPairChunks + 1) * ns * 8 + 16;
   const int ki = KPL == 1 ? 0 : KPL == 2 ? 1 : KPL == 4 ? 2 : 3;
   int rc = smem_attr_once(k_gemv_pair_tma<T, KPL, EV>, (int)smem, g_pair_smem_done[sizeof(T) == 8][ki][EV]);
@@ -900,7 +921,22 @@ int rowpass_grid(int64_t rows) {
 size_t rowpass_scratch_bytes(const RowPassArgs& a) {
   if (a.dot) return (size_t)rowpass_grid(a.rows) * sizeof(double);
   if (!a.acc) return 0;
-  return (size_t)rowpass_grid(a.rows) * (size_t)a.d * sizeof(double);
+  // the GEMV pair also keeps one row-sum partial per CTA after the d columns
+  return (size_t)rowpass_grid(a.rows) * (size_t)(a.d + (a.fwd ? 1 : 0)) * sizeof(double);
+}
+
+bool rowpass_pair_tma(const RowPassArgs& a) { return pair_tma_ok(a); }
+
+int rowpass_ctas(const RowPassArgs& a) {
+  int grid = rowpass_grid(a.rows);
+  if (pair_tma_ok(a) && grid > num_sms()) grid = num_sms();
+  return grid;
+}
+
+int launch_rowsum_finish(const double* partials, int n, void* out, int out_dtype, double div, cudaStream_t s) {
+  k_rowpass_reduce<<<1, 256, 0, s>>>(partials, n, 1, out, out_dtype, 1, 1.0, 0.0, div);
+  AMC_CUDA(cudaGetLastError());
+  return AMC_OK;
 }
 
 int launch_rowpass(const RowPassArgs& a, cudaStream_t s) {
@@ -911,8 +947,9 @@ int launch_rowpass(const RowPassArgs& a, cudaStream_t s) {
     return fail(AMC_ERR_INVALID, "row pass: the row program does not read the forward product");
   if (fault_injected("launch")) return fail(AMC_ERR_INJECTED, "row pass: injected launch failure (AMC_FAULT=launch)");
   // the CTAs that write partial rows (the reduce adds exactly these)
-  int grid = rowpass_grid(a.rows);
-  if (pair_tma_ok(a) && grid > num_sms()) grid = num_sms();
+  const int grid = rowpass_ctas(a);
+  if (a.rsum && !(a.closed && pair_tma_ok(a)))
+    return fail(AMC_ERR_INVALID, "row pass: a row sum needs the closed row form on contiguous rows");
   if (a.rows == 0) {
     // an empty contraction: every output is 0 (then alpha/beta)
     if (a.acc || a.dot) {

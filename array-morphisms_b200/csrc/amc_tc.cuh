@@ -70,6 +70,21 @@ __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_
                ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)) : "memory");
 }
 
+// The same copy with an L2 eviction-priority hint: data read once (a stream
+// over a matrix larger than L2) marked evict-first, so it does not push out
+// lines that are read again.  No multicast.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_load_1d_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                                  uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy) : "memory");
+}
+
 // ------------------------------------------------------------------ tensor memory
 // alloc/dealloc are warp-collective; the base address is written to *dst (shared).
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
