@@ -116,6 +116,10 @@ SIGNATURES = {
     "amc_conv2d_dgrad_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
     "amc_conv2d_wgrad_f32": [_P, _P, _P] + [_I32] * 11 + [_P],
     "amc_tc_peak_tf32": [_I32, _I32, _I32, _I32, _P, _P],
+    "amc_peer_group_create": [_I32, _I32, _I64, _PU64, _P],
+    "amc_peer_group_open": [_U64, _P],
+    "amc_peer_sum": [_U64, _P, _I64, _I32, _P, _P],
+    "amc_peer_group_destroy": [_U64],
     "amc_probe_bounded_wait": [_I32, _I32, _P],
 }
 

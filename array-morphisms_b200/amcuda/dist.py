@@ -6,10 +6,11 @@ across ranks:
   - independent items (filter-bank signals, attention batch entries, conv
     images for Y and dX) need no exchange;
   - a reduction that crosses the batch axis (the linear-regression gradient,
-    the conv weight gradient) is combined with a deterministic all-reduce:
-    an all-gather of each rank's partial followed by one fixed-order sum over
-    the rank axis, so
-    results do not depend on the collective's internal reduction order.
+    the conv weight gradient) is combined with a deterministic sum in rank
+    order, so results do not depend on a collective's internal reduction
+    order: PeerSum does it through NVLink peer memory in the library's own
+    kernels; allreduce_fixed_order is the same sum over torch.distributed
+    (an all-gather, then the rank-axis sum), for any backend.
 """
 from __future__ import annotations
 
@@ -60,6 +61,57 @@ def allreduce_fixed_order(t, group=None, async_op: bool = False):
         work = dist.all_gather(list(buf.unbind(0)), flat, group=group, async_op=async_op)
     pending = PendingReduce(t, buf, work if async_op else None)
     return pending if async_op else pending.wait()
+
+
+class PeerSum:
+    """The fixed-order sum over the ranks of one node through NVLink peer
+    memory (amc_peer_sum): each rank pushes its vector into every rank's
+    memory and sums all ranks' copies in rank order on its own GPU, in one
+    pair of launches and no NCCL call.  Ranks are added in rank order,
+    accumulated in double, so the result is bit-identical on every rank and
+    every run.  Needs one process per GPU
+    on the same node with peer access between the GPUs; `max_elems` bounds
+    the vectors (8-byte elements).  close() is collective."""
+
+    def __init__(self, max_elems: int, group=None):
+        import ctypes as C
+        import torch.distributed as dist
+        from . import _abi as A
+        from .realize import _ensure_init
+        _ensure_init()
+        self.group = group
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        h = C.c_uint64(0)
+        handle = (C.c_char * 64)()
+        A.call("amc_peer_group_create", self.rank, self.world, int(max_elems), C.byref(h), handle)
+        self.handle = h.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        blob = b"".join(handles)
+        A.call("amc_peer_group_open", self.handle, C.c_char_p(blob))
+
+    def sum_(self, t, stream=None):
+        """In place: t <- sum over ranks, in rank order (f32 / f64 CUDA tensor)."""
+        import ctypes as C
+        import torch
+        from . import _abi as A
+        if not t.is_contiguous():
+            raise ValueError("PeerSum: a contiguous tensor")
+        dt = {torch.float32: A.F32, torch.float64: A.F64}[t.dtype]
+        s = stream if stream is not None else torch.cuda.current_stream().cuda_stream
+        A.call("amc_peer_sum", self.handle, C.c_void_p(t.data_ptr()), t.numel(), dt, C.c_void_p(t.data_ptr()),
+               C.c_void_p(s))
+        return t
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        from . import _abi as A
+        if self.handle:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)   # no rank still pushes into a buffer about to be freed
+            A.call("amc_peer_group_destroy", self.handle)
+            self.handle = 0
 
 
 class ShardedLinearRegression:

@@ -292,6 +292,7 @@ int attention_check_error();
 int attention_bwd_check_error();
 int conv_check_error();
 int rowpass_check_error();
+int dist_check_error();
 int device_check_errors();  // all kernels' bounded-wait flags
 
 }  // namespace amc

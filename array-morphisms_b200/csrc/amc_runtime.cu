@@ -153,6 +153,8 @@ int device_check_errors() {
   if (rc) return rc;
   rc = rowpass_check_error();
   if (rc) return rc;
+  rc = dist_check_error();
+  if (rc) return rc;
   return conv_check_error();
 }
 

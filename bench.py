@@ -464,6 +464,8 @@ def time_steps(run, steps, warmup, stream, local, ws, pre=None, min_region_s: fl
         torch.cuda.synchronize()
         est = max(a.elapsed_time(b) / 1e3, 1e-6)
         steps = max(steps, min(max_steps, int(math.ceil(min_region_s / est))))
+        # every rank runs the same number of steps (collectives pair up)
+        steps = int(max_over_ranks(ws, float(steps)))
     barrier(ws)
     clk = Clocks(local)
     time.sleep(0.01)
@@ -495,6 +497,30 @@ def time_e2e(step, steps, stream):
     b.record(stream)
     torch.cuda.synchronize()
     return a.elapsed_time(b)
+
+
+def make_rank_sum(ws: int, n: int):
+    """The in-place rank-order sum of an n-element device vector over the
+    ranks: the library's peer-memory kernels (amcuda.dist.PeerSum) when the
+    GPUs reach each other, else allreduce_fixed_order over NCCL."""
+    if ws == 1:
+        return None
+    from amcuda.dist import PeerSum, allreduce_fixed_order
+    try:
+        ps = PeerSum(n)
+    except Exception as e:   # no peer access between these GPUs
+        print(f"bench: peer-memory rank sum unavailable ({e}); using allreduce_fixed_order", file=sys.stderr)
+        return allreduce_fixed_order
+
+    def run(t):
+        return ps.sum_(t)
+    run.peer = ps
+    return run
+
+
+def close_rank_sum(fn):
+    if fn is not None and hasattr(fn, "peer"):
+        fn.peer.close()
 
 
 _TC_PEAK = {}
@@ -682,7 +708,6 @@ def pc_conv(args, ws, rank, local):
     import numpy as np
     import torch
     from amcuda import workloads as W
-    from amcuda.dist import allreduce_fixed_order
     stream = torch.cuda.current_stream()
     N = args.batch or 64
     gen = lambda j, n: W.normal(W.seed_of(3, j), n, start=rank * n if j != 1 else 0)
@@ -690,13 +715,14 @@ def pc_conv(args, ws, rank, local):
     wt = torch.from_numpy((gen(1, 64 * 64 * 9) * math.sqrt(2 / 576)).astype(np.float32)).cuda().view(64, 64, 3, 3)
     dy = torch.from_numpy(gen(2, N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
     yy, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(wt)
+    rank_sum = make_rank_sum(ws, dw.numel())
 
     def run():
         W.conv2d_fwd(x, wt, yy)
         W.conv2d_dgrad(dy, wt, dx)
         W.conv2d_wgrad(x, dy, dw)
         if ws > 1:
-            allreduce_fixed_order(dw)   # dW sums over the batch shards
+            rank_sum(dw)   # dW sums over the batch shards, in rank order
     work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
     ms, steps, clocks = time_steps(run, args.steps, args.warmup, stream, local, ws, min_region_s=0.3, max_steps=4000)
     t = max_over_ranks(ws, sum(ms))
@@ -722,6 +748,7 @@ def pc_conv(args, ws, rank, local):
                                      "dW copied back, one stream"}
     cpu = cpu_other("conv", "f32") if rank == 0 and ws == 1 and not args.no_cpu else None
     traffic, tsrc = traffic_of("conv")
+    close_rank_sum(rank_sum)
     return entry(_METRIC["conv"], ws * work * steps / (t / 1e3) / 1e12, "TFLOP/s", t / steps, steps, "f32",
                  other_config("conv", args),
                  {"bound": "tensor", "kernel": "k_conv3x3_tc, k_conv_wgrad_tc", "achieved": per, "peak": peak,
@@ -795,7 +822,6 @@ def pc_linreg(args, ws, rank, local):
     import amcuda as am
     from amcuda import _abi as A
     from amcuda import workloads as W
-    from amcuda.dist import allreduce_fixed_order
     stream = torch.cuda.current_stream()
     sptr = stream.cuda_stream
     n, d = args.rows, 256
@@ -806,10 +832,17 @@ def pc_linreg(args, ws, rank, local):
     Xm = am.Concrete(None, (n, d), dtype="f64", dev=xb)
     ym = am.Concrete(None, (n, 1), dtype="f64", dev=yb)
     hook = None
+    rank_sum = make_rank_sum(ws, d)
     if ws > 1:
         def hook(dw):
-            t_ = torch.as_tensor(CudaView(dw._dev.devptr() + 8 * dw.offset, d), device="cuda")
-            allreduce_fixed_order(t_)
+            # the gradient sums over the row shards, in rank order
+            if dw._dev is None:   # the traced step's gradient comes back on the host
+                arr = dw.data
+                t_ = torch.from_numpy(arr[dw.offset:dw.offset + d].copy()).cuda()
+                rank_sum(t_)
+                arr[dw.offset:dw.offset + d] = t_.cpu().numpy()
+            else:
+                rank_sum(torch.as_tensor(CudaView(dw._dev.devptr() + 8 * dw.offset, d), device="cuda"))
     steps_total = args.warmup + max(args.steps, 64) + 64
     tr = W.LinregSSA(Xm, ym, np.zeros(d), 0.1 / ws, stream=sptr, max_steps=steps_total + 16, grad_hook=hook)
     tr.trace()
@@ -877,6 +910,7 @@ def pc_linreg(args, ws, rank, local):
                 cpu, e2e, replay_launches * steps, clocks, scaling="weak",
                 direct_kernel=direct, loss_first=float(losses[0]), loss_last=float(losses[-1]),
                 steps_trained=int(tr.steps))
+    close_rank_sum(rank_sum)
     del tr, Xm, ym, xb, yb
     _release()
     return out

@@ -367,6 +367,25 @@ int amc_conv2d_dgrad_f32(const float* dY, const float* W, float* dX, int32_t N, 
 int amc_conv2d_wgrad_f32(const float* X, const float* dY, float* dW, int32_t N, int32_t C, int32_t H, int32_t Wd,
                          int32_t K, int32_t KH, int32_t KW, int32_t SH, int32_t SW, int32_t PH, int32_t PW, void* stream);
 
+/* ---------------------------------------------------------------- multi-GPU
+ * Fixed-order sum over the GPUs of one node (one process per GPU), the
+ * reduction that crosses the batch axis of a sharded workload
+ * (batch-ops.scm:241-254 folds per-element results in index order).  Each
+ * rank creates a group (one device allocation exported by CUDA IPC; its
+ * 64-byte handle is written to handle_out), the host exchanges the handles
+ * (e.g. an all-gather), and every rank opens the group with all `world`
+ * handles in rank order.  amc_peer_sum then replaces out[i] by
+ * sum over ranks q = 0 .. world-1 of rank q's src[i], added in that order in
+ * double: every rank calls it with the same n and dtype in the same order.
+ * Each rank pushes its vector into every rank's memory over NVLink and waits
+ * (bounded; AMC_ERR_TIMEOUT at amc_synchronize when a rank never arrives)
+ * for the others.  Destroy only after every rank finished its last sum (a
+ * host barrier). */
+int amc_peer_group_create(int32_t rank, int32_t world, int64_t max_elems, uint64_t* group, void* handle_out);
+int amc_peer_group_open(uint64_t group, const void* handles);
+int amc_peer_sum(uint64_t group, const void* src, int64_t n, int32_t dtype, void* out, void* stream);
+int amc_peer_group_destroy(uint64_t group);
+
 /* Tensor-core throughput probe (diagnostic; no reference counterpart): one
  * CTA per SM, `warps` (1..4) threads each issue iters x 4 back-to-back
  * tcgen05.mma kind::tf32 products of M=128, N=n (32, 64, 128 or 256), K=8
