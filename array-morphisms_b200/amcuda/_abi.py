@@ -121,6 +121,7 @@ SIGNATURES = {
     "amc_peer_sum": [_U64, _P, _I64, _I32, _P, _P],
     "amc_peer_group_destroy": [_U64],
     "amc_probe_bounded_wait": [_I32, _I32, _P],
+    "amc_colfold_launch_count": [_P],
 }
 
 _lib = None

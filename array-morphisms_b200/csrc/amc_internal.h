@@ -136,6 +136,10 @@ struct ScanArgs {
 };
 int launch_scan(const ScanArgs& a, cudaStream_t s);
 int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scratch_bytes, size_t* scratch_need);
+// The column fold (amc_colfold.cu): launched, or AMC_ERR_UNSUPPORTED when the
+// reduction is not of its kind (nothing launched, no error recorded).
+int launch_colfold(const ReduceArgs& a, cudaStream_t s);
+long long colfold_launch_count();
 
 struct PadArgs {
   int32_t rank, mode;
@@ -292,6 +296,7 @@ int attention_check_error();
 int attention_bwd_check_error();
 int conv_check_error();
 int rowpass_check_error();
+int colfold_check_error();
 int dist_check_error();
 int device_check_errors();  // all kernels' bounded-wait flags
 

@@ -1211,6 +1211,12 @@ int launch_reduce(const ReduceArgs& a, cudaStream_t s, void* scratch, size_t scr
   }
   const bool sumlike = a.op == AMC_RED_SUM || a.op == AMC_RED_MEAN;
   const bool src_float = a.src_dtype == AMC_F32 || a.src_dtype == AMC_F64;
+  // column fold: few outputs adjacent in memory, a program of closed form,
+  // tiles that TMA can move (amc_colfold.cu); else the staged form below
+  if (OT < 8 && ofast && a.orank == 1 && a.rrank == 1) {
+    const int rc = launch_colfold(a, s);
+    if (rc != AMC_ERR_UNSUPPORTED) return rc;
+  }
   // staged form: few outputs, adjacent in memory, small program
   if (OT < 8 && ofast && a.orank == 1 && a.rrank == 1 && a.nleaf >= 1 && a.nleaf <= 2 && a.prog.max_depth <= 3 &&
       a.prog.n > 0) {

@@ -155,6 +155,8 @@ int device_check_errors() {
   if (rc) return rc;
   rc = dist_check_error();
   if (rc) return rc;
+  rc = colfold_check_error();
+  if (rc) return rc;
   return conv_check_error();
 }
 

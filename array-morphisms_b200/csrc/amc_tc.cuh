@@ -289,5 +289,4 @@ int make_tmap_2d_f32_box(CUtensorMap* map, const void* base, uint64_t rows, uint
 enum class TmapSwizzle { kNone, k32, k128, k128Atom32 };
 int make_tmap_2d_f32_swz(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
                          uint32_t box_cols, uint32_t box_rows, TmapSwizzle swizzle);
-
 }  // namespace amc

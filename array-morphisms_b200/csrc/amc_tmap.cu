@@ -6,17 +6,23 @@
 
 namespace amc {
 
-int make_tmap_2d_f32_swz(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
-                         uint32_t box_cols, uint32_t box_rows, TmapSwizzle swizzle) {
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 encoder() {
   static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
   if (!encode) {
     cudaDriverEntryPointQueryResult q;
     void* fn = nullptr;
     cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
-      return fail(AMC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
-    encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess && fn) encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
   }
+  return encode;
+}
+}  // namespace
+
+int make_tmap_2d_f32_swz(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                         uint32_t box_cols, uint32_t box_rows, TmapSwizzle swizzle) {
+  auto encode = encoder();
+  if (!encode) return fail(AMC_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
   if (((uintptr_t)base & 15) || ((pitch_elems * 4) & 15)) return fail(AMC_ERR_INVALID, "tensor map: base or pitch not 16-byte aligned");
   const uint32_t span = swizzle == TmapSwizzle::k32 ? 32 : swizzle == TmapSwizzle::kNone ? 0 : 128;
   // a swizzled box row spans exactly the swizzle width

@@ -405,6 +405,11 @@ int amc_tc_peak_tf32(int32_t n, int32_t warps, int32_t a_tmem, int32_t iters, do
  * Synchronizes the stream. */
 int amc_probe_bounded_wait(int32_t limit, int32_t arrive, void* stream);
 
+/* Launch counter (diagnostic; no reference counterpart): how many column-fold
+ * reductions (adjacent outputs, closed-form element program, TMA tiles) this
+ * process has launched, so tests can tell that path from the staged one. */
+int amc_colfold_launch_count(int64_t* count);
+
 #ifdef __cplusplus
 }
 #endif
