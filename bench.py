@@ -934,10 +934,43 @@ def pc_linreg(args, ws, rank, local):
                  "algorithmic_bytes_per_step": work},
                 cpu, e2e, replay_launches * steps, clocks, scaling="weak",
                 direct_kernel=direct, loss_first=float(losses[0]), loss_last=float(losses[-1]),
-                steps_trained=int(tr.steps))
+                steps_trained=int(tr.steps), blas=blas_lines(args, Xm, n, d, stream, local, ws, hbm))
     close_rank_sum(rank_sum)
     del tr, Xm, ym, xb, yb
     _release()
+    return out
+
+
+def blas_lines(args, Xm, n, d, stream, local, ws, hbm):
+    """morph-matvec X w, morph-matvec X^T r and morph-dot over the config-5 X
+    (blas-exec.scm:260-310) through realize plans, each timed alone on the
+    device-resident X (larger than L2).  GB/s of the algorithmic bytes: X
+    once, plus the vectors."""
+    import amcuda as am
+    from amcuda import workloads as W
+    sptr = stream.cuda_stream
+    w = am.morph_from_numpy(W.normal(W.seed_of(6, 0), d), "f64")
+    r = am.morph_from_numpy(W.normal(W.seed_of(6, 1), n), "f64")
+    flat = am.morph_reshape(Xm, (n * d,))
+    half = n * d // 2
+    v1 = am.morph_slice(flat, (0,), (half,))
+    v2 = am.morph_slice(flat, (half,), (2 * half,))
+    cases = {
+        "matvec": (am.morph_matvec(Xm, w), n * d * 8 + d * 8 + n * 8, f"X w, X {n} x {d} f64"),
+        "matvec_t": (am.morph_matvec(am.morph_transpose(Xm), r), n * d * 8 + n * 8 + d * 8,
+                     f"X^T r, X {n} x {d} f64 (a transposed view)"),
+        "dot": (am.morph_dot(v1, v2), 2 * half * 8 + 8, f"dot of the two halves of X ({half} f64 each)"),
+    }
+    out = {}
+    for name, (tree, work, what) in cases.items():
+        plan = am.Plan(tree)
+        ms, steps, _ = time_steps(lambda: plan.execute(sptr), args.steps, args.warmup, stream, local, ws)
+        t = max_over_ranks(ws, sum(ms) / len(ms))
+        value = work / (t / 1e3) / 1e9
+        out[name] = {"what": what, "value": value, "unit": "GB/s", "ms_per_step": t, "steps": steps,
+                     "frac_of_hbm": value / hbm, "launches_per_step": plan.stats()["launches"],
+                     "algorithmic_bytes": work}
+        del plan
     return out
 
 
