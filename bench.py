@@ -47,9 +47,29 @@ sys.path.insert(0, str(ROOT / "array-morphisms_b200"))
 HBM_FALLBACK = 6650.0
 
 # DRAM bytes per launch of the dominant kernel from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum), with what was captured.
-# None where no capture of the current kernel exists.
-NCU_TRAFFIC: dict = {}
+# (dram__bytes_read.sum + dram__bytes_write.sum, one pass, the full-size
+# workload of the named bench command), with what was captured.  Absent
+# where no capture of the current kernel exists.
+_NCU = "ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum --clock-control none -k regex:{k} -s {s} -c 1 "
+_BENCH = "python bench.py --workload {w} --no-e2e --no-cpu --steps 2 --warmup 3"
+NCU_TRAFFIC: dict = {
+    "filterbank": {"bytes_per_launch": 4.54e9 + 4.23e9,
+                   "source": _NCU.format(k="k_fir_tma", s=3) + _BENCH.format(w="filterbank") + " --no-per-config"
+                             + ": k_fir_tma, 64 x 2^24 samples, read 4.54 GB + write 4.23 GB"},
+    "fused_f64": {"bytes_per_launch": 8.424e6,
+                  "source": "ncu --set full --clock-control none -k regex:k_colfold -s 3 -c 1 python bench.py "
+                            "--workload fused --dtype f64 --no-e2e --no-cpu --no-cold --steps 20 --warmup 3: "
+                            "k_colfold, read 8.42 MB + write 0 (the 8 KB result stays in L2)"},
+    "conv": {"bytes_per_launch": 51.61e6 + 4.77e6,
+             "source": _NCU.format(k="k_conv3x3_tc", s=4) + _BENCH.format(w="conv")
+                       + ": k_conv3x3_tc (forward), read 51.61 MB + write 4.77 MB (most of Y stays in L2)"},
+    "attention": {"bytes_per_launch": 541.16e6 + 238.75e6,
+                  "source": _NCU.format(k="k_attn_bwd_dkv_tc", s=3) + _BENCH.format(w="attention")
+                            + ": k_attn_bwd_dkv_tc (the largest share of the step), read 541.16 MB + write 238.75 MB"},
+    "linreg": {"bytes_per_launch": 8.66e9 + 13.95e6,
+               "source": _NCU.format(k="k_gemv_pair_tma", s=3) + _BENCH.format(w="linreg")
+                         + ": k_gemv_pair_tma, X 2^22 x 256 f64, read 8.66 GB + write 13.95 MB"},
+}
 
 
 def peaks():
@@ -928,7 +948,7 @@ def pc_linreg(args, ws, rank, local):
     traffic, tsrc = traffic_of("linreg")
     out = entry(_METRIC["linreg"], ws * work * steps / (t / 1e3) / 1e9, "GB/s", t / steps, steps, "f64",
                 other_config("linreg", args),
-                {"bound": "hbm", "kernel": "k_rowpass<double,8,FWD,ACC> (the GEMV pair) + its partial sum",
+                {"bound": "hbm", "kernel": "k_gemv_pair_tma<double,8,3> (the GEMV pair with the loss folded in) + its partial sums",
                  "achieved": per, "peak": hbm, "unit": "GB/s", "frac": per / hbm, "traffic": traffic,
                  "traffic_source": tsrc, "peak_source": kind + " hbm_gbs (a copy: read + write)",
                  "algorithmic_bytes_per_step": work},
