@@ -761,9 +761,22 @@ __global__ void __launch_bounds__(kRowBlock) k_dot_partials(const TA* __restrict
                                                             const TB* __restrict__ y, long long sy, long long K,
                                                             double* __restrict__ partials) {
   const long long b0 = K * blockIdx.x / gridDim.x, b1 = K * (blockIdx.x + 1) / gridDim.x;
-  double s = 0.0;
-  for (long long k = b0 + threadIdx.x; k < b1; k += kRowBlock)
-    s = fma((double)__ldcs(x + k * sx), (double)__ldcs(y + k * sy), s);
+  // four independent chains, so eight loads per thread are in flight at
+  // once; their fixed combination keeps the result deterministic
+  double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
+  long long k = b0 + threadIdx.x;
+  for (; k + 3 * kRowBlock < b1; k += 4 * kRowBlock) {
+    const double x0 = (double)__ldcs(x + k * sx), y0 = (double)__ldcs(y + k * sy);
+    const double x1 = (double)__ldcs(x + (k + kRowBlock) * sx), y1 = (double)__ldcs(y + (k + kRowBlock) * sy);
+    const double x2 = (double)__ldcs(x + (k + 2 * kRowBlock) * sx), y2 = (double)__ldcs(y + (k + 2 * kRowBlock) * sy);
+    const double x3 = (double)__ldcs(x + (k + 3 * kRowBlock) * sx), y3 = (double)__ldcs(y + (k + 3 * kRowBlock) * sy);
+    s0 = fma(x0, y0, s0);
+    s1 = fma(x1, y1, s1);
+    s2 = fma(x2, y2, s2);
+    s3 = fma(x3, y3, s3);
+  }
+  for (; k < b1; k += kRowBlock) s0 = fma((double)__ldcs(x + k * sx), (double)__ldcs(y + k * sy), s0);
+  double s = (s0 + s1) + (s2 + s3);
   s = reduce1(s);
   __shared__ double ws[kRowWarps];
   if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
