@@ -323,7 +323,10 @@ def ssa_vjp(fwd: SSAProgram, param_vals: list, loss_val) -> SSAProgram:
     zero = const(0.0, loss_b.shape, loss_b.dtype)
     loss_out = emit("add", [loss_val, zero], loss_b.shape, loss_b.dtype, lambda v: morph_add(v[0], v[1]))
     grads = [param_grad[_vid(p)] for p in param_vals if _vid(p) in param_grad]
-    return SSAProgram(fwd.constants, fwd.morph_to_val, fwd.bindings + bwd, [loss_out] + grads, len(param_vals))
+    # the joint forward + backward program goes through the psi-composition
+    # fusion pass, as ssa.scm:1024-1032 does
+    return ssa_element_wise_fusion_pass(
+        SSAProgram(fwd.constants, fwd.morph_to_val, fwd.bindings + bwd, [loss_out] + grads, len(param_vals)))
 
 
 # ------------------------------------------------------------------ element-wise fusion pass
@@ -364,11 +367,12 @@ def ssa_element_wise_fusion_pass(prog: SSAProgram) -> SSAProgram:
     consumer(producer(...), ...) in double with no rounding of the
     intermediate (compose-flat-combiners), stored to the consumer's dtype.
 
-    ssa_vjp does not apply this pass: realize already fuses element-wise
-    nodes on the device and rounds each to its dtype, which equals the
-    unfused program; the pass's unrounded composition differs from it only
-    in f32 programs.  A merge is skipped when the result would exceed a map
-    node's 4 operands or program limits."""
+    ssa_vjp applies this pass to the joint program, as the reference does,
+    so a merged chain runs on the device as one map node whose program
+    rounds only its final value; in f32 programs that differs from the
+    unfused node-by-node rounding, in f64 it does not.  A producer that is
+    also a program output is not merged away.  A merge is skipped when the
+    result would exceed a map node's 4 operands or program limits."""
     from . import _abi as A
     sd: dict = {}
     for cid, m in prog.constants.items():
@@ -380,6 +384,12 @@ def ssa_element_wise_fusion_pass(prog: SSAProgram) -> SSAProgram:
         for v in b.inputs:
             if isinstance(v, BindingRef) and v.id in uses:
                 uses[v.id] += 1
+    # a program output is read after the program: it keeps its binding
+    # (ssa-compute-use-counts counts binding inputs only; a producer that is
+    # also an output would otherwise vanish into its consumer)
+    for v in prog.outputs:
+        if isinstance(v, BindingRef) and v.id in uses:
+            uses[v.id] += 1
     bs, out = list(prog.bindings), []
     while bs:
         p = bs.pop(0)

@@ -22,23 +22,30 @@
 //
 // Work split.  A CTA owns 4 adjacent outputs and all R rows, in chunks of 64
 // rows.  Warps 1-7 (the workers) take 16-byte pieces of leaf rows (2 outputs
-// of f64, 4 of a 4-byte type): a worker loads the piece of every leaf for its
-// (row, piece) positions of 8 chunks at once into registers, so all of the
-// group's loads are in flight together as in a plain streaming read, then
-// evaluates the elements straight from registers and writes the values into
-// the chunk's slot of a ring of value buffers in shared memory.  Warp 0
-// folds each output's values in ascending row order as chunks become ready
-// (one mbarrier per slot, one arrival per worker warp), so the fold (one
-// dependent add per row) overlaps the arrival of later chunks, and it frees
-// each slot for the chunk NS ahead.
+// of f64, 4 of a 4-byte type): for its (row, piece) positions of 8 chunks a
+// worker copies the piece of every leaf into its own staging slots with
+// cp.async, one commit group per position, so all of the group's copies are
+// in flight together as in a plain streaming read.  It evaluates each
+// position as soon as its own group has landed, with no barrier between
+// workers.
+//   f64 and f32 sums: the values go into the chunk's slot of a ring of value
+//     buffers in shared memory, and warp 0 folds each output's values in
+//     ascending row order as chunks become ready (one mbarrier per slot, one
+//     arrival per worker warp).  The fold, one dependent add per row, runs
+//     with 16 values prefetched into registers and frees each slot for the
+//     chunk NS ahead.
+//   integer sums: wrapping sums are associative, so each worker keeps partial
+//     sums of its positions and the CTA combines them by shuffles, with no
+//     chain at all.
 //
-// Three other designs were measured first and lost to this one: a 2-D TMA
-// tile (4 or 8 outputs x 64 rows), whose 32- and 64-byte box rows came in at
-// about one per 20 SM clocks; 16-byte cp.async into raw tiles with mbarrier
-// completion; and register loads stored to raw tiles followed by a CTA-wide
-// barrier per chunk.  In the last two the workers' per-chunk staging
-// (stores, barrier, index arithmetic) took about 0.7 us per chunk, which set
-// the pace of the whole step.
+// Other designs were measured first and lost to this one:
+//   - a 2-D TMA tile (4 or 8 outputs x 64 rows), whose 32- and 64-byte box
+//     rows came in at about one per 20 SM clocks;
+//   - cp.async into shared raw tiles with a CTA-wide barrier per chunk, where
+//     the per-chunk staging (stores, barrier, index arithmetic) took about
+//     0.7 us per chunk and set the pace of the whole step;
+//   - register staging, which needed more than 128 registers, so the spills
+//     serialised the loads.
 //
 // Every wait is bounded; a wait that gives up records AMC_ERR_TIMEOUT in a
 // device flag that the host reads after the step.
