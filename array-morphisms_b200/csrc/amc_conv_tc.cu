@@ -535,8 +535,23 @@ __global__ void __launch_bounds__(256) k_wgrad_reduce(const float* __restrict__ 
   const int ci = o & 63, co = (o >> 6) & 63, kh = (o >> 12) % 3, kw = (o >> 12) / 3;
   const int blk = kh == 2 ? 1 : 0, lane = kh == 2 ? 64 + co : kh * 64 + co;
   const size_t off = ((size_t)(kw * 2 + blk) * 128 + lane) * kC + ci;
+  // the partials of group g are added in ascending order; the loads of four
+  // of them are issued together (a partial of a CTA that had no chunk is
+  // read but not added)
   float s = 0.f;
-  for (int p = g; p < nparts; p += 8)
+  int p = g;
+  for (; p + 24 < nparts; p += 32) {
+    const int c0 = counts[p], c1 = counts[p + 8], c2 = counts[p + 16], c3 = counts[p + 24];
+    const float v0 = __ldg(partials + (size_t)p * kWgPart + off);
+    const float v1 = __ldg(partials + (size_t)(p + 8) * kWgPart + off);
+    const float v2 = __ldg(partials + (size_t)(p + 16) * kWgPart + off);
+    const float v3 = __ldg(partials + (size_t)(p + 24) * kWgPart + off);
+    if (c0) s += v0;
+    if (c1) s += v1;
+    if (c2) s += v2;
+    if (c3) s += v3;
+  }
+  for (; p < nparts; p += 8)
     if (counts[p]) s += __ldg(partials + (size_t)p * kWgPart + off);
   red[g][l] = s;
   __syncthreads();
