@@ -45,6 +45,7 @@ struct PeerGroup {
 };
 
 constexpr size_t kFlagBytes = 256;   // flags area (up to 32 ranks), keeps the slots 256-byte aligned
+constexpr int kDistThreads = 128;
 
 std::mutex g_groups_mu;
 std::unordered_map<uint64_t, PeerGroup*> g_groups;
@@ -65,7 +66,7 @@ struct PushArgs {
   char* peer[32];
 };
 
-__global__ void k_peer_push(const __grid_constant__ PushArgs a) {
+__global__ void __launch_bounds__(kDistThreads) k_peer_push(const __grid_constant__ PushArgs a) {
   const long long nb = a.n * a.esize;
   const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, nthr = (long long)gridDim.x * blockDim.x;
   // 16-byte moves where the size allows, then the tail in elements
@@ -102,7 +103,7 @@ __device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned l
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__global__ void k_peer_signal_sum(const __grid_constant__ SumArgs a) {
+__global__ void __launch_bounds__(kDistThreads) k_peer_signal_sum(const __grid_constant__ SumArgs a) {
   __shared__ int ok;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     __threadfence_system();
@@ -211,8 +212,10 @@ int amc_peer_sum(uint64_t h, const void* src, int64_t n, int32_t dtype, void* ou
   pa.src = src; pa.n = n; pa.esize = (int32_t)esize; pa.world = g->world;
   pa.slot_off = parity_off + g->rank * slot_bytes;
   for (int q = 0; q < g->world; ++q) pa.peer[q] = g->peer[q];
-  const int blocks = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, (n * esize / 16 + 255) / 256));
-  k_peer_push<<<blocks, 256, 0, s>>>(pa);
+  // 128-thread CTAs with few registers fit beside a resident tensor-core CTA
+  // on the same SM, so the sum can overlap other work of the step
+  const int blocks = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, (n * esize / 16 + kDistThreads - 1) / kDistThreads));
+  k_peer_push<<<blocks, kDistThreads, 0, s>>>(pa);
   AMC_CUDA(cudaGetLastError());
   SumArgs sa;
   memset(&sa, 0, sizeof sa);
@@ -222,8 +225,8 @@ int amc_peer_sum(uint64_t h, const void* src, int64_t n, int32_t dtype, void* ou
   sa.base = g->base;
   sa.flags_local = (volatile unsigned long long*)g->base;
   for (int q = 0; q < g->world; ++q) sa.peer[q] = g->peer[q];
-  const int sblocks = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, (n + 255) / 256));
-  k_peer_signal_sum<<<sblocks, 256, 0, s>>>(sa);
+  const int sblocks = (int)std::min<int64_t>(num_sms(), std::max<int64_t>(1, (n + kDistThreads - 1) / kDistThreads));
+  k_peer_signal_sum<<<sblocks, kDistThreads, 0, s>>>(sa);
   AMC_CUDA(cudaGetLastError());
   return AMC_OK;
 }

@@ -532,8 +532,8 @@ def make_rank_sum(ws: int, n: int):
         print(f"bench: peer-memory rank sum unavailable ({e}); using allreduce_fixed_order", file=sys.stderr)
         return allreduce_fixed_order
 
-    def run(t):
-        return ps.sum_(t)
+    def run(t, stream=None):
+        return ps.sum_(t, stream)
     run.peer = ps
     return run
 
@@ -761,13 +761,26 @@ def pc_conv(args, ws, rank, local):
     dy = torch.from_numpy(gen(2, N * 64 * 56 * 56).astype(np.float32)).cuda().view(N, 64, 56, 56)
     yy, dx, dw = torch.empty_like(x), torch.empty_like(x), torch.empty_like(wt)
     rank_sum = make_rank_sum(ws, dw.numel())
+    # dW first: its rank-order sum (peer-memory kernels of a few registers,
+    # which fit beside the conv CTAs) runs on a side stream while the
+    # forward and data-gradient passes run on the main one
+    overlap = rank_sum is not None and hasattr(rank_sum, "peer")
+    side = torch.cuda.Stream() if overlap else None
+    w_done, s_done = torch.cuda.Event(), torch.cuda.Event()
 
     def run():
+        W.conv2d_wgrad(x, dy, dw)
+        if overlap:
+            w_done.record(stream)
+            side.wait_event(w_done)
+            rank_sum(dw, side.cuda_stream)   # dW sums over the batch shards, in rank order
         W.conv2d_fwd(x, wt, yy)
         W.conv2d_dgrad(dy, wt, dx)
-        W.conv2d_wgrad(x, dy, dw)
-        if ws > 1:
-            rank_sum(dw)   # dW sums over the batch shards, in rank order
+        if overlap:
+            s_done.record(side)
+            stream.wait_event(s_done)
+        elif ws > 1:
+            rank_sum(dw)
     work = 3 * 2.0 * N * 64 * 64 * 9 * 56 * 56
     ms, steps, clocks = time_steps(run, args.steps, args.warmup, stream, local, ws, min_region_s=0.3, max_steps=4000)
     t = max_over_ranks(ws, sum(ms))
