@@ -892,6 +892,8 @@ def pc_linreg(args, ws, rank, local):
     hook = None
     rank_sum = make_rank_sum(ws, d)
     if ws > 1:
+        views = {}   # the replay's gradient lives at a fixed arena address: one torch view of it
+
         def hook(dw):
             # the gradient sums over the row shards, in rank order
             if dw._dev is None:   # the traced step's gradient comes back on the host
@@ -900,7 +902,10 @@ def pc_linreg(args, ws, rank, local):
                 rank_sum(t_)
                 arr[dw.offset:dw.offset + d] = t_.cpu().numpy()
             else:
-                rank_sum(torch.as_tensor(CudaView(dw._dev.devptr() + 8 * dw.offset, d), device="cuda"))
+                ptr = dw._dev.devptr() + 8 * dw.offset
+                if ptr not in views:
+                    views[ptr] = torch.as_tensor(CudaView(ptr, d), device="cuda")
+                rank_sum(views[ptr])
     steps_total = args.warmup + max(args.steps, 64) + 64
     tr = W.LinregSSA(Xm, ym, np.zeros(d), 0.1 / ws, stream=sptr, max_steps=steps_total + 16, grad_hook=hook)
     tr.trace()
