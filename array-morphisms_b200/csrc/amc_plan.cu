@@ -184,6 +184,12 @@ struct Builder {
   // this buffer would run before the buffer is written (watch_hit).
   uint64_t watch_buf = 0;
   bool watch_hit = false;
+  // The forward product X w of the last GEMV pair: slots created after the
+  // pair that read it (r0_reads).  When none does and it is no result, the
+  // pair need not store it (plan_create clears the store pointer).
+  uint64_t r0_watch = 0;
+  int r0_reads = 0;
+  int pairs_built = 0;
   // The GEMV pair planned last: its launch arguments (shared with its step,
   // which reads them at launch), the buffer of X w and the partial sums.
   struct {
@@ -256,6 +262,12 @@ struct Builder {
     if (watch_buf)
       for (uint64_t r : reads)
         if (r == watch_buf) watch_hit = true;
+    if (r0_watch)
+      for (uint64_t r : reads)
+        if (r == r0_watch) {
+          ++r0_reads;
+          break;
+        }
     uint64_t h = 0;
     int rc = plan->add_slot(dtype, numel(rank, shape), reads, &h);
     if (rc) return rc;
@@ -750,6 +762,13 @@ struct Builder {
     if (rc) return rc;
     a.out = ptr_of(o.buf);
     if (try_fold_row_sum(a, e, o, op)) {
+      // the folded sum reads the pair's partials, not X w
+      if (r0_watch)
+        for (uint64_t rb : reads)
+          if (rb == r0_watch) {
+            --r0_reads;
+            break;
+          }
       out = Val();
       out.view = o;
       return AMC_OK;
@@ -1277,6 +1296,9 @@ struct Builder {
     pair.args = ap;
     pair.r0 = r0.buf;
     pair.part = part.buf;
+    ++pairs_built;
+    r0_watch = r0.buf;
+    r0_reads = 0;
     memo[j] = Val();
     memo[j]->view = dw;
     return AMC_OK;
@@ -1570,6 +1592,12 @@ int plan_create(void* ctx, const amc_node* nodes, int32_t n, uint64_t* out) {
     r.offset = res.offset;
     buf_retain(res.buf);
     p->results.push_back(r);
+  }
+  if (!rc && b.pairs_built == 1 && b.pair.args && b.r0_reads == 0) {
+    // nothing after the pair reads X w and it is no result: skip its store
+    bool is_result = false;
+    for (auto& r : p->results) is_result = is_result || r.buf == b.r0_watch;
+    if (!is_result) b.pair.args->r = nullptr;
   }
   if (!rc) {
     if (p->ctx_replay) p->ctx_ids = ctx_counter(ctx) - p->ctx_first_id;
